@@ -1,0 +1,280 @@
+// fr_gemv.cuh -- q8_1 quantizer and the NVFP4 x q8_1 matvec for B200.
+//
+// Matvec design (HBM-bound; one pass over the weight rows per launch):
+//   * Each CTA owns a contiguous range of weight rows.  Because ggml's
+//     block_nvfp4 rows are contiguous, that range is one contiguous byte
+//     stream, which a single producer lane moves into a shared-memory ring with
+//     1-D bulk copies (cp.async.bulk, the TMA engine, no multicast) completing
+//     on mbarriers.  No register or LSU cost for the stream itself.
+//   * A "stage" is the rows one consumer warp finishes in one pass
+//     (32 / LG rows, LG lanes per row); stage i goes to ring slot i % NS and
+//     consumer warp i % 8, so every slot has exactly one consumer.
+//   * The activations (T tokens of q8_1) are staged once per CTA into shared
+//     memory, byte-permuted to the order the weight decode produces and
+//     swizzled for conflict-free 128-bit reads.  The f32 entry points quantize
+//     into that staging area directly (the reference fuses quantize_q8_1 into
+//     its GEMV prologues the same way, src/fr_win_flint_sm120.cu:1047-1049).
+//   * Weight decode: two prmt per 4 codes against the table |kvalues| with the
+//     sign bit selecting 0 (prmt sign-replicate of a positive byte), once for
+//     the code and once for the code with bit 3 flipped, so
+//     sum kv*q = dp4a(pos, q) - dp4a(neg, q) exactly in int32 per 16-value
+//     sub-block, as vec_dot_nvfp4_q8_1 computes it
+//     (src/fr_win_flint_sm120.cu:320-342); then fp32 (d_w * d_q8) * sumi.
+//   * Weight bytes are fetched before griddepcontrol.wait (they do not depend
+//     on the previous kernel), so under PDL the stream starts while the
+//     producer of the activations is still finishing.
+#pragma once
+
+#include "fr_common.cuh"
+
+namespace frb {
+
+// ------------------------------------------------------------ quantize_q8_1
+__global__ void __launch_bounds__(256) k_quantize_q8_1(const float *__restrict__ x, int64_t ldx,
+                                                       uint8_t *__restrict__ q8, int64_t ldq, int T, int K) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int nc = K / Q8_ELEMS;
+    const int64_t c = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    if (c >= static_cast<int64_t>(T) * nc) return;
+    const int t = static_cast<int>(c / nc), ch = static_cast<int>(c % nc);
+    const float xi = x[t * ldx + static_cast<int64_t>(ch) * Q8_ELEMS + lane];
+    const q8_lane r = q8_1_chunk(xi);
+    uint8_t *blk = q8 + (t * ldq + ch) * Q8_BYTES;
+    blk[4 + lane] = static_cast<uint8_t>(r.q);
+    if (lane == 0) {
+        const __half2 ds = __halves2half2(__float2half_rn(r.d), __float2half_rn(r.sum));
+        *reinterpret_cast<__half2 *>(blk) = ds;
+    }
+}
+
+// ------------------------------------------------------------ matvec
+constexpr int GV_CWARPS = 8;                        // consumer warps
+constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;    // + one producer warp
+
+enum GvEpi : int { GV_PLAIN = 0, GV_SWIGLU = 1 };
+
+struct GvParams {
+    const uint8_t *w0;      // rows [N, w_ld]
+    const uint8_t *w1;      // up rows for the SwiGLU pair (else null)
+    int64_t w_ld;           // bytes per row (multiple of 16 on the bulk path)
+    const uint8_t *q8;      // q8_1 activations [T, ldq blocks] (if x == null)
+    int64_t ldq;
+    const float *x;         // f32 activations [T, ldx] (fused quantize)
+    int64_t ldx;
+    const float *s0, *s1;   // per-tensor scales (nullable)
+    const float *resid;     // [T, ldr] added to the output (nullable)
+    int64_t ldr;
+    float *y;
+    int64_t ldy;
+    int N, K;
+    int t0, nt;             // token window of this launch
+    int rows_per_cta;
+    int rows_per_stage;     // 32 / LG
+    int n_slots;            // ring slots (multiple of GV_CWARPS)
+    int slot_bytes;         // bytes per slot (both operands)
+    int word_mode;          // rows not 16-byte aligned: producer warp copies words
+};
+
+// Byte position inside a sub-block's 16 activation bytes of value j (0..15),
+// matching the order nv_decode emits: words (j,j+8,j+1,j+9), (j+2,..), ...
+__device__ __forceinline__ int act_perm(int j) {
+    const int jj = j & 7, hi = j >> 3;
+    return (jj >> 1) * 4 + (jj & 1) * 2 + hi;
+}
+
+// Stage the activation of tokens [t0, t0+nt) into shared memory:
+// act_q: int4 per (token, 64-block, sub-block), swizzled by (b >> 1) & 3;
+// act_d: float2 per (token, 64-block) = 0.5 * f16-rounded q8_1 scales.
+__device__ __forceinline__ void gv_stage_act(const GvParams &p, int4 *act_q, float2 *act_d, int warp, int lane) {
+    const int nc = p.K / Q8_ELEMS, NB = p.K / NV_ELEMS;
+    uint8_t *aq = reinterpret_cast<uint8_t *>(act_q);
+    float *ad = reinterpret_cast<float *>(act_d);
+    for (int c = warp; c < p.nt * nc; c += GV_CWARPS) {
+        const int t = c / nc, ch = c % nc;
+        int8_t q;
+        float d;
+        if (p.x != nullptr) {
+            const q8_lane r = q8_1_chunk(p.x[(p.t0 + t) * p.ldx + static_cast<int64_t>(ch) * Q8_ELEMS + lane]);
+            q = r.q;
+            d = __half2float(__float2half_rn(r.d));
+        } else {
+            const uint8_t *blk = p.q8 + ((p.t0 + t) * p.ldq + ch) * Q8_BYTES;
+            q = static_cast<int8_t>(blk[4 + lane]);
+            d = __low2float(*reinterpret_cast<const __half2 *>(blk));
+        }
+        const int b = ch >> 1;
+        const int s = ((ch & 1) << 1) | (lane >> 4);
+        const int slot = (t * NB + b) * 4 + (s ^ ((b >> 1) & 3));
+        aq[slot * 16 + act_perm(lane & 15)] = static_cast<uint8_t>(q);
+        if (lane == 0) ad[(t * NB + b) * 2 + (ch & 1)] = 0.5f * d;
+    }
+}
+
+// dot of one 64-block (9 words at `blk`) with TT tokens' staged activations
+template <int TT>
+__device__ __forceinline__ void gv_block(const uint32_t *blk, int b, int NB, int nt,
+                                         const int4 *act_q, const float2 *act_d, float (&acc)[TT]) {
+    const uint32_t dw = blk[0];
+    nv_word dec[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dec[i] = nv_decode(blk[1 + i]);
+    float sc[4];
+    ue4m3x4(dw, sc);
+    const int swz = (b >> 1) & 3;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        if (t < nt) {
+            const int4 *aq = act_q + (t * NB + b) * 4;
+            const float2 dd = act_d[t * NB + b];
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const int4 a = aq[s ^ swz];
+                int ip = dp4a(dec[2 * s].p0, a.x, 0);
+                ip = dp4a(dec[2 * s].p1, a.y, ip);
+                ip = dp4a(dec[2 * s + 1].p0, a.z, ip);
+                ip = dp4a(dec[2 * s + 1].p1, a.w, ip);
+                int in = dp4a(dec[2 * s].n0, a.x, 0);
+                in = dp4a(dec[2 * s].n1, a.y, in);
+                in = dp4a(dec[2 * s + 1].n0, a.z, in);
+                in = dp4a(dec[2 * s + 1].n1, a.w, in);
+                const float dsc = sc[s] * (s < 2 ? dd.x : dd.y);
+                acc[t] += dsc * static_cast<float>(ip - in);
+            }
+        }
+    }
+}
+
+template <int LG, int TT, int EPI>
+__global__ void __launch_bounds__(GV_THREADS) k_gemv(const GvParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NS = p.n_slots;
+    const int NB = p.K / NV_ELEMS;
+    constexpr bool DUAL = EPI == GV_SWIGLU;
+
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + NS;
+    uint8_t *ring = smem + 2048;                                    // barriers fit in 2 KB
+    int4 *act_q = reinterpret_cast<int4 *>(ring + static_cast<size_t>(NS) * p.slot_bytes);
+    float2 *act_d = reinterpret_cast<float2 *>(act_q + static_cast<size_t>(p.nt) * NB * 4);
+
+    const int r_begin = blockIdx.x * p.rows_per_cta;
+    const int r_end = min(p.N, r_begin + p.rows_per_cta);
+    const int n_rows = r_end - r_begin;
+    const int RS = p.rows_per_stage;
+    const int n_st = n_rows > 0 ? (n_rows + RS - 1) / RS : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], p.word_mode ? 32 : 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == GV_CWARPS && p.word_mode) {
+        // ---------------- producer, rows not 16-byte aligned (K % 256 != 0):
+        // the warp copies 4-byte words, then every lane arrives on `full`.
+        const int wpr = static_cast<int>(p.w_ld / 4);
+        for (int i = 0; i < n_st; ++i) {
+            const int s = i % NS;
+            if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1, 1)) break;
+            const int rows = min(RS, n_rows - i * RS);
+            const int64_t off = static_cast<int64_t>(r_begin + i * RS) * p.w_ld;
+            uint32_t *dst = reinterpret_cast<uint32_t *>(ring + static_cast<size_t>(s) * p.slot_bytes);
+            const uint32_t *src0 = reinterpret_cast<const uint32_t *>(p.w0 + off);
+            for (int k = lane; k < rows * wpr; k += 32) dst[k] = __ldg(src0 + k);
+            if (DUAL) {
+                const uint32_t *src1 = reinterpret_cast<const uint32_t *>(p.w1 + off);
+                for (int k = lane; k < rows * wpr; k += 32) dst[RS * wpr + k] = __ldg(src1 + k);
+            }
+            mbar_arrive(&full[s]);
+        }
+        return;
+    }
+    if (warp == GV_CWARPS) {
+        // ---------------- producer: stream the weight rows
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            for (int i = 0; i < n_st; ++i) {
+                const int s = i % NS;
+                if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1, 1)) break;
+                const int rows = min(RS, n_rows - i * RS);
+                const uint32_t bytes = static_cast<uint32_t>(rows * p.w_ld);
+                const int64_t off = static_cast<int64_t>(r_begin + i * RS) * p.w_ld;
+                uint8_t *dst = ring + static_cast<size_t>(s) * p.slot_bytes;
+                mbar_expect_tx(&full[s], DUAL ? 2 * bytes : bytes);
+                bulk_g2s_hint(dst, p.w0 + off, bytes, &full[s], pol);
+                if (DUAL) bulk_g2s_hint(dst + RS * p.w_ld, p.w1 + off, bytes, &full[s], pol);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    fr_pdl_wait();
+    gv_stage_act(p, act_q, act_d, warp, lane);
+    named_bar(1, GV_CWARPS * 32);
+    fr_pdl_trigger();
+
+    const float sc0 = p.s0 ? *p.s0 : 1.0f;
+    const float sc1 = (DUAL && p.s1) ? *p.s1 : 1.0f;
+    const int g = lane / LG, j = lane % LG;
+
+    for (int i = warp; i < n_st; i += GV_CWARPS) {
+        const int s = i % NS;
+        if (!mbar_wait(&full[s], (i / NS) & 1, 2)) return;
+        const int rows = min(RS, n_rows - i * RS);
+        const uint8_t *st = ring + static_cast<size_t>(s) * p.slot_bytes;
+        float acc0[TT], acc1[TT];
+#pragma unroll
+        for (int t = 0; t < TT; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
+        if (g < rows) {
+            const uint8_t *row0 = st + static_cast<size_t>(g) * p.w_ld;
+            for (int b = j; b < NB; b += LG) {
+                gv_block<TT>(reinterpret_cast<const uint32_t *>(row0 + b * NV_BYTES), b, NB, p.nt, act_q, act_d, acc0);
+                if (DUAL)
+                    gv_block<TT>(reinterpret_cast<const uint32_t *>(row0 + RS * p.w_ld + b * NV_BYTES), b, NB,
+                                 p.nt, act_q, act_d, acc1);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+#pragma unroll
+            for (int off = LG / 2; off > 0; off >>= 1) {
+                acc0[t] += __shfl_xor_sync(0xffffffffu, acc0[t], off);
+                if (DUAL) acc1[t] += __shfl_xor_sync(0xffffffffu, acc1[t], off);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (j == 0 && g < rows) {
+            const int row = r_begin + i * RS + g;
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                if (t < p.nt) {
+                    const int64_t tt = p.t0 + t;
+                    float v;
+                    if (DUAL) {
+                        // fused mmvq epilogue: x = up, gate = gate, SwiGLU
+                        float result = acc1[t];
+                        result *= sc1;
+                        float gate = acc0[t];
+                        gate *= sc0;
+                        result *= silu_f(gate);
+                        v = result;
+                    } else {
+                        v = acc0[t] * sc0;
+                        if (p.resid) v += p.resid[tt * p.ldr + row];
+                    }
+                    p.y[tt * p.ldy + row] = v;
+                }
+            }
+        }
+    }
+}
+
+} // namespace frb

@@ -1,0 +1,205 @@
+/*
+ * fr_b200.h -- C-ABI of the B200 (sm_100a) NVFP4-weight x q8_1-activation
+ * matmul hot path, a drop-in for FlashRT-llama.cpp's NVFP4 mul_mat /
+ * mul_mat_id path.
+ *
+ * Conventions (the reference's, include/fr_kernels.h:1-6 and
+ * docs/development.md:11-25):
+ *   - raw device pointers, the caller's cudaStream_t, no framework types;
+ *   - every entry returns an int: 0 on success, -1 on a shape / alignment /
+ *     null-pointer precondition, -3 on a layout overflow, -cudaError_t on a
+ *     CUDA launch error (the reference's codes), and the FR_E* codes below
+ *     for conditions the reference has no code for;
+ *   - nothing aborts; nothing allocates while the stream is being captured
+ *     (an entry that would have to grow a workspace then returns
+ *     FR_ECAPTURE).
+ *
+ * Formats: ggml's block_nvfp4 (36 B per 64 values: 4 UE4M3 sub-block scales
+ * + 32 bytes of E2M1 codes, sub-block s in qs[8s..8s+7], byte j = value j in
+ * the low nibble and value j+8 in the high nibble) and block_q8_1 (36 B per
+ * 32 values: half d, half sum, int8 qs[32]).  Weights [N rows, K] are rows of
+ * K/64 blocks, `w_ld` bytes apart; activations / outputs are row-major f32.
+ */
+#ifndef FR_B200_H
+#define FR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <stdbool.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ codes */
+#define FR_OK          0
+#define FR_EINVAL     (-1)    /* shape / alignment / null pointer (reference -1) */
+#define FR_ELAYOUT    (-3)    /* scale layout larger than the buffer (reference -3) */
+#define FR_ECAPTURE   (-901)  /* a workspace would have to grow during stream capture */
+#define FR_EINJECTED  (-902)  /* host-side fault injection fired (fr_fault_inject) */
+#define FR_ENODEVICE  (-903)  /* no sm_100 device current */
+
+int         fr_version(void);
+const char *fr_strerror(int rc);
+
+/* Device-side status word: bounded waits inside the kernels that give up set
+ * bit 0 (and a site id in bits 8..15) and return instead of hanging;
+ * out-of-range routing ids set bit 1.  Reads (and optionally clears) the
+ * word of the current device.  Synchronises the device. */
+int fr_device_status(uint32_t *status, int clear);
+
+/* Host-side fault injection (test aid): the next call of the entry point
+ * whose name equals `site` returns FR_EINJECTED before launching anything.
+ * NULL clears.  Also read once from the environment variable FR_FAULT. */
+int fr_fault_inject(const char *site);
+
+/* Number of kernels this library has launched in this process. */
+uint64_t fr_kernel_launches(void);
+
+/* ------------------------------------------------------------------ sizes */
+int64_t fr_nvfp4_row_bytes(int64_t K);   /* K/64 * 36 */
+int64_t fr_q8_1_row_bytes(int64_t K);    /* K/32 * 36 */
+
+/* --------------------------------------------------- (a1) quantize_q8_1
+ * x [T, ldx] f32 -> q8 [T, ldq blocks] block_q8_1.  K % 32 == 0.
+ * Bit-exact: d = amax/127, q = roundf(x/d) (IEEE division), ds = half2(d, sum
+ * in xor-butterfly order).  Replaces frt_q8_1_chunk / frt_b_q8
+ * (src/fr_win_flint_sm120.cu:289-300, src/fr_win_flint_batched.cuh:178-190)
+ * and ggml-cuda's quantize_q8_1 in front of mmvq. */
+int fr_quantize_q8_1(const float *x, int64_t ldx, void *q8, int64_t ldq,
+                     int T, int K, cudaStream_t stream);
+
+/* ------------------------------------------- (a3/a4) NVFP4 x q8_1 matvec
+ * y[t, n] = scale * dot(W[n], q8[t]) (+ resid[t, n]) for t < T, n < N.
+ * scale / resid nullable (1.0 / none).  K % 64 == 0, 1 <= T <= 128.
+ * Replaces the mmvq NVFP4 x q8_1 decode GEMV and the Flint row dots
+ * (src/fr_win_flint_sm120.cu:320-414, windows :889-920, :1201-1232) and the
+ * batched frt_m_gemv / frt_b_gemv (src/fr_win_flint_bmma.cuh:193-310,
+ * src/fr_win_flint_batched.cuh:215-289). */
+int fr_gemv_nvfp4_q8_1(const void *w, int64_t w_ld, const void *q8, int64_t ldq,
+                       const float *scale, const float *resid, int64_t ldr,
+                       float *y, int64_t ldy, int N, int K, int T, cudaStream_t stream);
+
+/* Same, with the q8_1 quantization of f32 x [T, ldx] fused into the kernel. */
+int fr_gemv_nvfp4_f32(const void *w, int64_t w_ld, const float *x, int64_t ldx,
+                      const float *scale, const float *resid, int64_t ldr,
+                      float *y, int64_t ldy, int N, int K, int T, cudaStream_t stream);
+
+/* Gate/up pair with the fused mmvq SwiGLU epilogue
+ * y = (su * dot(Wu[n], q8)) * silu(sg * dot(Wg[n], q8))
+ * (src/fr_win_flint_sm120.cu:1944-1952, frt_dense_gu :1024-1101). */
+int fr_gemv_nvfp4_q8_1_swiglu(const void *wg, const void *wu, int64_t w_ld,
+                              const void *q8, int64_t ldq, const float *sg, const float *su,
+                              float *y, int64_t ldy, int N, int K, int T, cudaStream_t stream);
+
+/* ggml_mul_mat(src0 = NVFP4 [N, K], src1 = f32 [T, K]) -> dst f32 [T, N] with
+ * ggml's q8_1 activation semantics: the f32 rows are quantized to q8_1 and
+ * multiplied by the NVFP4 rows.  The op surface of ggml_cuda_mul_mat for an
+ * NVFP4 src0 (hosts/llama.cpp/patches/0001-...:109-121, the Thor predicate
+ * src/fr_dispatch.cu:267-289).  T >= 1 (no upper bound). */
+int fr_mul_mat_nvfp4(const void *src0, int64_t nb01, const float *src1, int64_t ld1,
+                     float *dst, int64_t ldd, int N, int K, int T, cudaStream_t stream);
+
+/* Dense SwiGLU FFN (the Flint DENSEFFN window, src/fr_win_flint_sm120.cu:
+ * 1024-1101): out[t] = sd * Wd . q8( swiglu(Wg, Wu; q8(x[t])) ) (+ resid[t]).
+ * x / resid / out are [T, n_embd]; Wg, Wu [n_ff, n_embd]; Wd [n_embd, n_ff].
+ * The optional check buffers (nullable) receive the intermediates the
+ * reference's check mode inspects: glu [T, n_ff] f32, glu_q8 [T, n_ff/32]
+ * blocks. */
+int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
+                 const float *sg, const float *su, const float *sd, const float *resid,
+                 float *out, int T, int n_embd, int n_ff,
+                 float *chk_glu, void *chk_glu_q8, cudaStream_t stream);
+
+/* -------------------------------------------------------------- (a7/a8) MoE routing
+ * logits[t, e] = x[t] . W_r[e] (f32), softmax over E, n_used rounds of
+ * arg-max (lower expert id wins ties), w = p / max(sum p_sel, clamp)
+ * (frt_router_fused, src/fr_win_qwen36_sm120.cu:1785-1870), then the token
+ * permute (src/fr_win_flint_batched_moe.cuh:76-166): eoff [E+1] (first
+ * grouped slot of each expert), slots [T*n_used] (slot ids t*n_used + k grouped
+ * by expert, in slot order inside an expert), act [E+1] (active experts
+ * ascending, count at act[E]).  E % 32 == 0, E <= 256, n_used <= 32, K % 4 == 0. */
+int fr_moe_route(const float *x, int64_t ldx, const float *w_r, int T, int K, int E,
+                 int n_used, float clamp_val, float *logits, int32_t *ids, float *wts,
+                 int32_t *eoff, int32_t *slots, int32_t *act, cudaStream_t stream);
+
+/* ------------------------------------------------------- (a9) mul_mat_id
+ * ggml_mul_mat_id: dst[t, k, :] = W[ids[t, k]] . q8(x[t, k or 0]) for t < T,
+ * k < n_used.  W is E experts of [N, K] NVFP4 rows (nb01 bytes per row, nb02
+ * bytes per expert).  x rows: x + t*x_ld_tok + k*x_ld_slot floats
+ * (x_ld_slot = 0 broadcasts one row per token, the gate/up case).
+ * dst rows: dst + t*dst_ld_tok + k*dst_ld_slot.  Rows are grouped by expert
+ * so every used expert's weights are read once per call.  The hook
+ * ggml_cuda_frt_moe_mul_mat_id (src/fr_win_qwen36_sm120.cu:2502-2618)
+ * with the q8_1 arithmetic of ggml's MMVQ/MMQ mul_mat_id. */
+int fr_mul_mat_id_nvfp4(const void *w, int64_t nb01, int64_t nb02, int E,
+                        const float *x, int64_t x_ld_slot, int64_t x_ld_tok,
+                        const int32_t *ids, int64_t ids_ld,
+                        float *dst, int64_t dst_ld_slot, int64_t dst_ld_tok,
+                        int T, int n_used, int N, int K, cudaStream_t stream);
+
+/* --------------------------------------------- (a7-a10) fused MoE FFN layer
+ * route -> grouped gate/up (SwiGLU) -> q8_1 of the GLU -> grouped down ->
+ * weighted slot-order combine: out[t] = sum_k w[t,k] * sd[e] * Wd[e] . q8(glu)
+ * (+ resid[t]).  Experts: Wg/Wu [E][n_ff, n_embd], Wd [E][n_embd, n_ff];
+ * per-expert scales sg/su/sd [E] (nullable -> 1).  W_r [E, n_embd] f32.
+ * Check buffers (nullable): ids/wts [T, n_used], glu [T, n_used, n_ff] f32,
+ * part [T, n_used, n_embd] f32 (unweighted per-slot down outputs). */
+int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const void *wu,
+                     const void *wd, const float *sg, const float *su, const float *sd,
+                     const float *resid, float *out, int T, int n_embd, int n_ff, int E,
+                     int n_used, float clamp_val,
+                     int32_t *chk_ids, float *chk_wts, float *chk_glu, float *chk_part,
+                     cudaStream_t stream);
+
+/* ------------------------------------------------- (a5/a6) W4A4 tcgen05 path
+ * The reference's Thor launch interface (include/fr_kernels.h:21-57), same
+ * arguments, same meaning, same return codes; C++ callers also get the
+ * namespace ggml_cuda_flashrt forwarders at the end of this header. */
+int64_t fr_sf_bytes(int64_t rows, int64_t K);        /* include/fr_kernels.h:25-29 */
+int64_t fr_packed_bytes(int64_t rows, int64_t K);    /* include/fr_kernels.h:31-33 */
+/* include/fr_kernels.h:49-50 */
+int fr_quantize_act_f32(const float *src, void *dst_packed, void *dst_sfa,
+                        int M, int K, cudaStream_t stream);
+/* include/fr_kernels.h:56-57 */
+int fr_repack_weight(const void *ggml_blocks, void *dst_packed, void *dst_sf,
+                     int N, int K, cudaStream_t stream);
+/* D [M, N] = alpha * A [M, K] . B [N, K]^T, NVFP4 x NVFP4 block-scaled on
+ * tcgen05 (kind::mxf4nvf4), f32 out.  K % 64 == 0, N % 16 == 0.
+ * include/fr_kernels.h:41-44 */
+int fr_gemm_f32out(const void *A_packed, const void *SFA, const void *B_packed, const void *SFB,
+                   float *D, int M, int N, int K, float alpha, bool widen, cudaStream_t stream);
+
+/* ------------------------------------------------------ synthetic inputs
+ * Host-side, deterministic (splitmix64 + Box-Muller in double) generator of
+ * the benchmark inputs: NVFP4 rows with E2M1 codes uniform over 0..15 and
+ * sub-block scales e4m3(|N(0,1)| * scale_sigma) (RNE), and N(mean, std) f32. */
+void fr_synth_nvfp4(uint64_t seed, int64_t rows, int64_t K, double scale_sigma, void *out_blocks);
+void fr_synth_normal(uint64_t seed, int64_t n, double mean, double stddev, float *out);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+/* Drop-in C++ spellings of the reference launch interface. */
+namespace ggml_cuda_flashrt {
+static inline int64_t round_up_i64(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+static inline int64_t sf_bytes(int64_t rows, int64_t K) { return fr_sf_bytes(rows, K); }
+static inline int64_t packed_bytes(int64_t rows, int64_t K) { return fr_packed_bytes(rows, K); }
+static inline int gemm_f32out(const void *A_packed, const void *SFA, const void *B_packed,
+                              const void *SFB, float *D, int M, int N, int K, float alpha,
+                              bool widen, cudaStream_t stream) {
+    return fr_gemm_f32out(A_packed, SFA, B_packed, SFB, D, M, N, K, alpha, widen, stream);
+}
+static inline int quantize_act_f32(const float *src, void *dst_packed, void *dst_sfa, int M, int K,
+                                   cudaStream_t stream) {
+    return fr_quantize_act_f32(src, dst_packed, dst_sfa, M, K, stream);
+}
+static inline int repack_weight(const void *ggml_blocks, void *dst_packed, void *dst_sf, int N, int K,
+                                cudaStream_t stream) {
+    return fr_repack_weight(ggml_blocks, dst_packed, dst_sf, N, K, stream);
+}
+} /* namespace ggml_cuda_flashrt */
+#endif
+
+#endif /* FR_B200_H */

@@ -1,0 +1,227 @@
+"""ctypes view of the CPU oracle (liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline legs of bench.py as the checker.  The product never imports it.
+Every function here forwards to oracle/fr_oracle.c, which cites the reference
+lines it restates.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+
+
+def build() -> str:
+    """Compile liboracle.so in place (make), return its path."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        sig = {
+            "or_f32_to_f16": (C.c_uint16, [C.c_float]),
+            "or_f16_to_f32": (C.c_float, [C.c_uint16]),
+            "or_ue4m3_half": (C.c_float, [C.c_uint8]),
+            "or_e4m3_to_f32": (C.c_float, [C.c_uint8]),
+            "or_f32_to_e4m3_satfinite": (C.c_uint8, [C.c_float]),
+            "or_f32_to_e2m1_act": (C.c_uint8, [C.c_float]),
+            "or_nvfp4_dequant": (None, [_u8p, C.c_int64, _f32p]),
+            "or_quantize_q8_1": (None, [_f32p, C.c_int64, C.c_int, C.c_int, _u8p]),
+            "or_quantize_q8_ggml_cpu": (None, [_f32p, C.c_int64, _i8p, _u16p]),
+            "or_gemv_q8_1": (None, [_u8p, C.c_int64, _u8p, C.c_int64, C.c_float, C.c_int, C.c_int,
+                                    C.c_int, _f64p, C.c_int64, C.c_int]),
+            "or_gemv_q8_1_f32": (None, [_u8p, C.c_int64, _u8p, C.c_int64, C.c_float, C.c_int, C.c_int,
+                                        C.c_int, _f32p, C.c_int64, C.c_int]),
+            "or_silu": (C.c_float, [C.c_float]),
+            "or_topk_softmax": (None, [_f32p, C.c_int, C.c_int, C.c_int, C.c_float, _i32p, _f32p]),
+            "or_router_logits": (None, [_f32p, _f32p, C.c_int, C.c_int, C.c_int, _f64p]),
+            "or_group_by_expert": (None, [_i32p, C.c_int, C.c_int, C.c_int, _i32p, _i32p, _i32p]),
+            "or_sf_offset": (C.c_int64, [C.c_int64, C.c_int64, C.c_int64]),
+            "or_sf_bytes": (C.c_int64, [C.c_int64, C.c_int64]),
+            "or_quantize_act_f32": (None, [_f32p, C.c_int, C.c_int, _u8p, _u8p]),
+            "or_repack_weight": (None, [_u8p, C.c_int, C.c_int, _u8p, _u8p]),
+            "or_gemm_f32out": (None, [_u8p, _u8p, _u8p, _u8p, _f64p, C.c_int, C.c_int, C.c_int,
+                                      C.c_float, C.c_int]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+# ---------------------------------------------------------------- helpers
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def nvfp4_dequant(blocks: np.ndarray) -> np.ndarray:
+    b = _c(blocks, np.uint8).reshape(-1)
+    nb = b.size // 36
+    out = np.empty(nb * 64, np.float32)
+    lib().or_nvfp4_dequant(b, nb, out)
+    return out
+
+
+def quantize_q8_1(x: np.ndarray) -> np.ndarray:
+    """x [T, K] f32 -> uint8 [T, K/32*36] q8_1 blocks."""
+    x = _c(x, np.float32)
+    if x.ndim == 1:
+        x = x[None]
+    T, K = x.shape
+    out = np.empty((T, K // 32 * 36), np.uint8)
+    lib().or_quantize_q8_1(x, K, T, K, out)
+    return out
+
+
+def quantize_q8_ggml_cpu(x: np.ndarray):
+    x = _c(x, np.float32).reshape(-1)
+    q = np.empty(x.size, np.int8)
+    d = np.empty(x.size // 32, np.uint16)
+    lib().or_quantize_q8_ggml_cpu(x, x.size, q, d)
+    return q, d
+
+
+def gemv_q8_1(w: np.ndarray, q8: np.ndarray, N: int, K: int, scale: float = 1.0,
+              nthreads: int = 0) -> np.ndarray:
+    """w uint8 [N, K/64*36], q8 uint8 [T, K/32*36] -> y f64 [T, N]."""
+    w = _c(w, np.uint8)
+    q8 = _c(q8, np.uint8)
+    if q8.ndim == 1:
+        q8 = q8[None]
+    T = q8.shape[0]
+    y = np.empty((T, N), np.float64)
+    lib().or_gemv_q8_1(w.reshape(-1), K // 64 * 36, q8.reshape(-1), K // 32, scale, N, K, T,
+                       y, N, nthreads)
+    return y
+
+
+def gemv_q8_1_f32(w, q8, N, K, scale=1.0, nthreads=0):
+    w = _c(w, np.uint8)
+    q8 = _c(q8, np.uint8)
+    if q8.ndim == 1:
+        q8 = q8[None]
+    T = q8.shape[0]
+    y = np.empty((T, N), np.float32)
+    lib().or_gemv_q8_1_f32(w.reshape(-1), K // 64 * 36, q8.reshape(-1), K // 32, scale, N, K, T,
+                           y, N, nthreads)
+    return y
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    x = _c(x, np.float32)
+    return np.array([lib().or_silu(float(v)) for v in x.reshape(-1)], np.float32).reshape(x.shape)
+
+
+def silu_np(x: np.ndarray) -> np.ndarray:
+    """Vectorised x / (1 + exp(-x)) in float32 (the same formula as or_silu)."""
+    x = np.asarray(x, np.float32)
+    with np.errstate(over="ignore"):
+        return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def router_logits(x, wr):
+    x = _c(x, np.float32)
+    wr = _c(wr, np.float32)
+    T, K = x.shape
+    E = wr.shape[0]
+    out = np.empty((T, E), np.float64)
+    lib().or_router_logits(x, wr, T, K, E, out)
+    return out
+
+
+def topk_softmax(logits, n_used, clamp=6.103515625e-5):
+    logits = _c(logits, np.float32)
+    T, E = logits.shape
+    ids = np.empty((T, n_used), np.int32)
+    w = np.empty((T, n_used), np.float32)
+    lib().or_topk_softmax(logits, T, E, n_used, clamp, ids, w)
+    return ids, w
+
+
+def group_by_expert(ids, E):
+    ids = _c(ids, np.int32)
+    T, n_used = ids.shape
+    eoff = np.empty(E + 1, np.int32)
+    slots = np.empty(T * n_used, np.int32)
+    act = np.empty(E + 1, np.int32)
+    lib().or_group_by_expert(ids, T, n_used, E, eoff, slots, act)
+    return eoff, slots, act
+
+
+def sf_bytes(rows, K):
+    return int(lib().or_sf_bytes(rows, K))
+
+
+def sf_offset(row, k, K):
+    return int(lib().or_sf_offset(row, k, K))
+
+
+def quantize_act_f32(x):
+    x = _c(x, np.float32)
+    M, K = x.shape
+    packed = np.zeros((M, K // 2), np.uint8)
+    sf = np.zeros(sf_bytes(M, K), np.uint8)
+    lib().or_quantize_act_f32(x, M, K, packed, sf)
+    return packed, sf
+
+
+def repack_weight(blocks, N, K):
+    b = _c(blocks, np.uint8).reshape(-1)
+    packed = np.zeros((N, K // 2), np.uint8)
+    sf = np.zeros(sf_bytes(N, K), np.uint8)
+    lib().or_repack_weight(b, N, K, packed, sf)
+    return packed, sf
+
+
+def gemm_f32out(A, SFA, B, SFB, M, N, K, alpha=1.0, nthreads=0):
+    D = np.empty((M, N), np.float64)
+    lib().or_gemm_f32out(_c(A, np.uint8).reshape(-1), _c(SFA, np.uint8), _c(B, np.uint8).reshape(-1),
+                         _c(SFB, np.uint8), D, M, N, K, alpha, nthreads)
+    return D
+
+
+# ------------------------------------------------------------ comparisons
+
+def rel_err(mine: np.ndarray, ref: np.ndarray, floor_frac: float = 1e-3) -> float:
+    """max |mine - ref| / max(|ref|, floor_frac * rms(ref))."""
+    mine = np.asarray(mine, np.float64)
+    ref = np.asarray(ref, np.float64)
+    if not np.all(np.isfinite(mine)):
+        return float("inf")
+    rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
+    den = np.maximum(np.abs(ref), floor_frac * rms + 1e-30)
+    return float(np.max(np.abs(mine - ref) / den)) if ref.size else 0.0
+
+
+def ref_gate_bad(mine, ref, atol=1e-4, rtol=2e-3) -> int:
+    """The reference's conjunctive gate (src/fr_win_flint_batched.cuh:478-489):
+    bad iff abs > atol and rel > rtol, and any non-finite value is bad."""
+    mine = np.asarray(mine, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.abs(mine - ref)
+    rel = d / (np.abs(ref) + 1e-6)
+    bad = (d > atol) & (rel > rtol)
+    bad |= ~np.isfinite(mine)
+    return int(bad.sum())
