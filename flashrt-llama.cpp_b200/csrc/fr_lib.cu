@@ -404,3 +404,89 @@ int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
 }
 
 } // extern "C"
+
+// ======================================================================
+// Dense FFN without device allocation (static scratch).  For callers that
+// cannot call cudaMalloc: graph capture, hosts whose allocator plans every
+// buffer up front, fixed device-memory budgets.
+// ======================================================================
+namespace frb {
+
+static __device__ __align__(256) unsigned char g_ffn_noalloc_scratch[FR_FFN_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_ffn_noalloc_scratch for the current device.  In host
+// code the array's name is only a host-side stand-in, so the address is looked
+// up once per device with that device current and cached.
+static int ffn_noalloc_scratch(unsigned char **out) {
+    static unsigned char *addr[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_rc(e);
+    if (dev < 0 || dev >= 64) return FR_ENODEVICE;
+    std::lock_guard<std::mutex> lk(mu);
+    if (addr[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_ffn_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_rc(e);
+        addr[dev] = static_cast<unsigned char *>(p);
+    }
+    *out = addr[dev];
+    return FR_OK;
+}
+
+} // namespace frb
+
+extern "C" int fr_ffn_nvfp4_noalloc(const float *x, const void *wg, const void *wu, const void *wd,
+                                    const float *sg, const float *su, const float *sd, const float *resid,
+                                    float *out, int T, int n_embd, int n_ff, cudaStream_t stream) {
+    if (fault_hit("fr_ffn_nvfp4_noalloc")) return FR_EINJECTED;
+    if (!x || !wg || !wu || !wd || !out || T <= 0 || n_embd % 256 != 0 || n_ff % 256 != 0) return FR_EINVAL;
+    if (!aligned16(wg) || !aligned16(wu) || !aligned16(wd)) return FR_EINVAL;
+    const size_t q8x_bytes = static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES;
+    const size_t glu_bytes = static_cast<size_t>(T) * n_ff * sizeof(float);
+    const size_t gq8_bytes = static_cast<size_t>(T) * (n_ff / 32) * Q8_BYTES;
+    // each piece starts on a 256-byte boundary
+    const size_t o_glu = (q8x_bytes + 255) / 256 * 256;
+    const size_t o_gq8 = o_glu + (glu_bytes + 255) / 256 * 256;
+    if (o_gq8 + gq8_bytes > FR_FFN_NOALLOC_SCRATCH_BYTES) return FR_ETOOBIG;
+    unsigned char *scratch = nullptr;
+    int rc = ffn_noalloc_scratch(&scratch);
+    if (rc != FR_OK) return rc;
+    void *q8x = scratch;
+    float *glu = reinterpret_cast<float *>(scratch + o_glu);
+    void *gq8 = scratch + o_gq8;
+    const int64_t ld_gu = static_cast<int64_t>(n_embd) / 64 * NV_BYTES;
+    const int64_t ld_d = static_cast<int64_t>(n_ff) / 64 * NV_BYTES;
+    rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
+    if (rc != FR_OK) return rc;
+    GvParams p{};
+    p.w0 = static_cast<const uint8_t *>(wg);
+    p.w1 = static_cast<const uint8_t *>(wu);
+    p.w_ld = ld_gu;
+    p.q8 = static_cast<const uint8_t *>(q8x);
+    p.ldq = n_embd / 32;
+    p.s0 = sg;
+    p.s1 = su;
+    p.y = glu;
+    p.ldy = n_ff;
+    p.N = n_ff;
+    p.K = n_embd;
+    rc = gemv_run(p, T, true, stream);
+    if (rc != FR_OK) return rc;
+    rc = quantize_launch(glu, n_ff, gq8, n_ff / 32, T, n_ff, stream);
+    if (rc != FR_OK) return rc;
+    GvParams q{};
+    q.w0 = static_cast<const uint8_t *>(wd);
+    q.w_ld = ld_d;
+    q.q8 = static_cast<const uint8_t *>(gq8);
+    q.ldq = n_ff / 32;
+    q.s0 = sd;
+    q.resid = resid;
+    q.ldr = n_embd;
+    q.y = out;
+    q.ldy = n_embd;
+    q.N = n_embd;
+    q.K = n_ff;
+    return gemv_run(q, T, false, stream);
+}

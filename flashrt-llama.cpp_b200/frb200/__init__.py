@@ -53,6 +53,7 @@ SIGNATURES = {
     "fr_gemv_nvfp4_q8_1_swiglu": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp]),
     "fr_mul_mat_nvfp4": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp]),
     "fr_ffn_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "fr_ffn_nvfp4_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "fr_moe_route": (_i32, [_vp, _i64, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "fr_mul_mat_id_nvfp4": (_i32, [_vp, _i64, _i64, _i32, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64,
                                    _i32, _i32, _i32, _i32, _vp]),

@@ -112,6 +112,34 @@ int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
                  float *out, int T, int n_embd, int n_ff,
                  float *chk_glu, void *chk_glu_q8, cudaStream_t stream);
 
+/* The same dense FFN for callers that cannot allocate device memory.
+ * No counterpart in the reference.
+ *
+ * fr_ffn_nvfp4 grows a private workspace with cudaMalloc the first time it
+ * sees a larger shape.  Some callers cannot allow that: code running while a
+ * stream is being captured into a CUDA graph (cudaMalloc is not permitted
+ * there), hosts such as ggml whose allocator plans every buffer of a graph up
+ * front and expects operators not to allocate behind its back, and serving
+ * processes with a fixed device-memory budget.  This entry point allocates
+ * nothing: its intermediates (q8_1 of x, the GLU, q8_1 of the GLU) live in a
+ * static device array of FR_FFN_NOALLOC_SCRATCH_BYTES that every GPU which
+ * loads the library holds until the process exits.
+ *   - Required scratch: T * (n_embd/32*36 + n_ff*4 + n_ff/32*36) bytes; a
+ *     call that needs more returns FR_ETOOBIG and launches nothing.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls share the one array and it keeps the last call's contents.
+ *     Every intermediate is fully rewritten by each call, so nothing needs
+ *     clearing, but calls that overlap on the GPU (different streams without
+ *     ordering between them) race on the array: order them on one stream or
+ *     with events. */
+#define FR_FFN_NOALLOC_SCRATCH_BYTES (8u << 20)
+#define FR_ETOOBIG    (-904)  /* request larger than the static scratch */
+int fr_ffn_nvfp4_noalloc(const float *x, const void *wg, const void *wu, const void *wd,
+                         const float *sg, const float *su, const float *sd, const float *resid,
+                         float *out, int T, int n_embd, int n_ff, cudaStream_t stream);
+
 /* -------------------------------------------------------------- (a7/a8) MoE routing
  * logits[t, e] = x[t] . W_r[e] (f32), softmax over E, n_used rounds of
  * arg-max (lower expert id wins ties), w = p / max(sum p_sel, clamp)
