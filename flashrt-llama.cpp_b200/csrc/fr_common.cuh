@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <cfloat>
 
 #include "../../include/fr_b200.h"
 

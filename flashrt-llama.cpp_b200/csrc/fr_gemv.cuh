@@ -30,8 +30,11 @@
 namespace frb {
 
 // ------------------------------------------------------------ quantize_q8_1
-__global__ void __launch_bounds__(256) k_quantize_q8_1(const float *__restrict__ x, int64_t ldx,
-                                                       uint8_t *__restrict__ q8, int64_t ldq, int T, int K) {
+// Row r of the output is x row (r / n_in) * ldx + (r % n_in) * ldx_in, so one
+// launch also covers [T, n_used, K] activations with two strides.
+__global__ void __launch_bounds__(256) k_quantize_q8_1(const float *__restrict__ x, int64_t ldx, int n_in,
+                                                       int64_t ldx_in, uint8_t *__restrict__ q8, int64_t ldq,
+                                                       int T, int K) {
     fr_pdl_wait();
     fr_pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -39,7 +42,8 @@ __global__ void __launch_bounds__(256) k_quantize_q8_1(const float *__restrict__
     const int64_t c = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
     if (c >= static_cast<int64_t>(T) * nc) return;
     const int t = static_cast<int>(c / nc), ch = static_cast<int>(c % nc);
-    const float xi = x[t * ldx + static_cast<int64_t>(ch) * Q8_ELEMS + lane];
+    const int64_t xrow = static_cast<int64_t>(t / n_in) * ldx + static_cast<int64_t>(t % n_in) * ldx_in;
+    const float xi = x[xrow + static_cast<int64_t>(ch) * Q8_ELEMS + lane];
     const q8_lane r = q8_1_chunk(xi);
     uint8_t *blk = q8 + (t * ldq + ch) * Q8_BYTES;
     blk[4 + lane] = static_cast<uint8_t>(r.q);

@@ -8,6 +8,10 @@
 #include "fr_common.cuh"
 #include "fr_runtime.cuh"
 #include "fr_gemv.cuh"
+#include "fr_moe.cuh"
+#include "fr_w4a4.cuh"
+
+#include <cudaTypedefs.h>
 
 namespace frb {
 
@@ -140,14 +144,8 @@ template <int LG, int TT, int EPI>
 static int gv_launch_inst(const GvParams &p, const GvPlan &pl, cudaStream_t stream) {
     auto kern = k_gemv<LG, TT, EPI>;
     static bool attr_done[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_done[dev & 63]) {
-        const DevInfo &di = dev_info();
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin);
-        if (e != cudaSuccess) return cuda_rc(e);
-        attr_done[dev & 63] = true;
-    }
+    const int arc = allow_max_smem(kern, attr_done);
+    if (arc != FR_OK) return arc;
     return launch_pdl(kern, dim3(pl.grid), dim3(GV_THREADS), pl.smem, stream, p);
 }
 
@@ -199,11 +197,16 @@ static int check_gemv_shape(const void *w, int64_t w_ld, int N, int K, int T) {
     return FR_OK;
 }
 
-static int quantize_launch(const float *x, int64_t ldx, void *q8, int64_t ldq, int T, int K, cudaStream_t stream) {
-    const int64_t chunks = static_cast<int64_t>(T) * (K / 32);
+static int quantize_launch2(const float *x, int64_t ldx, int n_in, int64_t ldx_in, void *q8, int64_t ldq, int rows,
+                            int K, cudaStream_t stream) {
+    const int64_t chunks = static_cast<int64_t>(rows) * (K / 32);
     const int grid = static_cast<int>((chunks + 7) / 8);
-    return launch_pdl(k_quantize_q8_1, dim3(grid), dim3(256), 0, stream, x, ldx,
-                      static_cast<uint8_t *>(q8), ldq, T, K);
+    return launch_pdl(k_quantize_q8_1, dim3(grid), dim3(256), 0, stream, x, ldx, n_in, ldx_in,
+                      static_cast<uint8_t *>(q8), ldq, rows, K);
+}
+
+static int quantize_launch(const float *x, int64_t ldx, void *q8, int64_t ldq, int T, int K, cudaStream_t stream) {
+    return quantize_launch2(x, ldx, 1, 0, q8, ldq, T, K, stream);
 }
 
 } // namespace frb
@@ -225,6 +228,7 @@ const char *fr_strerror(int rc) {
     case FR_ECAPTURE: return "workspace growth refused during stream capture";
     case FR_EINJECTED: return "injected fault";
     case FR_ENODEVICE: return "no suitable CUDA device";
+    case FR_ETOOBIG: return "request larger than the static scratch";
     default: break;
     }
     if (rc < 0 && rc > -1000) return cudaGetErrorString(static_cast<cudaError_t>(-rc));
@@ -490,3 +494,350 @@ extern "C" int fr_ffn_nvfp4_noalloc(const float *x, const void *wg, const void *
     q.K = n_ff;
     return gemv_run(q, T, false, stream);
 }
+
+// ======================================================================
+// MoE: routing, mul_mat_id, fused MoE FFN
+// ======================================================================
+namespace frb {
+
+struct MoePlan {
+    int LG, TT, RS, rows_per_cta, chunks, grid, slot_bytes;
+    size_t smem;
+};
+
+static MoePlan moe_plan(int N, int K, int64_t w_ld, bool dual, int max_active, int max_tok) {
+    const DevInfo &di = dev_info();
+    MoePlan pl{};
+    const int NB = K / 64;
+    pl.LG = pick_lg(NB);
+    pl.RS = 32 / pl.LG;
+    pl.slot_bytes = static_cast<int>((pl.RS * w_ld * (dual ? 2 : 1) + 15) / 16 * 16);
+    pl.TT = pow2_tokens(std::max(1, std::min(8, max_tok)));
+    const size_t act = static_cast<size_t>(pl.TT) * NB * 72;
+    const int smem_cap = di.smem_optin > 0 ? di.smem_optin : 227 * 1024;
+    const long half = (smem_cap - 2048) / 2 - 2048 - 1024 - static_cast<long>(act);
+    const long full = smem_cap - 4096 - 1024 - static_cast<long>(act);
+    long budget = half >= pl.slot_bytes * 4 ? half : full;
+    int max_st = static_cast<int>(std::min<long>(256, budget / pl.slot_bytes));
+    max_st = std::max(1, max_st);
+    const int target = std::max(1, 2 * di.sms);
+    const long rows_total = static_cast<long>(N) * std::max(1, max_active);
+    int rpc = static_cast<int>((rows_total + target - 1) / target);
+    rpc = (rpc + pl.RS - 1) / pl.RS * pl.RS;
+    rpc = std::max(pl.RS, std::min(rpc, max_st * pl.RS));
+    pl.rows_per_cta = rpc;
+    pl.chunks = (N + rpc - 1) / rpc;
+    pl.grid = std::max(1, max_active) * pl.chunks;
+    const int n_st = (rpc + pl.RS - 1) / pl.RS;
+    pl.smem = 2048 + static_cast<size_t>(n_st) * pl.slot_bytes + act;
+    return pl;
+}
+
+template <int LG, int TT, bool DUAL>
+static int moe_launch_inst(const MoeParams &p, const MoePlan &pl, cudaStream_t stream) {
+    auto kern = k_moe_gemv<LG, TT, DUAL>;
+    static bool attr_done[64] = {};
+    const int arc = allow_max_smem(kern, attr_done);
+    if (arc != FR_OK) return arc;
+    return launch_pdl(kern, dim3(pl.grid), dim3(GV_THREADS), pl.smem, stream, p);
+}
+
+template <int LG, bool DUAL>
+static int moe_launch_tt(const MoeParams &p, const MoePlan &pl, cudaStream_t stream) {
+    switch (pl.TT) {
+    case 1: return moe_launch_inst<LG, 1, DUAL>(p, pl, stream);
+    case 2: return moe_launch_inst<LG, 2, DUAL>(p, pl, stream);
+    case 4: return moe_launch_inst<LG, 4, DUAL>(p, pl, stream);
+    default: return moe_launch_inst<LG, 8, DUAL>(p, pl, stream);
+    }
+}
+
+template <bool DUAL>
+static int moe_launch(MoeParams p, int max_active, int max_tok, cudaStream_t stream) {
+    const MoePlan pl = moe_plan(p.N, p.K, p.w_ld, DUAL, max_active, max_tok);
+    p.rows_per_cta = pl.rows_per_cta;
+    p.chunks = pl.chunks;
+    p.rows_per_stage = pl.RS;
+    p.slot_bytes = pl.slot_bytes;
+    p.word_mode = (p.w_ld % 16 != 0 || p.e_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(p.w0) & 15) ||
+                   (p.w1 && (reinterpret_cast<uintptr_t>(p.w1) & 15))) ? 1 : 0;
+    switch (pl.LG) {
+    case 32: return moe_launch_tt<32, DUAL>(p, pl, stream);
+    case 16: return moe_launch_tt<16, DUAL>(p, pl, stream);
+    case 8: return moe_launch_tt<8, DUAL>(p, pl, stream);
+    default: return moe_launch_tt<4, DUAL>(p, pl, stream);
+    }
+}
+
+static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+static int group_smem(int T, int n_used) {
+    return static_cast<int>((static_cast<size_t>(T) * n_used + 2 * MOE_MAX_E) * sizeof(int32_t));
+}
+
+static int route_launch(const float *x, int64_t ldx, const float *w_r, int T, int K, int E, int n_used,
+                        float clamp_val, float *logits, int32_t *ids, float *wts, int32_t *eoff, int32_t *slots,
+                        int32_t *act, cudaStream_t stream) {
+    int rc = launch_pdl(k_router_logits, dim3((E + 3) / 4, (T + 3) / 4), dim3(256), 0, stream, x, ldx, w_r, logits,
+                        T, K, E);
+    if (rc != FR_OK) return rc;
+    static bool attr_done[64] = {};
+    rc = allow_max_smem(k_topk_group, attr_done);
+    if (rc != FR_OK) return rc;
+    return launch_pdl(k_topk_group, dim3(1), dim3(1024), group_smem(T, n_used), stream,
+                      static_cast<const float *>(logits), T, E, n_used, clamp_val, ids, wts, eoff, slots, act);
+}
+
+static int check_route_shape(int T, int K, int E, int n_used) {
+    if (T <= 0 || K <= 0 || K % 4 != 0 || E <= 0 || E % 32 != 0 || E > MOE_MAX_E) return FR_EINVAL;
+    if (n_used <= 0 || n_used > MOE_MAX_USED || n_used > E) return FR_EINVAL;
+    if (static_cast<long>(T) * n_used > MOE_MAX_SLOTS) return FR_EINVAL;
+    return FR_OK;
+}
+
+} // namespace frb
+
+extern "C" {
+
+int fr_moe_route(const float *x, int64_t ldx, const float *w_r, int T, int K, int E, int n_used, float clamp_val,
+                 float *logits, int32_t *ids, float *wts, int32_t *eoff, int32_t *slots, int32_t *act,
+                 cudaStream_t stream) {
+    if (fault_hit("fr_moe_route")) return FR_EINJECTED;
+    int rc = check_route_shape(T, K, E, n_used);
+    if (rc != FR_OK) return rc;
+    if (!x || !w_r || !logits || !ids || !wts || !eoff || !slots || !act || ldx < K) return FR_EINVAL;
+    if (!aligned16(x) || !aligned16(w_r) || ldx % 4 != 0) return FR_EINVAL;
+    return route_launch(x, ldx, w_r, T, K, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream);
+}
+
+int fr_mul_mat_id_nvfp4(const void *w, int64_t nb01, int64_t nb02, int E, const float *x, int64_t x_ld_slot,
+                        int64_t x_ld_tok, const int32_t *ids, int64_t ids_ld, float *dst, int64_t dst_ld_slot,
+                        int64_t dst_ld_tok, int T, int n_used, int N, int K, cudaStream_t stream) {
+    if (fault_hit("fr_mul_mat_id_nvfp4")) return FR_EINJECTED;
+    if (!w || !x || !ids || !dst || T <= 0 || n_used <= 0 || N <= 0 || K <= 0 || K % 64 != 0) return FR_EINVAL;
+    if (E <= 0 || E > MOE_MAX_E || n_used > 64 || static_cast<long>(T) * n_used > MOE_MAX_SLOTS) return FR_EINVAL;
+    if (nb01 < static_cast<int64_t>(K / 64) * NV_BYTES || nb01 % 4 != 0 || nb02 < nb01 * N || nb02 % 4 != 0) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(w) & 3) || ids_ld < n_used || x_ld_tok < K) return FR_EINVAL;
+    const bool bcast = x_ld_slot == 0;
+    const int qrows = bcast ? T : T * n_used;
+    const size_t q8_bytes = align256(static_cast<size_t>(qrows) * (K / 32) * Q8_BYTES);
+    const size_t grp_bytes = align256(static_cast<size_t>(2 * (E + 1) + T * n_used) * sizeof(int32_t));
+    void *wsp = nullptr;
+    int rc = workspace_get(WS_MOE, q8_bytes + grp_bytes, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    uint8_t *q8 = static_cast<uint8_t *>(wsp);
+    int32_t *eoff = reinterpret_cast<int32_t *>(q8 + q8_bytes);
+    int32_t *act = eoff + (E + 1);
+    int32_t *slots = act + (E + 1);
+    static bool attr_done[64] = {};
+    rc = allow_max_smem(k_group_ids, attr_done);
+    if (rc != FR_OK) return rc;
+    rc = launch_pdl(k_group_ids, dim3(1), dim3(1024), group_smem(T, n_used), stream, ids, ids_ld, T, n_used, E, eoff,
+                    slots, act);
+    if (rc != FR_OK) return rc;
+    rc = bcast ? quantize_launch2(x, x_ld_tok, 1, 0, q8, K / 32, T, K, stream)
+               : quantize_launch2(x, x_ld_tok, n_used, x_ld_slot, q8, K / 32, T * n_used, K, stream);
+    if (rc != FR_OK) return rc;
+    MoeParams p{};
+    p.w0 = static_cast<const uint8_t *>(w);
+    p.e_stride = nb02;
+    p.w_ld = nb01;
+    p.N = N;
+    p.K = K;
+    p.q8 = q8;
+    p.ldq = K / 32;
+    p.bcast = bcast ? 1 : 0;
+    p.n_used = n_used;
+    p.E = E;
+    p.eoff = eoff;
+    p.slots = slots;
+    p.act = act;
+    p.out = dst;
+    p.ld_tok = dst_ld_tok;
+    p.ld_slot = dst_ld_slot;
+    return moe_launch<false>(p, std::min(E, T * n_used), T, stream);
+}
+
+int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const void *wu, const void *wd, const float *sg,
+                     const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                     int E, int n_used, float clamp_val, int32_t *chk_ids, float *chk_wts, float *chk_glu,
+                     float *chk_part, cudaStream_t stream) {
+    if (fault_hit("fr_moe_ffn_nvfp4")) return FR_EINJECTED;
+    int rc = check_route_shape(T, n_embd, E, n_used);
+    if (rc != FR_OK) return rc;
+    if (!x || !w_r || !wg || !wu || !wd || !out || n_embd % 64 != 0 || n_ff % 64 != 0) return FR_EINVAL;
+    if (!aligned16(x) || !aligned16(w_r)) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(wg) & 3) || (reinterpret_cast<uintptr_t>(wu) & 3) ||
+        (reinterpret_cast<uintptr_t>(wd) & 3))
+        return FR_EINVAL;
+    const int S = T * n_used;
+    const int64_t ld_gu = static_cast<int64_t>(n_embd) / 64 * NV_BYTES;
+    const int64_t ld_d = static_cast<int64_t>(n_ff) / 64 * NV_BYTES;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_logits = take(static_cast<size_t>(T) * E * 4);
+    const size_t o_ids = take(static_cast<size_t>(S) * 4);
+    const size_t o_wts = take(static_cast<size_t>(S) * 4);
+    const size_t o_eoff = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_act = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_slots = take(static_cast<size_t>(S) * 4);
+    const size_t o_q8x = take(static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES);
+    const size_t o_glu = take(static_cast<size_t>(S) * n_ff * 4);
+    const size_t o_q8g = take(static_cast<size_t>(S) * (n_ff / 32) * Q8_BYTES);
+    const size_t o_part = take(static_cast<size_t>(S) * n_embd * 4);
+    void *wsp = nullptr;
+    rc = workspace_get(WS_MOE, off, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    uint8_t *base = static_cast<uint8_t *>(wsp);
+    float *logits = reinterpret_cast<float *>(base + o_logits);
+    int32_t *ids = chk_ids ? chk_ids : reinterpret_cast<int32_t *>(base + o_ids);
+    float *wts = chk_wts ? chk_wts : reinterpret_cast<float *>(base + o_wts);
+    int32_t *eoff = reinterpret_cast<int32_t *>(base + o_eoff);
+    int32_t *act = reinterpret_cast<int32_t *>(base + o_act);
+    int32_t *slots = reinterpret_cast<int32_t *>(base + o_slots);
+    uint8_t *q8x = base + o_q8x;
+    float *glu = chk_glu ? chk_glu : reinterpret_cast<float *>(base + o_glu);
+    uint8_t *q8g = base + o_q8g;
+    float *part = chk_part ? chk_part : reinterpret_cast<float *>(base + o_part);
+
+    rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream);
+    if (rc != FR_OK) return rc;
+    rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
+    if (rc != FR_OK) return rc;
+    MoeParams p{};
+    p.w0 = static_cast<const uint8_t *>(wg);
+    p.w1 = static_cast<const uint8_t *>(wu);
+    p.e_stride = ld_gu * n_ff;
+    p.w_ld = ld_gu;
+    p.N = n_ff;
+    p.K = n_embd;
+    p.q8 = q8x;
+    p.ldq = n_embd / 32;
+    p.bcast = 1;
+    p.n_used = n_used;
+    p.E = E;
+    p.eoff = eoff;
+    p.slots = slots;
+    p.act = act;
+    p.s0 = sg;
+    p.s1 = su;
+    p.out = glu;
+    p.ld_tok = static_cast<int64_t>(n_used) * n_ff;
+    p.ld_slot = n_ff;
+    const int max_active = std::min(E, S);
+    rc = moe_launch<true>(p, max_active, T, stream);
+    if (rc != FR_OK) return rc;
+    rc = quantize_launch(glu, n_ff, q8g, n_ff / 32, S, n_ff, stream);
+    if (rc != FR_OK) return rc;
+    MoeParams q{};
+    q.w0 = static_cast<const uint8_t *>(wd);
+    q.e_stride = ld_d * n_embd;
+    q.w_ld = ld_d;
+    q.N = n_embd;
+    q.K = n_ff;
+    q.q8 = q8g;
+    q.ldq = n_ff / 32;
+    q.bcast = 0;
+    q.n_used = n_used;
+    q.E = E;
+    q.eoff = eoff;
+    q.slots = slots;
+    q.act = act;
+    q.s0 = sd;
+    q.out = part;
+    q.ld_tok = static_cast<int64_t>(n_used) * n_embd;
+    q.ld_slot = n_embd;
+    rc = moe_launch<false>(q, max_active, T, stream);
+    if (rc != FR_OK) return rc;
+    return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream,
+                      static_cast<const float *>(part), static_cast<const float *>(wts), resid, out, n_used, n_embd);
+}
+
+} // extern "C"
+
+// ======================================================================
+// W4A4: quantize_act_f32, repack_weight, gemm_f32out (include/fr_kernels.h)
+// ======================================================================
+namespace frb {
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// [rows, row_bytes] uint8 matrix, box 128 rows x 128 bytes, 128-byte swizzle
+static int make_map_sw128(CUtensorMap *map, const void *base, int64_t rows, int64_t row_bytes) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return FR_ENODEVICE;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    cuuint32_t box[2] = {128, 128};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
+}
+
+} // namespace frb
+
+extern "C" {
+
+int64_t fr_sf_bytes(int64_t rows, int64_t K) { return (rows + 127) / 128 * 128 * (((K / 16) + 3) / 4 * 4); }
+int64_t fr_packed_bytes(int64_t rows, int64_t K) { return rows * (K / 2); }
+
+int fr_quantize_act_f32(const float *src, void *dst_packed, void *dst_sfa, int M, int K, cudaStream_t stream) {
+    if (fault_hit("fr_quantize_act_f32")) return FR_EINJECTED;
+    if (!src || !dst_packed || !dst_sfa || M <= 0 || K <= 0 || K % 16 != 0) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst_packed) & 7)) return FR_EINVAL;
+    const int nb = K / 16;
+    return launch_pdl(k_quantize_act, dim3((nb + 127) / 128, M), dim3(128), 0, stream,
+                      reinterpret_cast<const float4 *>(src), static_cast<uint2 *>(dst_packed),
+                      static_cast<uint8_t *>(dst_sfa), M, K);
+}
+
+int fr_repack_weight(const void *ggml_blocks, void *dst_packed, void *dst_sf, int N, int K, cudaStream_t stream) {
+    if (fault_hit("fr_repack_weight")) return FR_EINJECTED;
+    if (!ggml_blocks || !dst_packed || !dst_sf || N <= 0 || K <= 0 || K % 64 != 0) return FR_EINVAL;
+    if (reinterpret_cast<uintptr_t>(dst_packed) & 7) return FR_EINVAL;
+    // the layout's largest offset must fit the caller's sf_bytes(N, K) buffer
+    if (sf_offset(N - 1, K - 16, K) + 1 > fr_sf_bytes(N, K)) return FR_ELAYOUT;
+    const int K16 = K / 16;
+    return launch_pdl(k_repack, dim3((K16 + 127) / 128, N), dim3(128), 0, stream,
+                      static_cast<const uint8_t *>(ggml_blocks), static_cast<uint2 *>(dst_packed),
+                      static_cast<uint8_t *>(dst_sf), N, K);
+}
+
+int fr_gemm_f32out(const void *A_packed, const void *SFA, const void *B_packed, const void *SFB, float *D, int M,
+                   int N, int K, float alpha, bool widen, cudaStream_t stream) {
+    (void) widen;   // the reference ignores it too (src/fr_gemm_f32out.cu:196-197)
+    if (fault_hit("fr_gemm_f32out")) return FR_EINJECTED;
+    if (!A_packed || !SFA || !B_packed || !SFB || !D || M <= 0 || N <= 0 || K <= 0) return FR_EINVAL;
+    if (K % 64 != 0 || N % 16 != 0) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(D) & 15) || (reinterpret_cast<uintptr_t>(A_packed) & 15) ||
+        (reinterpret_cast<uintptr_t>(B_packed) & 15) || (reinterpret_cast<uintptr_t>(SFA) & 15) ||
+        (reinterpret_cast<uintptr_t>(SFB) & 15))
+        return FR_EINVAL;
+    CUtensorMap ma, mb;
+    int rc = make_map_sw128(&ma, A_packed, M, K / 2);
+    if (rc != FR_OK) return rc;
+    rc = make_map_sw128(&mb, B_packed, N, K / 2);
+    if (rc != FR_OK) return rc;
+    static bool attr_done[64] = {};
+    rc = allow_max_smem(k_gemm_nvf4, attr_done);
+    if (rc != FR_OK) return rc;
+    GemmArgs g{static_cast<const uint8_t *>(SFA), static_cast<const uint8_t *>(SFB), D, M, N, K, alpha};
+    return launch_pdl(k_gemm_nvf4, dim3((N + G_BN - 1) / G_BN, (M + G_BM - 1) / G_BM), dim3(G_THREADS), G_SMEM,
+                      stream, ma, mb, g);
+}
+
+} // extern "C"

@@ -1,0 +1,392 @@
+// fr_moe.cuh -- MoE routing, token permute, expert-grouped matvec, combine.
+//
+//   k_router_logits : logits[t, e] = x[t] . W_r[e]           (f32)
+//   k_topk_group    : softmax top-k per token (one warp per token, the
+//                     reference's algorithm, src/fr_win_qwen36_sm120.cu:
+//                     1826-1870) and, in the same single-CTA launch, the token
+//                     permute: eoff/slots/act (src/fr_win_flint_batched_moe.cuh:
+//                     76-166).  Slots inside an expert are in slot order, so the
+//                     grouping is deterministic (the reference's atomics leave
+//                     it unspecified).
+//   k_group_ids     : the same permute for ids given by the caller (mul_mat_id)
+//   k_moe_gemv      : CTA = (active expert, row chunk).  The chunk's weight rows
+//                     are bulk-copied into shared memory once and stay resident
+//                     while the expert's tokens pass through in windows of TT,
+//                     so every used expert's rows are read from HBM once per
+//                     call, whatever the number of tokens routed to it.
+//   k_moe_combine   : out[t] = sum_k part[t,k] * w[t,k] in slot order (+ resid)
+//                     (src/fr_win_flint_batched_moe.cuh:342-379).
+#pragma once
+
+#include "fr_gemv.cuh"
+
+namespace frb {
+
+constexpr int MOE_MAX_E = 256;
+constexpr int MOE_MAX_USED = 32;
+constexpr int MOE_MAX_SLOTS = 8192;   // T * n_used handled by the single-CTA permute
+
+// ------------------------------------------------------------ router logits
+// grid (E / 4, ceil(T / 4)), 256 threads: 4 expert rows x 4 tokens per CTA.
+__global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, int64_t ldx,
+                                                       const float *__restrict__ wr, float *__restrict__ logits,
+                                                       int T, int K, int E) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    __shared__ float red[8][16];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e0 = blockIdx.x * 4, t0 = blockIdx.y * 4;
+    float acc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[r][u] = 0.0f;
+    for (int k = tid * 4; k < K; k += 256 * 4) {
+        float4 wv[4], xv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            wv[r] = (e0 + r < E) ? *reinterpret_cast<const float4 *>(wr + static_cast<int64_t>(e0 + r) * K + k)
+                                 : make_float4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            xv[u] = (t0 + u < T) ? *reinterpret_cast<const float4 *>(x + static_cast<int64_t>(t0 + u) * ldx + k)
+                                 : make_float4(0, 0, 0, 0);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                acc[r][u] += wv[r].x * xv[u].x + wv[r].y * xv[u].y + wv[r].z * xv[u].z + wv[r].w * xv[u].w;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            float v = acc[r][u];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) red[warp][r * 4 + u] = v;
+        }
+    __syncthreads();
+    if (tid < 16) {
+        const int r = tid >> 2, u = tid & 3;
+        float v = red[0][tid];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) v += red[w][tid];
+        if (e0 + r < E && t0 + u < T) logits[static_cast<int64_t>(t0 + u) * E + e0 + r] = v;
+    }
+}
+
+// ------------------------------------------------------------ permute helper
+// Single-CTA stable grouping of n_slots slot ids held in shared memory
+// (ids_s[s] = expert of slot s): eoff[E+1], slots[], act[E+1].  1024 threads.
+__device__ __forceinline__ void group_slots(const int32_t *ids_s, int n_slots, int E, int32_t *eoff,
+                                            int32_t *slots, int32_t *act, int32_t *cnt_s, int32_t *off_s) {
+    const int tid = threadIdx.x;
+    if (tid < E) {
+        int c = 0;
+        for (int s = 0; s < n_slots; ++s) c += ids_s[s] == tid;
+        cnt_s[tid] = c;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0, na = 0;
+        for (int e = 0; e < E; ++e) {
+            off_s[e] = run;
+            eoff[e] = run;
+            run += cnt_s[e];
+            if (cnt_s[e] > 0) act[na++] = e;
+        }
+        eoff[E] = run;
+        for (int e = na; e < E; ++e) act[e] = -1;
+        act[E] = na;
+    }
+    __syncthreads();
+    if (tid < E && cnt_s[tid] > 0) {
+        int pos = off_s[tid];
+        for (int s = 0; s < n_slots; ++s)
+            if (ids_s[s] == tid) slots[pos++] = s;
+    }
+}
+
+// ------------------------------------------------------------ top-k + permute
+// One CTA of 1024 threads.  Warp w routes tokens w, w+32, ...
+__global__ void __launch_bounds__(1024) k_topk_group(const float *__restrict__ logits, int T, int E, int n_used,
+                                                     float clamp_val, int32_t *__restrict__ ids_out,
+                                                     float *__restrict__ w_out, int32_t *__restrict__ eoff,
+                                                     int32_t *__restrict__ slots, int32_t *__restrict__ act) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    extern __shared__ int32_t sm_i[];
+    int32_t *ids_s = sm_i;                        // [T * n_used]
+    int32_t *cnt_s = ids_s + T * n_used;          // [E]
+    int32_t *off_s = cnt_s + MOE_MAX_E;           // [E]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = E / 32;
+    for (int t = warp; t < T; t += 32) {
+        const float *l = logits + static_cast<int64_t>(t) * E;
+        float wt[MOE_MAX_E / 32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+            wt[i] = (i < per) ? l[lane + 32 * i] : -INFINITY;
+            mx = fmaxf(mx, wt[i]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+            if (i < per) {
+                wt[i] = expf(wt[i] - mx);
+                sum += wt[i];
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        const float inv = 1.0f / sum;
+#pragma unroll
+        for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+            if (i < per) {
+                wt[i] *= inv;
+                if (isnan(wt[i])) wt[i] = -FLT_MAX;
+            } else {
+                wt[i] = -INFINITY;
+            }
+        }
+        float wsum = 0.0f, outw = 0.0f;
+        for (int k = 0; k < n_used; ++k) {
+            float bv = wt[0];
+            int be = lane;
+#pragma unroll
+            for (int i = 1; i < MOE_MAX_E / 32; ++i) {
+                if (wt[i] > bv) { bv = wt[i]; be = lane + 32 * i; }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const float v = __shfl_xor_sync(0xffffffffu, bv, off);
+                const int e = __shfl_xor_sync(0xffffffffu, be, off);
+                if (v > bv || (v == bv && e < be)) { bv = v; be = e; }
+            }
+            if ((be & 31) == lane) {
+#pragma unroll
+                for (int i = 0; i < MOE_MAX_E / 32; ++i)
+                    if (i == (be >> 5)) wt[i] = -INFINITY;
+                wsum += bv;
+            }
+            if (k == lane) outw = bv;
+            if (lane == 0) {
+                ids_out[static_cast<int64_t>(t) * n_used + k] = be;
+                ids_s[t * n_used + k] = be;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, off);
+        wsum = fmaxf(wsum, clamp_val);
+        const float invs = 1.0f / wsum;
+        if (lane < n_used) w_out[static_cast<int64_t>(t) * n_used + lane] = outw * invs;
+    }
+    __syncthreads();
+    group_slots(ids_s, T * n_used, E, eoff, slots, act, cnt_s, off_s);
+}
+
+// permute for caller-given ids [T, n_used] (row stride ids_ld); out-of-range
+// ids are flagged in the status word and routed to no expert.
+__global__ void __launch_bounds__(1024) k_group_ids(const int32_t *__restrict__ ids, int64_t ids_ld, int T,
+                                                    int n_used, int E, int32_t *__restrict__ eoff,
+                                                    int32_t *__restrict__ slots, int32_t *__restrict__ act) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    extern __shared__ int32_t sm_i[];
+    int32_t *ids_s = sm_i;
+    int32_t *cnt_s = ids_s + T * n_used;
+    int32_t *off_s = cnt_s + MOE_MAX_E;
+    for (int s = threadIdx.x; s < T * n_used; s += blockDim.x) {
+        int e = ids[static_cast<int64_t>(s / n_used) * ids_ld + s % n_used];
+        if (e < 0 || e >= E) {
+            fr_flag(FR_ST_BADINPUT);
+            e = -1;
+        }
+        ids_s[s] = e;
+    }
+    __syncthreads();
+    group_slots(ids_s, T * n_used, E, eoff, slots, act, cnt_s, off_s);
+}
+
+// ------------------------------------------------------------ grouped matvec
+struct MoeParams {
+    const uint8_t *w0, *w1;     // expert-major rows; w1 = up rows for the SwiGLU pair
+    int64_t e_stride;           // bytes per expert
+    int64_t w_ld;               // bytes per row
+    int N, K;                   // rows per expert, row length
+    const uint8_t *q8;          // q8_1 rows: token rows (bcast) or slot rows
+    int64_t ldq;                // blocks per q8 row
+    int bcast, n_used, E;
+    const int32_t *eoff, *slots, *act;
+    const float *s0, *s1;       // per-expert scales [E] (nullable)
+    float *out;                 // row of slot (t, k): out + t*ld_tok + k*ld_slot
+    int64_t ld_tok, ld_slot;
+    int rows_per_cta, chunks, rows_per_stage, slot_bytes, word_mode;
+};
+
+template <int LG, int TT, bool DUAL>
+__global__ void __launch_bounds__(GV_THREADS) k_moe_gemv(const MoeParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NB = p.K / NV_ELEMS;
+    const int RS = p.rows_per_stage;
+    __shared__ int tok_row[TT];       // q8 row per staged token
+    __shared__ int out_off[TT];       // t*ld_tok + k*ld_slot
+
+    fr_pdl_wait();
+    const int a = blockIdx.x / p.chunks, chunk = blockIdx.x % p.chunks;
+    const int n_act = p.act[p.E];
+    if (a >= n_act) return;
+    const int e = p.act[a];
+    const int s_begin = p.eoff[e], s_end = p.eoff[e + 1];
+    const int r_begin = chunk * p.rows_per_cta;
+    const int n_rows = min(p.N, r_begin + p.rows_per_cta) - r_begin;
+    if (n_rows <= 0 || e < 0 || e >= p.E) return;
+    const int n_st = (n_rows + RS - 1) / RS;
+
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint8_t *ring = smem + 2048;
+    int4 *act_q = reinterpret_cast<int4 *>(ring + static_cast<size_t>(n_st) * p.slot_bytes);
+    float2 *act_d = reinterpret_cast<float2 *>(act_q + static_cast<size_t>(TT) * NB * 4);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < n_st; ++s) mbar_init(&full[s], p.word_mode ? 32 : 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const uint8_t *w0 = p.w0 + static_cast<int64_t>(e) * p.e_stride;
+    const uint8_t *w1 = DUAL ? p.w1 + static_cast<int64_t>(e) * p.e_stride : nullptr;
+
+    if (warp == GV_CWARPS) {
+        // producer: every stage of this chunk into its own slot (no reuse)
+        for (int i = 0; i < n_st; ++i) {
+            const int rows = min(RS, n_rows - i * RS);
+            const int64_t off = static_cast<int64_t>(r_begin + i * RS) * p.w_ld;
+            uint8_t *dst = ring + static_cast<size_t>(i) * p.slot_bytes;
+            if (p.word_mode) {
+                const int wpr = static_cast<int>(p.w_ld / 4);
+                uint32_t *d32 = reinterpret_cast<uint32_t *>(dst);
+                const uint32_t *a0 = reinterpret_cast<const uint32_t *>(w0 + off);
+                for (int k = lane; k < rows * wpr; k += 32) d32[k] = __ldg(a0 + k);
+                if (DUAL) {
+                    const uint32_t *a1 = reinterpret_cast<const uint32_t *>(w1 + off);
+                    for (int k = lane; k < rows * wpr; k += 32) d32[RS * wpr + k] = __ldg(a1 + k);
+                }
+                mbar_arrive(&full[i]);
+            } else if (lane == 0) {
+                const uint32_t bytes = static_cast<uint32_t>(rows * p.w_ld);
+                mbar_expect_tx(&full[i], DUAL ? 2 * bytes : bytes);
+                bulk_g2s(dst, w0 + off, bytes, &full[i]);
+                if (DUAL) bulk_g2s(dst + RS * p.w_ld, w1 + off, bytes, &full[i]);
+            }
+        }
+        return;
+    }
+
+    const float sc0 = p.s0 ? p.s0[e] : 1.0f;
+    const float sc1 = (DUAL && p.s1) ? p.s1[e] : 1.0f;
+    const int g = lane / LG, j = lane % LG;
+    const int nc = p.K / Q8_ELEMS;
+    bool waited = false;
+
+    for (int w0t = s_begin; w0t < s_end; w0t += TT) {
+        const int nt = min(TT, s_end - w0t);
+        if (threadIdx.x < nt) {
+            const int sl = p.slots[w0t + threadIdx.x];
+            const int t = sl / p.n_used, k = sl % p.n_used;
+            tok_row[threadIdx.x] = p.bcast ? t : sl;
+            out_off[threadIdx.x] = static_cast<int>(t * p.ld_tok + k * p.ld_slot);
+        }
+        named_bar(1, GV_CWARPS * 32);
+        // stage the window's activations (gathered rows)
+        {
+            uint8_t *aq = reinterpret_cast<uint8_t *>(act_q);
+            float *ad = reinterpret_cast<float *>(act_d);
+            for (int c = warp; c < nt * nc; c += GV_CWARPS) {
+                const int t = c / nc, ch = c % nc;
+                const uint8_t *blk = p.q8 + (static_cast<int64_t>(tok_row[t]) * p.ldq + ch) * Q8_BYTES;
+                const int8_t q = static_cast<int8_t>(blk[4 + lane]);
+                const int b = ch >> 1;
+                const int s = ((ch & 1) << 1) | (lane >> 4);
+                const int sl = (t * NB + b) * 4 + (s ^ ((b >> 1) & 3));
+                aq[sl * 16 + act_perm(lane & 15)] = static_cast<uint8_t>(q);
+                if (lane == 0) ad[(t * NB + b) * 2 + (ch & 1)] = 0.5f * __low2float(*reinterpret_cast<const __half2 *>(blk));
+            }
+        }
+        named_bar(1, GV_CWARPS * 32);
+        for (int i = warp; i < n_st; i += GV_CWARPS) {
+            if (!waited && !mbar_wait(&full[i], 0, 3)) return;
+            const int rows = min(RS, n_rows - i * RS);
+            const uint8_t *st = ring + static_cast<size_t>(i) * p.slot_bytes;
+            float acc0[TT], acc1[TT];
+#pragma unroll
+            for (int t = 0; t < TT; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
+            if (g < rows) {
+                const uint8_t *row0 = st + static_cast<size_t>(g) * p.w_ld;
+                for (int b = j; b < NB; b += LG) {
+                    gv_block<TT>(reinterpret_cast<const uint32_t *>(row0 + b * NV_BYTES), b, NB, nt, act_q, act_d, acc0);
+                    if (DUAL)
+                        gv_block<TT>(reinterpret_cast<const uint32_t *>(row0 + RS * p.w_ld + b * NV_BYTES), b, NB, nt,
+                                     act_q, act_d, acc1);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+#pragma unroll
+                for (int off = LG / 2; off > 0; off >>= 1) {
+                    acc0[t] += __shfl_xor_sync(0xffffffffu, acc0[t], off);
+                    if (DUAL) acc1[t] += __shfl_xor_sync(0xffffffffu, acc1[t], off);
+                }
+            }
+            if (j == 0 && g < rows) {
+                const int row = r_begin + i * RS + g;
+#pragma unroll
+                for (int t = 0; t < TT; ++t) {
+                    if (t < nt) {
+                        float v;
+                        if (DUAL) {
+                            float result = acc1[t];
+                            result *= sc1;
+                            float gate = acc0[t];
+                            gate *= sc0;
+                            result *= silu_f(gate);
+                            v = result;
+                        } else {
+                            v = acc0[t] * sc0;
+                        }
+                        p.out[static_cast<int64_t>(out_off[t]) + row] = v;
+                    }
+                }
+            }
+        }
+        waited = true;
+        named_bar(1, GV_CWARPS * 32);
+    }
+    fr_pdl_trigger();
+}
+
+// ------------------------------------------------------------ combine
+// out[t, r] = sum_k part[t*n_used + k, r] * w[t, k]  (k ascending) (+ resid)
+__global__ void __launch_bounds__(256) k_moe_combine(const float *__restrict__ part, const float *__restrict__ wts,
+                                                     const float *__restrict__ resid, float *__restrict__ out,
+                                                     int n_used, int n_embd) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    __shared__ float ws[MOE_MAX_USED];
+    const int t = blockIdx.y;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (threadIdx.x < n_used) ws[threadIdx.x] = wts[static_cast<int64_t>(t) * n_used + threadIdx.x];
+    __syncthreads();
+    if (r >= n_embd) return;
+    const float *pt = part + static_cast<int64_t>(t) * n_used * n_embd + r;
+    float sum = pt[0] * ws[0];
+    for (int k = 1; k < n_used; ++k) sum += pt[static_cast<int64_t>(k) * n_embd] * ws[k];
+    if (resid) sum = sum + resid[static_cast<int64_t>(t) * n_embd + r];
+    out[static_cast<int64_t>(t) * n_embd + r] = sum;
+}
+
+} // namespace frb

@@ -57,6 +57,24 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
     return cuda_rc(e);
 }
 
+// Allow `kern` the largest dynamic shared memory the device offers next to
+// its static shared memory (once per device and kernel).
+template <typename K>
+int allow_max_smem(K kern, bool *done_per_dev) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (done_per_dev[dev & 63]) return FR_OK;
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return cuda_rc(e);
+    const DevInfo &di = dev_info();
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             di.smem_optin - static_cast<int>(fa.sharedSizeBytes));
+    if (e != cudaSuccess) return cuda_rc(e);
+    done_per_dev[dev & 63] = true;
+    return FR_OK;
+}
+
 // Grow-only device workspace, one per (device, purpose).  Never shrinks and
 // never moves while large enough, so captured graphs stay valid; refuses to
 // grow while the stream is capturing (the reference's rule,

@@ -1,0 +1,167 @@
+"""Parity of the MoE path (routing, token permute, mul_mat_id, fused MoE FFN)
+against the CPU oracle, through the C-ABI on a B200.
+
+Tolerances: routing ids identical to the oracle's top-k on the same logits
+(lower id wins ties), routing weights within 2e-6 relative, the permute
+identical, matvec outputs within max rel err 1e-3 of the fp64 oracle (as in
+test_gpu_dense.py), q8_1 of the device GLU bit-exact, the combine within 1e-5.
+Stages are checked on the device's own intermediates, as the reference's
+FRT_B_HREF mode does (src/fr_win_flint_batched_moe.cuh:381-475).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-3
+CLAMP = 6.103515625e-5
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _check(mine, ref, O, what=""):
+    mine = np.asarray(mine, np.float64)
+    assert np.all(np.isfinite(mine)), what
+    err = O.rel_err(mine, ref)
+    assert err <= RTOL, f"{what}: max rel err {err:.3e}"
+    assert O.ref_gate_bad(mine, ref) == 0, what
+
+
+@pytest.mark.parametrize("T,E,n_used", [(1, 128, 8), (64, 128, 8), (5, 256, 6), (33, 32, 4), (200, 128, 8)])
+def test_route_topk_and_permute(fr, O, dev, T, E, n_used):
+    import torch
+    K = 2048
+    x = fr.synth_normal(300 + T, T * K).reshape(T, K)
+    wr = fr.synth_normal(301, E * K, 0.0, 0.02).reshape(E, K)
+    logits, ids, wts, eoff, slots, act = fr.moe_route(_t(x, dev), _t(wr, dev), n_used, CLAMP)
+    torch.cuda.synchronize()
+    lg = logits.cpu().numpy()
+    ref_l = O.router_logits(x, wr)
+    assert np.max(np.abs(lg - ref_l)) <= 1e-4 * np.max(np.abs(ref_l)) + 1e-6
+    rid, rw = O.topk_softmax(lg, n_used, CLAMP)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(wts.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    reoff, rslots, ract = O.group_by_expert(rid, E)
+    np.testing.assert_array_equal(eoff.cpu().numpy(), reoff)
+    np.testing.assert_array_equal(slots.cpu().numpy(), rslots)
+    na = int(ract[E])
+    a = act.cpu().numpy()
+    assert a[E] == na
+    np.testing.assert_array_equal(a[:na], ract[:na])
+
+
+def test_route_ties_pick_lower_id(fr, O, dev):
+    import torch
+    T, E, K, n_used = 2, 64, 256, 4
+    x = np.zeros((T, K), np.float32)
+    x[:, 0] = 1.0
+    wr = np.zeros((E, K), np.float32)
+    wr[[3, 17, 40, 41, 60], 0] = 2.0          # five equal logits
+    _, ids, wts, _, _, _ = fr.moe_route(_t(x, dev), _t(wr, dev), n_used, CLAMP)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ids.cpu().numpy(), [[3, 17, 40, 41]] * T)
+    np.testing.assert_allclose(wts.cpu().numpy(), 0.25, rtol=1e-6)
+
+
+def _expert_dot(O, w_all, e, N, K, q8row):
+    rb = K // 64 * 36
+    W = w_all[e * N:(e + 1) * N]
+    return O.gemv_q8_1(W, q8row, N, K)[0]
+
+
+@pytest.mark.parametrize("T,n_used,bcast", [(1, 8, True), (4, 8, False), (16, 6, True), (3, 2, False)])
+def test_mul_mat_id(fr, O, dev, T, n_used, bcast):
+    import torch
+    E, N, K = 32, 256, 768 if not bcast else 2048
+    w = fr.synth_nvfp4(400 + T, E * N, K)
+    rng = np.random.default_rng(T * 10 + n_used)
+    ids = np.stack([rng.choice(E, n_used, replace=False) for _ in range(T)]).astype(np.int32)
+    if bcast:
+        x = fr.synth_normal(401, T * K).reshape(T, K)
+    else:
+        x = fr.synth_normal(402, T * n_used * K).reshape(T, n_used, K)
+    wd = _t(w.reshape(E, N, -1), dev)
+    out = fr.mul_mat_id(wd, E, N, K, _t(x, dev), _t(ids, dev), bcast)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for t in range(T):
+        for k in range(n_used):
+            xr = x[t] if bcast else x[t, k]
+            ref = _expert_dot(O, w, ids[t, k], N, K, O.quantize_q8_1(xr.reshape(1, K)))
+            _check(got[t, k], ref, O, f"t={t} k={k}")
+    assert fr.device_status() == 0
+
+
+def test_mul_mat_id_repeated_expert(fr, O, dev):
+    """An expert used by every token (and twice by one) is still read once and
+    gives each slot its own row."""
+    import torch
+    E, N, K, T, n_used = 8, 128, 512, 12, 3
+    w = fr.synth_nvfp4(410, E * N, K)
+    ids = np.full((T, n_used), 5, np.int32)
+    ids[:, 1] = np.arange(T) % E
+    x = fr.synth_normal(411, T * K).reshape(T, K)
+    out = fr.mul_mat_id(_t(w.reshape(E, N, -1), dev), E, N, K, _t(x, dev), _t(ids, dev), True)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for t in range(T):
+        q = O.quantize_q8_1(x[t].reshape(1, K))
+        for k in range(n_used):
+            _check(got[t, k], _expert_dot(O, w, ids[t, k], N, K, q), O, f"t={t} k={k}")
+
+
+def test_mul_mat_id_bad_ids_flagged(fr, dev):
+    import torch
+    E, N, K, T, n_used = 4, 64, 256, 2, 2
+    w = torch.zeros((E, N, K // 64 * 36), dtype=torch.uint8, device=dev)
+    x = torch.zeros((T, K), dtype=torch.float32, device=dev)
+    ids = torch.tensor([[0, 7], [1, -2]], dtype=torch.int32, device=dev)
+    out = torch.full((T, n_used, N), 3.0, dtype=torch.float32, device=dev)
+    fr.mul_mat_id(w, E, N, K, x, ids, True, out=out)
+    torch.cuda.synchronize()
+    st = fr.device_status()
+    assert st & 0x2
+    o = out.cpu().numpy()
+    assert np.all(o[0, 0] == 0) and np.all(o[1, 0] == 0)      # valid slots computed
+    assert np.all(o[0, 1] == 3.0) and np.all(o[1, 1] == 3.0)  # invalid slots untouched
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_moe_ffn_stagewise(fr, O, dev, T):
+    """Config 3: hidden 2048, 128 experts, FFN 768, top-8 softmax, SiLU-gated."""
+    import torch
+    n_embd, n_ff, E, n_used = 2048, 768, 128, 8
+    wg = fr.synth_nvfp4(501, E * n_ff, n_embd)
+    wu = fr.synth_nvfp4(502, E * n_ff, n_embd)
+    wd = fr.synth_nvfp4(503, E * n_embd, n_ff)
+    wr = fr.synth_normal(504, E * n_embd, 0.0, 0.02).reshape(E, n_embd)
+    x = fr.synth_normal(505 + T, T * n_embd).reshape(T, n_embd)
+    r = fr.synth_normal(506, T * n_embd).reshape(T, n_embd)
+    xd = _t(x, dev)
+    out, chk = fr.moe_ffn(xd, _t(wr, dev), _t(wg, dev), _t(wu, dev), _t(wd, dev), n_embd, n_ff, E, n_used,
+                          resid=_t(r, dev), check=True)
+    _, ids_r, wts_r, _, _, _ = fr.moe_route(xd, _t(wr, dev), n_used, CLAMP)
+    torch.cuda.synchronize()
+    ids = chk["ids"].cpu().numpy()
+    wts = chk["wts"].cpu().numpy()
+    np.testing.assert_array_equal(ids, ids_r.cpu().numpy())
+    np.testing.assert_array_equal(wts, wts_r.cpu().numpy())
+    glu = chk["glu"].cpu().numpy()
+    part = chk["part"].cpu().numpy()
+    o = out.cpu().numpy()
+    tok = sorted({0, T // 2, T - 1})
+    for t in tok:
+        qx = O.quantize_q8_1(x[t].reshape(1, n_embd))
+        for k in range(n_used):
+            e = ids[t, k]
+            g = _expert_dot(O, wg, e, n_ff, n_embd, qx)
+            u = _expert_dot(O, wu, e, n_ff, n_embd, qx)
+            _check(glu[t, k], u * (g / (1.0 + np.exp(-g))), O, f"glu t={t} k={k}")
+            qg = O.quantize_q8_1(glu[t, k].reshape(1, n_ff))
+            _check(part[t, k], _expert_dot(O, wd, e, n_embd, n_ff, qg), O, f"part t={t} k={k}")
+        ref = (part[t].astype(np.float64) * wts[t].astype(np.float64)[:, None]).sum(0) + r[t]
+        np.testing.assert_allclose(o[t], ref, rtol=1e-5, atol=1e-5)
+    assert fr.device_status() == 0
