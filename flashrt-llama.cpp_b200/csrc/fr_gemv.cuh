@@ -54,7 +54,11 @@ __global__ void __launch_bounds__(256) k_quantize_q8_1(const float *__restrict__
 }
 
 // ------------------------------------------------------------ matvec
-constexpr int GV_CWARPS = 8;                        // consumer warps
+constexpr int GV_CWARPS = 8;                        // consumer warps (MoE kernel)
+#ifndef FR_GV_CW
+#define FR_GV_CW 16
+#endif
+constexpr int GV_MAIN_CW = FR_GV_CW;                // consumer warps of the dense matvec
 constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;    // + one producer warp
 
 enum GvEpi : int { GV_PLAIN = 0, GV_SWIGLU = 1 };
@@ -91,28 +95,80 @@ __device__ __forceinline__ int act_perm(int j) {
 // Stage the activation of tokens [t0, t0+nt) into shared memory:
 // act_q: int4 per (token, 64-block, sub-block), swizzled by (b >> 1) & 3;
 // act_d: float2 per (token, 64-block) = 0.5 * f16-rounded q8_1 scales.
+// Loads are batched so that each thread has up to 8 in flight: the staging
+// costs about one L2 round trip per batch instead of one per chunk.
+__device__ __forceinline__ void act_put(uint8_t *aq, float *ad, int NB, int t, int ch, int j, int8_t q) {
+    const int b = ch >> 1;
+    const int s = ((ch & 1) << 1) | (j >> 4);
+    const int slot = (t * NB + b) * 4 + (s ^ ((b >> 1) & 3));
+    aq[slot * 16 + act_perm(j & 15)] = static_cast<uint8_t>(q);
+    (void) ad;
+}
+
+template <int CW>
 __device__ __forceinline__ void gv_stage_act(const GvParams &p, int4 *act_q, float2 *act_d, int warp, int lane) {
     const int nc = p.K / Q8_ELEMS, NB = p.K / NV_ELEMS;
     uint8_t *aq = reinterpret_cast<uint8_t *>(act_q);
     float *ad = reinterpret_cast<float *>(act_d);
-    for (int c = warp; c < p.nt * nc; c += GV_CWARPS) {
-        const int t = c / nc, ch = c % nc;
-        int8_t q;
-        float d;
-        if (p.x != nullptr) {
-            const q8_lane r = q8_1_chunk(p.x[(p.t0 + t) * p.ldx + static_cast<int64_t>(ch) * Q8_ELEMS + lane]);
-            q = r.q;
-            d = __half2float(__float2half_rn(r.d));
-        } else {
-            const uint8_t *blk = p.q8 + ((p.t0 + t) * p.ldq + ch) * Q8_BYTES;
-            q = static_cast<int8_t>(blk[4 + lane]);
-            d = __low2float(*reinterpret_cast<const __half2 *>(blk));
+    constexpr int BATCH = 8;
+    if (p.x != nullptr) {
+        // f32 input: one warp per 32-value chunk (the butterfly needs the warp)
+        const int total = p.nt * nc;
+        for (int base = warp; base < total; base += CW * BATCH) {
+            float v[BATCH];
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u) {
+                const int c = base + CW * u;
+                v[u] = 0.0f;
+                if (c < total) {
+                    const int t = c / nc, ch = c % nc;
+                    v[u] = p.x[(p.t0 + t) * p.ldx + static_cast<int64_t>(ch) * Q8_ELEMS + lane];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u) {
+                const int c = base + CW * u;
+                if (c < total) {
+                    const int t = c / nc, ch = c % nc;
+                    const q8_lane r = q8_1_chunk(v[u]);
+                    act_put(aq, ad, NB, t, ch, lane, r.q);
+                    if (lane == 0) ad[(t * NB + (ch >> 1)) * 2 + (ch & 1)] = 0.5f * __half2float(__float2half_rn(r.d));
+                }
+            }
         }
-        const int b = ch >> 1;
-        const int s = ((ch & 1) << 1) | (lane >> 4);
-        const int slot = (t * NB + b) * 4 + (s ^ ((b >> 1) & 3));
-        aq[slot * 16 + act_perm(lane & 15)] = static_cast<uint8_t>(q);
-        if (lane == 0) ad[(t * NB + b) * 2 + (ch & 1)] = 0.5f * d;
+    } else {
+        // q8_1 input: every consumer thread moves 4-byte words of the blocks
+        const int tid = warp * 32 + lane;
+        const int total = p.nt * nc * 9;
+        for (int base = tid; base < total; base += CW * 32 * BATCH) {
+            uint32_t w[BATCH];
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u) {
+                const int wi = base + CW * 32 * u;
+                w[u] = 0;
+                if (wi < total) {
+                    const int c = wi / 9, k = wi % 9;
+                    const int t = c / nc, ch = c % nc;
+                    w[u] = *reinterpret_cast<const uint32_t *>(p.q8 + ((p.t0 + t) * p.ldq + ch) * Q8_BYTES + 4 * k);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u) {
+                const int wi = base + CW * 32 * u;
+                if (wi < total) {
+                    const int c = wi / 9, k = wi % 9;
+                    const int t = c / nc, ch = c % nc;
+                    if (k == 0) {
+                        const __half2 ds = *reinterpret_cast<const __half2 *>(&w[u]);
+                        ad[(t * NB + (ch >> 1)) * 2 + (ch & 1)] = 0.5f * __low2float(ds);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            act_put(aq, ad, NB, t, ch, 4 * (k - 1) + i, static_cast<int8_t>((w[u] >> (8 * i)) & 0xFF));
+                    }
+                }
+            }
+        }
     }
 }
 
@@ -150,69 +206,118 @@ __device__ __forceinline__ void gv_block(const uint32_t *blk, int b, int NB, int
     }
 }
 
-template <int LG, int TT, int EPI>
-__global__ void __launch_bounds__(GV_THREADS) k_gemv(const GvParams p) {
+// Activation of one 64-block for up to TT tokens, held in registers while
+// the lane walks several weight rows (TT <= 2) -- one shared-memory read of
+// the activation per block instead of one per row.
+template <int TT>
+struct ActBlk {
+    int4 q[TT][4];
+    float2 d[TT];
+};
+
+template <int TT>
+__device__ __forceinline__ void act_load(ActBlk<TT> &a, const int4 *act_q, const float2 *act_d, int b, int NB, int nt) {
+    const int swz = (b >> 1) & 3;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        if (t < nt) {
+#pragma unroll
+            for (int s = 0; s < 4; ++s) a.q[t][s] = act_q[(t * NB + b) * 4 + (s ^ swz)];
+            a.d[t] = act_d[t * NB + b];
+        }
+    }
+}
+
+// dot of one 64-block (9 words at `blk`) with register-held activations
+template <int TT>
+__device__ __forceinline__ void gv_block_reg(const uint32_t *blk, const ActBlk<TT> &a, int nt, float (&acc)[TT]) {
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) w[i] = blk[i];
+    float sc[4];
+    ue4m3x4(w[0], sc);
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const nv_word d0 = nv_decode(w[1 + 2 * s]);
+        const nv_word d1 = nv_decode(w[2 + 2 * s]);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+            if (t < nt) {
+                const int4 q = a.q[t][s];
+                int ip = dp4a(d0.p0, q.x, 0);
+                ip = dp4a(d0.p1, q.y, ip);
+                ip = dp4a(d1.p0, q.z, ip);
+                ip = dp4a(d1.p1, q.w, ip);
+                int in = dp4a(d0.n0, q.x, 0);
+                in = dp4a(d0.n1, q.y, in);
+                in = dp4a(d1.n0, q.z, in);
+                in = dp4a(d1.n1, q.w, in);
+                acc[t] += (sc[s] * (s < 2 ? a.d[t].x : a.d[t].y)) * static_cast<float>(ip - in);
+            }
+        }
+    }
+}
+
+// The matvec.  A stage is SR = 8 warps x (32/LG) lane groups x R2 rows; all
+// eight consumer warps work on every stage (warp w takes rows
+// [(w*(32/LG) + g) * R2, +R2) with lane group g), so each ring slot is waited
+// on by every warp in phase order and freed by eight arrivals.  Stages are
+// 16-74 KB: large enough that one bulk copy per operand keeps HBM busy.
+template <int LG, int TT, int EPI, int R2, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NS = p.n_slots;
     const int NB = p.K / NV_ELEMS;
     constexpr bool DUAL = EPI == GV_SWIGLU;
+    constexpr int GPW = 32 / LG;                         // lane groups per warp
+    constexpr int SR = CW * GPW * R2;             // rows per stage
+    constexpr bool HOLD = TT <= 2;
 
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + NS;
-    uint8_t *ring = smem + 2048;                                    // barriers fit in 2 KB
+    uint8_t *ring = smem + 2048;
     int4 *act_q = reinterpret_cast<int4 *>(ring + static_cast<size_t>(NS) * p.slot_bytes);
     float2 *act_d = reinterpret_cast<float2 *>(act_q + static_cast<size_t>(p.nt) * NB * 4);
 
     const int r_begin = blockIdx.x * p.rows_per_cta;
-    const int r_end = min(p.N, r_begin + p.rows_per_cta);
-    const int n_rows = r_end - r_begin;
-    const int RS = p.rows_per_stage;
-    const int n_st = n_rows > 0 ? (n_rows + RS - 1) / RS : 0;
+    const int n_rows = min(p.N, r_begin + p.rows_per_cta) - r_begin;
+    const int n_st = n_rows > 0 ? (n_rows + SR - 1) / SR : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], p.word_mode ? 32 : 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], CW);
         }
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == GV_CWARPS && p.word_mode) {
-        // ---------------- producer, rows not 16-byte aligned (K % 256 != 0):
-        // the warp copies 4-byte words, then every lane arrives on `full`.
-        const int wpr = static_cast<int>(p.w_ld / 4);
+    if (warp == CW) {
+        // ---------------- producer: stream the CTA's weight rows, before the
+        // PDL wait (weights do not depend on the previous kernel)
+        const int64_t dual_off = static_cast<int64_t>(SR) * p.w_ld;
         for (int i = 0; i < n_st; ++i) {
             const int s = i % NS;
             if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1, 1)) break;
-            const int rows = min(RS, n_rows - i * RS);
-            const int64_t off = static_cast<int64_t>(r_begin + i * RS) * p.w_ld;
-            uint32_t *dst = reinterpret_cast<uint32_t *>(ring + static_cast<size_t>(s) * p.slot_bytes);
-            const uint32_t *src0 = reinterpret_cast<const uint32_t *>(p.w0 + off);
-            for (int k = lane; k < rows * wpr; k += 32) dst[k] = __ldg(src0 + k);
-            if (DUAL) {
-                const uint32_t *src1 = reinterpret_cast<const uint32_t *>(p.w1 + off);
-                for (int k = lane; k < rows * wpr; k += 32) dst[RS * wpr + k] = __ldg(src1 + k);
-            }
-            mbar_arrive(&full[s]);
-        }
-        return;
-    }
-    if (warp == GV_CWARPS) {
-        // ---------------- producer: stream the weight rows
-        if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            for (int i = 0; i < n_st; ++i) {
-                const int s = i % NS;
-                if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1, 1)) break;
-                const int rows = min(RS, n_rows - i * RS);
+            const int rows = min(SR, n_rows - i * SR);
+            const int64_t off = static_cast<int64_t>(r_begin + i * SR) * p.w_ld;
+            uint8_t *dst = ring + static_cast<size_t>(s) * p.slot_bytes;
+            if (p.word_mode) {
+                const int nw = static_cast<int>(rows * p.w_ld / 4);
+                uint32_t *d32 = reinterpret_cast<uint32_t *>(dst);
+                const uint32_t *a0 = reinterpret_cast<const uint32_t *>(p.w0 + off);
+                for (int k = lane; k < nw; k += 32) d32[k] = __ldg(a0 + k);
+                if (DUAL) {
+                    const uint32_t *a1 = reinterpret_cast<const uint32_t *>(p.w1 + off);
+                    for (int k = lane; k < nw; k += 32) d32[dual_off / 4 + k] = __ldg(a1 + k);
+                }
+                mbar_arrive(&full[s]);
+            } else if (lane == 0) {
                 const uint32_t bytes = static_cast<uint32_t>(rows * p.w_ld);
-                const int64_t off = static_cast<int64_t>(r_begin + i * RS) * p.w_ld;
-                uint8_t *dst = ring + static_cast<size_t>(s) * p.slot_bytes;
                 mbar_expect_tx(&full[s], DUAL ? 2 * bytes : bytes);
-                bulk_g2s_hint(dst, p.w0 + off, bytes, &full[s], pol);
-                if (DUAL) bulk_g2s_hint(dst + RS * p.w_ld, p.w1 + off, bytes, &full[s], pol);
+                bulk_g2s(dst, p.w0 + off, bytes, &full[s]);
+                if (DUAL) bulk_g2s(dst + dual_off, p.w1 + off, bytes, &full[s]);
             }
         }
         return;
@@ -220,61 +325,91 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const GvParams p) {
 
     // ---------------- consumers
     fr_pdl_wait();
-    gv_stage_act(p, act_q, act_d, warp, lane);
-    named_bar(1, GV_CWARPS * 32);
+    gv_stage_act<CW>(p, act_q, act_d, warp, lane);
+    named_bar(1, CW * 32);
     fr_pdl_trigger();
 
     const float sc0 = p.s0 ? *p.s0 : 1.0f;
     const float sc1 = (DUAL && p.s1) ? *p.s1 : 1.0f;
     const int g = lane / LG, j = lane % LG;
+    const int rg0 = (warp * GPW + g) * R2;              // first stage row of this lane group
 
-    for (int i = warp; i < n_st; i += GV_CWARPS) {
+    for (int i = 0; i < n_st; ++i) {
         const int s = i % NS;
         if (!mbar_wait(&full[s], (i / NS) & 1, 2)) return;
-        const int rows = min(RS, n_rows - i * RS);
+        const int rows = min(SR, n_rows - i * SR);
         const uint8_t *st = ring + static_cast<size_t>(s) * p.slot_bytes;
-        float acc0[TT], acc1[TT];
+        float acc0[R2][TT], acc1[R2][TT];
 #pragma unroll
-        for (int t = 0; t < TT; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
-        if (g < rows) {
-            const uint8_t *row0 = st + static_cast<size_t>(g) * p.w_ld;
+        for (int r = 0; r < R2; ++r)
+#pragma unroll
+            for (int t = 0; t < TT; ++t) { acc0[r][t] = 0.0f; acc1[r][t] = 0.0f; }
+        if (rg0 < rows) {
+#pragma unroll 2
             for (int b = j; b < NB; b += LG) {
-                gv_block<TT>(reinterpret_cast<const uint32_t *>(row0 + b * NV_BYTES), b, NB, p.nt, act_q, act_d, acc0);
-                if (DUAL)
-                    gv_block<TT>(reinterpret_cast<const uint32_t *>(row0 + RS * p.w_ld + b * NV_BYTES), b, NB,
-                                 p.nt, act_q, act_d, acc1);
-            }
-        }
+                if constexpr (HOLD) {
+                    ActBlk<TT> a;
+                    act_load<TT>(a, act_q, act_d, b, NB, p.nt);
 #pragma unroll
-        for (int t = 0; t < TT; ++t) {
+                    for (int r = 0; r < R2; ++r) {
+                        if (rg0 + r < rows) {
+                            const uint8_t *row = st + static_cast<size_t>(rg0 + r) * p.w_ld + b * NV_BYTES;
+                            gv_block_reg<TT>(reinterpret_cast<const uint32_t *>(row), a, p.nt, acc0[r]);
+                            if (DUAL)
+                                gv_block_reg<TT>(reinterpret_cast<const uint32_t *>(row + SR * p.w_ld), a, p.nt, acc1[r]);
+                        }
+                    }
+                } else {
 #pragma unroll
-            for (int off = LG / 2; off > 0; off >>= 1) {
-                acc0[t] += __shfl_xor_sync(0xffffffffu, acc0[t], off);
-                if (DUAL) acc1[t] += __shfl_xor_sync(0xffffffffu, acc1[t], off);
+                    for (int r = 0; r < R2; ++r) {
+                        if (rg0 + r < rows) {
+                            const uint8_t *row = st + static_cast<size_t>(rg0 + r) * p.w_ld + b * NV_BYTES;
+                            gv_block<TT>(reinterpret_cast<const uint32_t *>(row), b, NB, p.nt, act_q, act_d, acc0[r]);
+                            if (DUAL)
+                                gv_block<TT>(reinterpret_cast<const uint32_t *>(row + SR * p.w_ld), b, NB, p.nt, act_q,
+                                             act_d, acc1[r]);
+                        }
+                    }
+                }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        if (j == 0 && g < rows) {
-            const int row = r_begin + i * RS + g;
+#pragma unroll
+        for (int r = 0; r < R2; ++r)
 #pragma unroll
             for (int t = 0; t < TT; ++t) {
-                if (t < p.nt) {
-                    const int64_t tt = p.t0 + t;
-                    float v;
-                    if (DUAL) {
-                        // fused mmvq epilogue: x = up, gate = gate, SwiGLU
-                        float result = acc1[t];
-                        result *= sc1;
-                        float gate = acc0[t];
-                        gate *= sc0;
-                        result *= silu_f(gate);
-                        v = result;
-                    } else {
-                        v = acc0[t] * sc0;
-                        if (p.resid) v += p.resid[tt * p.ldr + row];
+#pragma unroll
+                for (int off = LG / 2; off > 0; off >>= 1) {
+                    acc0[r][t] += __shfl_xor_sync(0xffffffffu, acc0[r][t], off);
+                    if (DUAL) acc1[r][t] += __shfl_xor_sync(0xffffffffu, acc1[r][t], off);
+                }
+            }
+        if (j == 0) {
+#pragma unroll
+            for (int r = 0; r < R2; ++r) {
+                if (rg0 + r < rows) {
+                    const int row = r_begin + i * SR + rg0 + r;
+#pragma unroll
+                    for (int t = 0; t < TT; ++t) {
+                        if (t < p.nt) {
+                            const int64_t tt = p.t0 + t;
+                            float v;
+                            if (DUAL) {
+                                // fused mmvq epilogue: x = up, gate = gate, SwiGLU
+                                float result = acc1[r][t];
+                                result *= sc1;
+                                float gate = acc0[r][t];
+                                gate *= sc0;
+                                result *= silu_f(gate);
+                                v = result;
+                            } else {
+                                v = acc0[r][t] * sc0;
+                                if (p.resid) v += p.resid[tt * p.ldr + row];
+                            }
+                            p.y[tt * p.ldy + row] = v;
+                        }
                     }
-                    p.y[tt * p.ldy + row] = v;
                 }
             }
         }

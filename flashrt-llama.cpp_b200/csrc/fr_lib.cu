@@ -86,7 +86,7 @@ int workspace_get(int purpose, size_t bytes, cudaStream_t stream, void **out) {
 
 // ------------------------------------------------------------- matvec launcher
 struct GvPlan {
-    int LG, TT, rows_per_stage, rows_per_cta, grid, n_slots, slot_bytes;
+    int LG, TT, R2, SR, rows_per_cta, grid, n_slots, slot_bytes;
     size_t smem;
 };
 
@@ -105,58 +105,65 @@ static int pow2_tokens(int nt) { return nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 
 
 static size_t gv_act_bytes(int nt, int K) { return static_cast<size_t>(nt) * (K / 64) * (64 + 8); }
 
+// One CTA per SM; a stage is 8 warps x (32/LG) lane groups x R2 rows, sized
+// to 16-80 KB so each operand moves in one large bulk copy; the ring holds as
+// many stages as shared memory allows (2..8).
 static GvPlan gv_plan(int N, int K, int64_t w_ld, int T, bool dual) {
     const DevInfo &di = dev_info();
     GvPlan pl{};
     const int NB = K / 64;
     pl.LG = pick_lg(NB);
-    pl.rows_per_stage = 32 / pl.LG;
-    pl.slot_bytes = static_cast<int>((pl.rows_per_stage * w_ld * (dual ? 2 : 1) + 15) / 16 * 16);
-    const int smem_cap = di.smem_optin > 0 ? di.smem_optin : 227 * 1024;
-    // tokens per launch: as many as fit next to a minimal ring
+    const int gpw = 32 / pl.LG;
+    constexpr int CW = GV_MAIN_CW;
+    const int smem_cap = (di.smem_optin > 0 ? di.smem_optin : 227 * 1024) - 1024;
+    const long row_bytes = w_ld * (dual ? 2 : 1);
     int nt = std::min(T, 8);
-    while (nt > 1 && gv_act_bytes(nt, K) + 2048 + static_cast<size_t>(GV_CWARPS) * pl.slot_bytes > static_cast<size_t>(smem_cap) - 4096)
+    while (nt > 1 && gv_act_bytes(nt, K) + 2048 + 2 * static_cast<size_t>(CW * gpw) * row_bytes >
+                         static_cast<size_t>(smem_cap))
         nt = nt / 2;
     pl.TT = pow2_tokens(nt);
-    if (pl.TT > nt) pl.TT = pow2_tokens(nt);
     const size_t act = gv_act_bytes(nt, K);
-    // two CTAs per SM when the ring fits in half the shared memory, else one
-    const int per_sm_budget = (smem_cap - 2048) / 2 - 1024;
-    int ctas_per_sm = 2;
-    long ring_budget = per_sm_budget - 2048 - static_cast<long>(act);
-    if (ring_budget < static_cast<long>(GV_CWARPS) * pl.slot_bytes * 2) {
-        ctas_per_sm = 1;
-        ring_budget = smem_cap - 4096 - static_cast<long>(act);
+    pl.R2 = 1;
+    if (pl.TT <= 2) {
+        for (int r2 : {4, 2}) {
+            const long st = static_cast<long>(CW) * gpw * r2 * row_bytes;
+            if (st <= 80 * 1024 && 2 * st + 2048 + static_cast<long>(act) <= smem_cap) { pl.R2 = r2; break; }
+        }
     }
-    int depth = static_cast<int>(ring_budget / (static_cast<long>(GV_CWARPS) * pl.slot_bytes));
-    depth = std::max(1, std::min(depth, 6));
-    pl.n_slots = GV_CWARPS * depth;
-    const int stages = (N + pl.rows_per_stage - 1) / pl.rows_per_stage;
-    const int max_grid = std::max(1, di.sms * ctas_per_sm);
-    const int st_per_cta = (stages + max_grid - 1) / max_grid;
-    pl.rows_per_cta = st_per_cta * pl.rows_per_stage;
+    pl.SR = CW * gpw * pl.R2;
+    pl.slot_bytes = static_cast<int>((pl.SR * row_bytes + 15) / 16 * 16);
+    const long budget = smem_cap - 2048 - static_cast<long>(act);
+    pl.n_slots = static_cast<int>(std::max(1L, std::min(8L, budget / pl.slot_bytes)));
+    const int sms = std::max(1, di.sms);
+    pl.rows_per_cta = (N + sms - 1) / sms;
     pl.grid = (N + pl.rows_per_cta - 1) / pl.rows_per_cta;
     pl.smem = 2048 + static_cast<size_t>(pl.n_slots) * pl.slot_bytes + act;
     return pl;
 }
 
-template <int LG, int TT, int EPI>
+template <int LG, int TT, int EPI, int R2>
 static int gv_launch_inst(const GvParams &p, const GvPlan &pl, cudaStream_t stream) {
-    auto kern = k_gemv<LG, TT, EPI>;
+    auto kern = k_gemv<LG, TT, EPI, R2, GV_MAIN_CW>;
     static bool attr_done[64] = {};
     const int arc = allow_max_smem(kern, attr_done);
     if (arc != FR_OK) return arc;
-    return launch_pdl(kern, dim3(pl.grid), dim3(GV_THREADS), pl.smem, stream, p);
+    return launch_pdl(kern, dim3(pl.grid), dim3((GV_MAIN_CW + 1) * 32), pl.smem, stream, p);
 }
 
 template <int LG, int EPI>
 static int gv_launch_tt(const GvParams &p, const GvPlan &pl, cudaStream_t stream) {
-    switch (pl.TT) {
-    case 1: return gv_launch_inst<LG, 1, EPI>(p, pl, stream);
-    case 2: return gv_launch_inst<LG, 2, EPI>(p, pl, stream);
-    case 4: return gv_launch_inst<LG, 4, EPI>(p, pl, stream);
-    default: return gv_launch_inst<LG, 8, EPI>(p, pl, stream);
+    if (pl.TT == 1) {
+        if (pl.R2 == 4) return gv_launch_inst<LG, 1, EPI, 4>(p, pl, stream);
+        if (pl.R2 == 2) return gv_launch_inst<LG, 1, EPI, 2>(p, pl, stream);
+        return gv_launch_inst<LG, 1, EPI, 1>(p, pl, stream);
     }
+    if (pl.TT == 2) {
+        if (pl.R2 == 4) return gv_launch_inst<LG, 2, EPI, 4>(p, pl, stream);
+        if (pl.R2 == 2) return gv_launch_inst<LG, 2, EPI, 2>(p, pl, stream);
+        return gv_launch_inst<LG, 2, EPI, 1>(p, pl, stream);
+    }
+    if (pl.TT == 4) return gv_launch_inst<LG, 4, EPI, 1>(p, pl, stream);
+    return gv_launch_inst<LG, 8, EPI, 1>(p, pl, stream);
 }
 
 template <int EPI>
@@ -173,7 +180,7 @@ static int gv_launch_lg(const GvParams &p, const GvPlan &pl, cudaStream_t stream
 static int gemv_run(GvParams p, int T, bool dual, cudaStream_t stream) {
     const GvPlan pl = gv_plan(p.N, p.K, p.w_ld, T, dual);
     p.rows_per_cta = pl.rows_per_cta;
-    p.rows_per_stage = pl.rows_per_stage;
+    p.rows_per_stage = pl.SR;
     p.n_slots = pl.n_slots;
     p.slot_bytes = pl.slot_bytes;
     p.word_mode = (p.w_ld % 16 != 0 || (reinterpret_cast<uintptr_t>(p.w0) & 15) ||
@@ -359,21 +366,18 @@ int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
     const int64_t ld_gu = static_cast<int64_t>(n_embd) / 64 * NV_BYTES;
     const int64_t ld_d = static_cast<int64_t>(n_ff) / 64 * NV_BYTES;
     int rc;
-    void *q8x = nullptr;
     float *glu = chk_glu;
-    void *gq8 = chk_glu_q8;
-    rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES, stream, &q8x);
-    if (rc != FR_OK) return rc;
     if (!glu) {
         void *p = nullptr;
         rc = workspace_get(WS_GLU, static_cast<size_t>(T) * n_ff * sizeof(float), stream, &p);
         if (rc != FR_OK) return rc;
         glu = static_cast<float *>(p);
     }
-    if (!gq8) {
-        rc = workspace_get(WS_GLUQ8, static_cast<size_t>(T) * (n_ff / 32) * Q8_BYTES, stream, &gq8);
-        if (rc != FR_OK) return rc;
-    }
+    // q8_1(x) in its own small kernel: under PDL it overlaps the start of the
+    // gate/up weight stream, which a quantizing prologue would delay
+    void *q8x = nullptr;
+    rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES, stream, &q8x);
+    if (rc != FR_OK) return rc;
     rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
     if (rc != FR_OK) return rc;
     GvParams p{};
@@ -390,6 +394,12 @@ int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
     p.K = n_embd;
     rc = gemv_run(p, T, true, stream);
     if (rc != FR_OK) return rc;
+    // q8_1 of the GLU, likewise a separate kernel overlapped by PDL
+    void *gq8 = chk_glu_q8;
+    if (!gq8) {
+        rc = workspace_get(WS_GLUQ8, static_cast<size_t>(T) * (n_ff / 32) * Q8_BYTES, stream, &gq8);
+        if (rc != FR_OK) return rc;
+    }
     rc = quantize_launch(glu, n_ff, gq8, n_ff / 32, T, n_ff, stream);
     if (rc != FR_OK) return rc;
     GvParams q{};
