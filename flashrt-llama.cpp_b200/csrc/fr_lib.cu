@@ -10,12 +10,27 @@
 #include "fr_gemv.cuh"
 #include "fr_moe.cuh"
 #include "fr_w4a4.cuh"
+#include "fr_tcgemv.cuh"
 
 #include <cudaTypedefs.h>
 
 namespace frb {
 
 std::atomic<uint64_t> g_launches{0};
+
+static bool tc_shape_ok(const void *w0, const void *w1, int64_t w_ld, int K);
+static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, int K, const float *x, int64_t ldx,
+                     const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
+                     int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream);
+// Tensor-core kernel for batches (T >= 3: it costs the same for T = 1..64),
+// dp4a kernel for T <= 2 and for shapes the TMA path cannot take; the path
+// can be forced either way.
+static bool use_tc(const void *w0, const void *w1, int64_t w_ld, int K, int T) {
+    const int path = matvec_path();
+    if (path == 1) return false;
+    if (path == 0 && T <= 2) return false;
+    return tc_shape_ok(w0, w1, w_ld, K);
+}
 
 // ------------------------------------------------------------- device info
 const DevInfo &dev_info() {
@@ -82,6 +97,48 @@ int workspace_get(int purpose, size_t bytes, cudaStream_t stream, void **out) {
     }
     *out = w.ptr;
     return FR_OK;
+}
+
+int workspace_get_zeroed(int purpose, size_t bytes, cudaStream_t stream, void **out) {
+    // its own grow-only buffers, cleared on every (re)allocation
+    static Workspace ws[64][WS_COUNT];
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || purpose < 0 || purpose >= WS_COUNT) return FR_EINVAL;
+    std::lock_guard<std::mutex> lk(mu);
+    Workspace &w = ws[dev][purpose];
+    if (w.cap < bytes) {
+        if (stream_capturing(stream)) return FR_ECAPTURE;
+        if (w.ptr) {
+            cudaError_t e = cudaStreamSynchronize(stream);
+            if (e != cudaSuccess) return cuda_rc(e);
+            cudaFree(w.ptr);
+            w.ptr = nullptr;
+            w.cap = 0;
+        }
+        const size_t cap = std::max<size_t>(bytes, 1 << 20);
+        cudaError_t e = cudaMalloc(&w.ptr, cap);
+        if (e != cudaSuccess) { w.ptr = nullptr; return cuda_rc(e); }
+        e = cudaMemsetAsync(w.ptr, 0, cap, stream);
+        if (e != cudaSuccess) return cuda_rc(e);
+        w.cap = cap;
+    }
+    *out = w.ptr;
+    return FR_OK;
+}
+
+static std::atomic<int> g_matvec_path{-1};
+int matvec_path() {
+    int v = g_matvec_path.load();
+    if (v < 0) {
+        const char *e = getenv("FR_MATVEC");
+        v = 0;
+        if (e && std::string(e) == "dp4a") v = 1;
+        if (e && std::string(e) == "tc") v = 2;
+        g_matvec_path.store(v);
+    }
+    return v;
 }
 
 // ------------------------------------------------------------- matvec launcher
@@ -267,6 +324,13 @@ int fr_fault_inject(const char *site) {
 
 uint64_t fr_kernel_launches(void) { return g_launches.load(); }
 
+int fr_set_matvec_path(int path) {
+    if (path < 0 || path > 2) return FR_EINVAL;
+    const int prev = matvec_path();
+    g_matvec_path.store(path);
+    return prev;
+}
+
 int64_t fr_nvfp4_row_bytes(int64_t K) { return K / 64 * NV_BYTES; }
 int64_t fr_q8_1_row_bytes(int64_t K) { return K / 32 * Q8_BYTES; }
 
@@ -283,6 +347,9 @@ int fr_gemv_nvfp4_q8_1(const void *w, int64_t w_ld, const void *q8, int64_t ldq,
     int rc = check_gemv_shape(w, w_ld, N, K, T);
     if (rc != FR_OK) return rc;
     if (!q8 || !y || ldq < K / 32 || ldy < N || (resid && ldr < N)) return FR_EINVAL;
+    if (use_tc(w, nullptr, w_ld, K, T))
+        return tc_matvec(static_cast<const uint8_t *>(w), nullptr, w_ld, N, K, nullptr, 0,
+                         static_cast<const uint8_t *>(q8), ldq, T, scale, nullptr, resid, ldr, y, ldy, false, stream);
     GvParams p{};
     p.w0 = static_cast<const uint8_t *>(w);
     p.w_ld = w_ld;
@@ -305,6 +372,9 @@ int fr_gemv_nvfp4_f32(const void *w, int64_t w_ld, const float *x, int64_t ldx, 
     int rc = check_gemv_shape(w, w_ld, N, K, T);
     if (rc != FR_OK) return rc;
     if (!x || !y || ldx < K || ldy < N || (resid && ldr < N)) return FR_EINVAL;
+    if (use_tc(w, nullptr, w_ld, K, T))
+        return tc_matvec(static_cast<const uint8_t *>(w), nullptr, w_ld, N, K, x, ldx, nullptr, 0, T, scale, nullptr,
+                         resid, ldr, y, ldy, false, stream);
     GvParams p{};
     p.w0 = static_cast<const uint8_t *>(w);
     p.w_ld = w_ld;
@@ -327,6 +397,9 @@ int fr_gemv_nvfp4_q8_1_swiglu(const void *wg, const void *wu, int64_t w_ld, cons
     int rc = check_gemv_shape(wg, w_ld, N, K, T);
     if (rc != FR_OK) return rc;
     if (!wu || (reinterpret_cast<uintptr_t>(wu) & 3) || !q8 || !y || ldq < K / 32 || ldy < N) return FR_EINVAL;
+    if (use_tc(wg, wu, w_ld, K, T))
+        return tc_matvec(static_cast<const uint8_t *>(wg), static_cast<const uint8_t *>(wu), w_ld, N, K, nullptr, 0,
+                         static_cast<const uint8_t *>(q8), ldq, T, sg, su, nullptr, 0, y, ldy, true, stream);
     GvParams p{};
     p.w0 = static_cast<const uint8_t *>(wg);
     p.w1 = static_cast<const uint8_t *>(wu);
@@ -348,6 +421,9 @@ int fr_mul_mat_nvfp4(const void *src0, int64_t nb01, const float *src1, int64_t 
     int rc = check_gemv_shape(src0, nb01, N, K, T);
     if (rc != FR_OK) return rc;
     if (!src1 || !dst || ld1 < K || ldd < N) return FR_EINVAL;
+    if (use_tc(src0, nullptr, nb01, K, T))
+        return tc_matvec(static_cast<const uint8_t *>(src0), nullptr, nb01, N, K, src1, ld1, nullptr, 0, T, nullptr,
+                         nullptr, nullptr, 0, dst, ldd, false, stream);
     if (T <= 2) return fr_gemv_nvfp4_f32(src0, nb01, src1, ld1, nullptr, nullptr, 0, dst, ldd, N, K, T, stream);
     void *q8 = nullptr;
     rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (K / 32) * Q8_BYTES, stream, &q8);
@@ -372,6 +448,19 @@ int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
         rc = workspace_get(WS_GLU, static_cast<size_t>(T) * n_ff * sizeof(float), stream, &p);
         if (rc != FR_OK) return rc;
         glu = static_cast<float *>(p);
+    }
+    if (use_tc(wg, wu, ld_gu, n_embd, T) && use_tc(wd, nullptr, ld_d, n_ff, T)) {
+        // tensor-core path: the hi/lo activation kernels quantize x and the GLU
+        // to q8_1 on the way (no q8_1 blocks needed)
+        rc = tc_matvec(static_cast<const uint8_t *>(wg), static_cast<const uint8_t *>(wu), ld_gu, n_ff, n_embd, x,
+                       n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, n_ff, true, stream);
+        if (rc != FR_OK) return rc;
+        if (chk_glu_q8) {
+            rc = quantize_launch(glu, n_ff, chk_glu_q8, n_ff / 32, T, n_ff, stream);
+            if (rc != FR_OK) return rc;
+        }
+        return tc_matvec(static_cast<const uint8_t *>(wd), nullptr, ld_d, n_embd, n_ff, glu, n_ff, nullptr, 0, T, sd,
+                         nullptr, resid, n_embd, out, n_embd, false, stream);
     }
     // q8_1(x) in its own small kernel: under PDL it overlaps the start of the
     // gate/up weight stream, which a quantizing prologue would delay
@@ -851,3 +940,138 @@ int fr_gemm_f32out(const void *A_packed, const void *SFA, const void *B_packed, 
 }
 
 } // extern "C"
+
+// ======================================================================
+// Tensor-core matvec (k_tcgemv) host side, and the dispatch between it and
+// the dp4a kernel
+// ======================================================================
+namespace frb {
+
+// TMA map of block_nvfp4 rows: [N rows, K/64*36 bytes], box 144 B x R rows
+static int make_map_wrows(CUtensorMap *map, const void *base, int N, int K, int64_t w_ld, int R) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return FR_ENODEVICE;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 64 * NV_BYTES), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(w_ld)};
+    cuuint32_t box[2] = {TG_WBOX, static_cast<cuuint32_t>(R)};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
+}
+
+// TMA map of the hi/lo activation: f16 [NP rows, Kp], box 64 x NP, 128 B swizzle
+static int make_map_act(CUtensorMap *map, const void *base, int NP, int Kp) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return FR_ENODEVICE;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(NP)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(Kp) * 2};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(NP)};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
+}
+
+static bool tc_shape_ok(const void *w0, const void *w1, int64_t w_ld, int K) {
+    if (K % 256 != 0 || w_ld % 16 != 0) return false;
+    if (reinterpret_cast<uintptr_t>(w0) & 15) return false;
+    if (w1 && (reinterpret_cast<uintptr_t>(w1) & 15)) return false;
+    const DevInfo &di = dev_info();
+    return di.cc_major == 10;
+}
+
+template <int NP, int EPI>
+static int tc_launch(const CUtensorMap &m0, const CUtensorMap &m1, const CUtensorMap &mb, TgArgs a, int grid,
+                     cudaStream_t stream) {
+    constexpr int NM = EPI == TG_SWIGLU ? 2 : 1;
+    constexpr int STAGE = NM * TG_WBYTES + 4 * NP * 128;
+    auto kern = k_tcgemv<NP, EPI>;
+    static bool attr_done[64] = {};
+    int rc = allow_max_smem(kern, attr_done);
+    if (rc != FR_OK) return rc;
+    const int cap = dev_info().smem_optin - 2048;
+    a.n_stages = std::max(1, std::min(4, cap / STAGE));
+    const size_t smem = 1024 + static_cast<size_t>(a.n_stages) * STAGE + 256;
+    return launch_pdl(kern, dim3(grid), dim3(TG_THREADS), smem, stream, m0, m1, mb, a);
+}
+
+// y[t] = W . x_q[t] (PLAIN) or SwiGLU(Wg . x_q[t], Wu . x_q[t]) for T tokens,
+// activations given as f32 rows (x) or q8_1 blocks (q8).
+static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, int K, const float *x, int64_t ldx,
+                     const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
+                     int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream) {
+    const DevInfo &di = dev_info();
+    const int G = std::max(1, di.sms);
+    const int NP = T <= 8 ? 16 : T <= 16 ? 32 : T <= 32 ? 64 : 128;
+    const int TW = NP / 2;
+    const int Kp = (K + 255) / 256 * 256;
+    const int n_kt = Kp / 256;
+    int ksplit = std::max(1, std::min(n_kt, (128 * G) / std::max(1, N)));
+    const int kt_per = (n_kt + ksplit - 1) / ksplit;
+    ksplit = (n_kt + kt_per - 1) / kt_per;
+    const int R = std::min(128, std::max(1, static_cast<int>((static_cast<int64_t>(N) * ksplit + G - 1) / G)));
+    const int n_rt = (N + R - 1) / R;
+
+    void *actp = nullptr;
+    int rc = workspace_get(WS_ACT, static_cast<size_t>(NP) * Kp * 2, stream, &actp);
+    if (rc != FR_OK) return rc;
+    // counters live at a fixed place (the first TG_MAX_COUNTERS words, zero
+    // after allocation and reset by every last split), partials after them
+    constexpr size_t TG_MAX_COUNTERS = 1 << 16;
+    if (static_cast<size_t>(n_rt) * 4 > TG_MAX_COUNTERS) return FR_EINVAL;
+    const size_t part_floats = static_cast<size_t>(n_rt) * ksplit * 2 * TW * 128;
+    const size_t part_off = TG_MAX_COUNTERS * 4;
+    void *wsp = nullptr;
+    rc = workspace_get_zeroed(WS_TGPART, part_off + part_floats * 4, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    void *partp = static_cast<uint8_t *>(wsp) + part_off;
+
+    CUtensorMap m0, m1, mb;
+    rc = make_map_wrows(&m0, w0, N, K, w_ld, R);
+    if (rc != FR_OK) return rc;
+    rc = make_map_wrows(&m1, dual ? w1 : w0, N, K, w_ld, R);
+    if (rc != FR_OK) return rc;
+    rc = make_map_act(&mb, actp, NP, Kp);
+    if (rc != FR_OK) return rc;
+
+    TgArgs a{};
+    a.N = N;
+    a.K = K;
+    a.R = R;
+    a.n_kt = n_kt;
+    a.ksplit = ksplit;
+    a.kt_per_split = kt_per;
+    a.s0 = s0;
+    a.s1 = s1;
+    a.resid = resid;
+    a.ldr = ldr;
+    a.y = y;
+    a.ldy = ldy;
+    a.part = static_cast<float *>(partp);
+    a.counter = static_cast<unsigned int *>(wsp);
+    for (int t0 = 0; t0 < T; t0 += TW) {
+        const int tw = std::min(TW, T - t0);
+        const int64_t chunks = static_cast<int64_t>(TW) * (Kp / 32);
+        rc = launch_pdl(k_act_hilo, dim3(static_cast<unsigned>((chunks + 7) / 8)), dim3(256), 0, stream,
+                        x ? x + t0 * ldx : static_cast<const float *>(nullptr), ldx,
+                        q8 ? q8 + t0 * ldq * Q8_BYTES : static_cast<const uint8_t *>(nullptr), ldq, tw, K, Kp, NP,
+                        static_cast<__half *>(actp));
+        if (rc != FR_OK) return rc;
+        a.T = tw;
+        a.t0 = t0;
+        const int grid = n_rt * ksplit;
+        switch (NP) {
+        case 16: rc = dual ? tc_launch<16, TG_SWIGLU>(m0, m1, mb, a, grid, stream) : tc_launch<16, TG_PLAIN>(m0, m1, mb, a, grid, stream); break;
+        case 32: rc = dual ? tc_launch<32, TG_SWIGLU>(m0, m1, mb, a, grid, stream) : tc_launch<32, TG_PLAIN>(m0, m1, mb, a, grid, stream); break;
+        case 64: rc = dual ? tc_launch<64, TG_SWIGLU>(m0, m1, mb, a, grid, stream) : tc_launch<64, TG_PLAIN>(m0, m1, mb, a, grid, stream); break;
+        default: rc = dual ? tc_launch<128, TG_SWIGLU>(m0, m1, mb, a, grid, stream) : tc_launch<128, TG_PLAIN>(m0, m1, mb, a, grid, stream); break;
+        }
+        if (rc != FR_OK) return rc;
+    }
+    return FR_OK;
+}
+
+} // namespace frb

@@ -85,6 +85,16 @@ struct Workspace {
 };
 int workspace_get(int purpose, size_t bytes, cudaStream_t stream, void **out);
 
-enum WsPurpose : int { WS_Q8 = 0, WS_GLU = 1, WS_GLUQ8 = 2, WS_MOE = 3, WS_COUNT = 8 };
+enum WsPurpose : int { WS_Q8 = 0, WS_GLU = 1, WS_GLUQ8 = 2, WS_MOE = 3, WS_ACT = 4, WS_TGPART = 5, WS_ACT2 = 6,
+                       WS_COUNT = 8 };
+
+// Same, but the buffer is zero-filled whenever it is (re)allocated (for
+// counters that kernels keep at zero between calls).
+int workspace_get_zeroed(int purpose, size_t bytes, cudaStream_t stream, void **out);
+
+// Matvec implementation choice: 0 = by shape, 1 = dp4a kernel, 2 = tensor-core
+// kernel.  Read once from FR_MATVEC (auto | dp4a | tc); fr_set_matvec_path
+// overrides it.
+int matvec_path();
 
 } // namespace frb

@@ -45,6 +45,7 @@ SIGNATURES = {
     "fr_device_status": (_i32, [C.POINTER(C.c_uint32), _i32]),
     "fr_fault_inject": (_i32, [C.c_char_p]),
     "fr_kernel_launches": (C.c_uint64, []),
+    "fr_set_matvec_path": (_i32, [_i32]),
     "fr_nvfp4_row_bytes": (_i64, [_i64]),
     "fr_q8_1_row_bytes": (_i64, [_i64]),
     "fr_quantize_q8_1": (_i32, [_vp, _i64, _vp, _i64, _i32, _i32, _vp]),
@@ -126,6 +127,11 @@ def synth_normal(seed: int, n: int, mean: float = 0.0, std: float = 1.0):
     out = np.empty(n, np.float32)
     lib().fr_synth_normal(seed, n, mean, std, out.ctypes.data)
     return out
+
+
+def set_matvec_path(path: int) -> int:
+    """0 = by shape, 1 = dp4a kernel, 2 = tensor-core kernel; returns the previous."""
+    return int(lib().fr_set_matvec_path(path))
 
 
 def device_status(clear: bool = True) -> int:

@@ -57,6 +57,13 @@ int fr_fault_inject(const char *site);
 /* Number of kernels this library has launched in this process. */
 uint64_t fr_kernel_launches(void);
 
+/* Matvec kernel selection (config knob, like the reference's FRT_* switches):
+ * 0 = by shape (tensor-core kernel when K % 256 == 0 and rows are 16-byte
+ * aligned, else the dp4a kernel), 1 = dp4a kernel, 2 = tensor-core kernel
+ * where the shape allows.  Initialised once from FR_MATVEC=auto|dp4a|tc.
+ * Returns the previous setting, or -1 for an invalid argument. */
+int fr_set_matvec_path(int path);
+
 /* ------------------------------------------------------------------ sizes */
 int64_t fr_nvfp4_row_bytes(int64_t K);   /* K/64 * 36 */
 int64_t fr_q8_1_row_bytes(int64_t K);    /* K/32 * 36 */

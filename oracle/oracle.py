@@ -204,8 +204,10 @@ def gemm_f32out(A, SFA, B, SFB, M, N, K, alpha=1.0, nthreads=0):
 
 # ------------------------------------------------------------ comparisons
 
-def rel_err(mine: np.ndarray, ref: np.ndarray, floor_frac: float = 1e-3) -> float:
-    """max |mine - ref| / max(|ref|, floor_frac * rms(ref))."""
+def rel_err(mine: np.ndarray, ref: np.ndarray, floor_frac: float = 1e-2) -> float:
+    """max |mine - ref| / max(|ref|, floor_frac * rms(ref)): the relative error,
+    with outputs smaller than 1% of the rms judged against 1% of the rms (a
+    relative error of a value near zero measures cancellation, not the kernel)."""
     mine = np.asarray(mine, np.float64)
     ref = np.asarray(ref, np.float64)
     if not np.all(np.isfinite(mine)):
@@ -213,6 +215,14 @@ def rel_err(mine: np.ndarray, ref: np.ndarray, floor_frac: float = 1e-3) -> floa
     rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
     den = np.maximum(np.abs(ref), floor_frac * rms + 1e-30)
     return float(np.max(np.abs(mine - ref) / den)) if ref.size else 0.0
+
+
+def norm_err(mine, ref) -> float:
+    """||mine - ref||_2 / ||ref||_2."""
+    mine = np.asarray(mine, np.float64)
+    ref = np.asarray(ref, np.float64)
+    den = float(np.linalg.norm(ref))
+    return float(np.linalg.norm(mine - ref)) / den if den > 0 else float(np.linalg.norm(mine))
 
 
 def ref_gate_bad(mine, ref, atol=1e-4, rtol=2e-3) -> int:

@@ -13,7 +13,8 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-RTOL = 1e-3
+RTOL = 1e-3      # max |d| / max(|ref|, 1% rms(ref))
+NTOL = 1e-5      # ||d|| / ||ref||
 CLAMP = 6.103515625e-5
 
 
@@ -27,6 +28,7 @@ def _check(mine, ref, O, what=""):
     assert np.all(np.isfinite(mine)), what
     err = O.rel_err(mine, ref)
     assert err <= RTOL, f"{what}: max rel err {err:.3e}"
+    assert O.norm_err(mine, ref) <= NTOL, what
     assert O.ref_gate_bad(mine, ref) == 0, what
 
 

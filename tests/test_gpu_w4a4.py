@@ -8,7 +8,8 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-RTOL = 1e-3
+RTOL = 1e-3      # max |d| / max(|ref|, 1% rms(ref))
+NTOL = 1e-5      # ||d|| / ||ref||
 E2M1 = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], np.float64)
 
 
@@ -44,6 +45,7 @@ def _check(mine, ref, O, what):
     assert np.all(np.isfinite(mine)), what
     err = O.rel_err(mine, ref)
     assert err <= RTOL, f"{what}: max rel err {err:.3e}"
+    assert O.norm_err(mine, ref) <= NTOL, what
 
 
 @pytest.mark.parametrize("M,K", [(1, 64), (3, 48), (130, 4096), (512, 14336), (7, 960)])
