@@ -1075,3 +1075,106 @@ static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, 
 }
 
 } // namespace frb
+
+// ======================================================================
+// Expert-parallel building blocks: expert FFN over pre-routed rows, combine
+// ======================================================================
+extern "C" {
+
+int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S, const void *wg, const void *wu,
+                         const void *wd, const float *sg, const float *su, const float *sd, float *out, int64_t ldo,
+                         int n_embd, int n_ff, int E, cudaStream_t stream) {
+    if (fault_hit("fr_moe_experts_nvfp4")) return FR_EINJECTED;
+    if (S < 0 || E <= 0 || E > MOE_MAX_E || n_embd <= 0 || n_ff <= 0) return FR_EINVAL;
+    if (S == 0) return FR_OK;
+    if (!x || !eid || !wg || !wu || !wd || !out || n_embd % 64 != 0 || n_ff % 64 != 0) return FR_EINVAL;
+    if (ldx < n_embd || ldo < n_embd || S > MOE_MAX_SLOTS) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(wg) & 3) || (reinterpret_cast<uintptr_t>(wu) & 3) ||
+        (reinterpret_cast<uintptr_t>(wd) & 3))
+        return FR_EINVAL;
+    const int64_t ld_gu = static_cast<int64_t>(n_embd) / 64 * NV_BYTES;
+    const int64_t ld_d = static_cast<int64_t>(n_ff) / 64 * NV_BYTES;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_eoff = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_act = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_slots = take(static_cast<size_t>(S) * 4);
+    const size_t o_q8x = take(static_cast<size_t>(S) * (n_embd / 32) * Q8_BYTES);
+    const size_t o_glu = take(static_cast<size_t>(S) * n_ff * 4);
+    const size_t o_q8g = take(static_cast<size_t>(S) * (n_ff / 32) * Q8_BYTES);
+    void *wsp = nullptr;
+    int rc = workspace_get(WS_MOE, off, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    uint8_t *base = static_cast<uint8_t *>(wsp);
+    int32_t *eoff = reinterpret_cast<int32_t *>(base + o_eoff);
+    int32_t *act = reinterpret_cast<int32_t *>(base + o_act);
+    int32_t *slots = reinterpret_cast<int32_t *>(base + o_slots);
+    uint8_t *q8x = base + o_q8x;
+    float *glu = reinterpret_cast<float *>(base + o_glu);
+    uint8_t *q8g = base + o_q8g;
+    static bool attr_done[64] = {};
+    rc = allow_max_smem(k_group_ids, attr_done);
+    if (rc != FR_OK) return rc;
+    // each row is one "token" with one slot
+    rc = launch_pdl(k_group_ids, dim3(1), dim3(1024), group_smem(S, 1), stream, eid, static_cast<int64_t>(1), S, 1, E,
+                    eoff, slots, act);
+    if (rc != FR_OK) return rc;
+    rc = quantize_launch(x, ldx, q8x, n_embd / 32, S, n_embd, stream);
+    if (rc != FR_OK) return rc;
+    MoeParams p{};
+    p.w0 = static_cast<const uint8_t *>(wg);
+    p.w1 = static_cast<const uint8_t *>(wu);
+    p.e_stride = ld_gu * n_ff;
+    p.w_ld = ld_gu;
+    p.N = n_ff;
+    p.K = n_embd;
+    p.q8 = q8x;
+    p.ldq = n_embd / 32;
+    p.bcast = 1;
+    p.n_used = 1;
+    p.E = E;
+    p.eoff = eoff;
+    p.slots = slots;
+    p.act = act;
+    p.s0 = sg;
+    p.s1 = su;
+    p.out = glu;
+    p.ld_tok = n_ff;
+    p.ld_slot = 0;
+    const int max_active = std::min(E, S);
+    rc = moe_launch<true>(p, max_active, S, stream);
+    if (rc != FR_OK) return rc;
+    rc = quantize_launch(glu, n_ff, q8g, n_ff / 32, S, n_ff, stream);
+    if (rc != FR_OK) return rc;
+    MoeParams q{};
+    q.w0 = static_cast<const uint8_t *>(wd);
+    q.e_stride = ld_d * n_embd;
+    q.w_ld = ld_d;
+    q.N = n_embd;
+    q.K = n_ff;
+    q.q8 = q8g;
+    q.ldq = n_ff / 32;
+    q.bcast = 1;
+    q.n_used = 1;
+    q.E = E;
+    q.eoff = eoff;
+    q.slots = slots;
+    q.act = act;
+    q.s0 = sd;
+    q.out = out;
+    q.ld_tok = ldo;
+    q.ld_slot = 0;
+    return moe_launch<false>(q, max_active, S, stream);
+}
+
+int fr_moe_combine(const float *part, const float *wts, const float *resid, float *out, int T, int n_used, int n_embd,
+                   cudaStream_t stream) {
+    if (fault_hit("fr_moe_combine")) return FR_EINJECTED;
+    if (T < 0 || n_used <= 0 || n_used > MOE_MAX_USED || n_embd <= 0) return FR_EINVAL;
+    if (T == 0) return FR_OK;
+    if (!part || !wts || !out) return FR_EINVAL;
+    return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream, part, wts, resid, out, n_used,
+                      n_embd);
+}
+
+} // extern "C"

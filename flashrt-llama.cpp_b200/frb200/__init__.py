@@ -60,6 +60,9 @@ SIGNATURES = {
                                    _i32, _i32, _i32, _i32, _vp]),
     "fr_moe_ffn_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                 _i32, _f32, _vp, _vp, _vp, _vp, _vp]),
+    "fr_moe_experts_nvfp4": (_i32, [_vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32,
+                                    _i32, _vp]),
+    "fr_moe_combine": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "fr_sf_bytes": (_i64, [_i64, _i64]),
     "fr_packed_bytes": (_i64, [_i64, _i64]),
     "fr_quantize_act_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
@@ -248,6 +251,27 @@ def moe_ffn(x, w_r, wg, wu, wd, n_embd, n_ff, E, n_used, sg=None, su=None, sd=No
          _ptr(resid), _ptr(out), T, n_embd, n_ff, E, n_used, clamp, _ptr(chk.get("ids")), _ptr(chk.get("wts")),
          _ptr(chk.get("glu")), _ptr(chk.get("part")), _stream(stream))
     return (out, chk) if check else out
+
+
+def moe_experts(x, eid, wg, wu, wd, n_embd, n_ff, E, sg=None, su=None, sd=None, out=None, stream=None):
+    """Expert FFN over pre-routed rows: x [S, n_embd] f32, eid [S] int32."""
+    import torch
+    S = x.shape[0]
+    if out is None:
+        out = torch.empty((S, n_embd), dtype=torch.float32, device=x.device)
+    call("fr_moe_experts_nvfp4", _ptr(x), x.stride(0) if S else n_embd, _ptr(eid), S, _ptr(wg), _ptr(wu), _ptr(wd),
+         _ptr(sg), _ptr(su), _ptr(sd), _ptr(out), out.stride(0) if S else n_embd, n_embd, n_ff, E, _stream(stream))
+    return out
+
+
+def moe_combine(part, wts, n_embd, resid=None, out=None, stream=None):
+    """part [T*n_used, n_embd], wts [T, n_used] -> out [T, n_embd]."""
+    import torch
+    T, n_used = wts.shape
+    if out is None:
+        out = torch.empty((T, n_embd), dtype=torch.float32, device=part.device)
+    call("fr_moe_combine", _ptr(part), _ptr(wts), _ptr(resid), _ptr(out), T, n_used, n_embd, _stream(stream))
+    return out
 
 
 def sf_bytes(rows: int, K: int) -> int:

@@ -1,0 +1,132 @@
+"""Multi-GPU plumbing: one process per GPU, torch.distributed (NCCL over
+NVLink / NVSwitch) for the exchanges, the library's kernels for the compute.
+
+The reference runs on one device only (its fusion windows bind to the first
+SM120 device that runs a graph); tensor and expert parallelism are new here.
+
+* Tensor-parallel dense FFN (config 2): rank r owns gate/up rows
+  [r*F/P, (r+1)*F/P) and down rows [r*D/P, (r+1)*D/P).  The GLU shards are
+  all-gathered before the down projection and the output shards after it.
+  q8_1 blocks cover 32 consecutive values and shard boundaries are multiples
+  of 32, so every rank quantizes the gathered GLU exactly as one GPU would.
+* Expert-parallel MoE (config 3): rank r owns experts [r*E/P, (r+1)*E/P) and
+  its own tokens.  Routing is computed locally (replicated router weights);
+  each routed slot's activation row goes to the expert's owner (all-to-all),
+  the owner runs its experts on the rows it received, the outputs come back
+  (all-to-all) and the token's owner combines them in slot order -- the same
+  arithmetic, in the same order, as the single-GPU fused layer.
+
+`Kernels` bundles the compute calls; `GpuKernels` (the default) goes through
+the C-ABI.  The exchange logic takes any object with the same methods, which is
+how the CPU tests drive it over gloo.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import (gemv_swiglu, moe_combine, moe_experts, moe_route, mul_mat, quantize_q8_1)
+
+
+class GpuKernels:
+    """Compute through libfrb200 (CUDA tensors)."""
+
+    def gate_up(self, x, wg, wu, n_rows, K):
+        q8 = quantize_q8_1(x)
+        return gemv_swiglu(wg, wu, q8, n_rows, K, x.shape[0])
+
+    def down(self, glu, wd, n_rows, K):
+        return mul_mat(wd, glu, n_rows, K)
+
+    def route(self, x, w_r, n_used, clamp):
+        _, ids, wts, _, _, _ = moe_route(x, w_r, n_used, clamp)
+        return ids, wts
+
+    def experts(self, x, eid, wg, wu, wd, n_embd, n_ff, E):
+        return moe_experts(x, eid, wg, wu, wd, n_embd, n_ff, E)
+
+    def combine(self, part, wts, n_embd, resid=None):
+        return moe_combine(part, wts, n_embd, resid=resid)
+
+
+def shard_range(n: int, rank: int, world: int):
+    """Contiguous shard [lo, hi) of n items for `rank`; n % world == 0 required."""
+    if n % world:
+        raise ValueError(f"{n} rows do not split over {world} ranks")
+    per = n // world
+    return rank * per, (rank + 1) * per
+
+
+def _all_gather_cols(t: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """[T, n] on every rank -> [T, world*n], shards in rank order."""
+    T, n = t.shape
+    buf = torch.empty((world * T, n), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(buf, t.contiguous(), group=group)
+    return buf.view(world, T, n).permute(1, 0, 2).reshape(T, world * n)
+
+
+def tp_ffn(x, wg_shard, wu_shard, wd_shard, n_embd, n_ff, group=None, kernels=None):
+    """Row-sharded dense SwiGLU FFN; x [T, n_embd] replicated, returns the full
+    output [T, n_embd] on every rank."""
+    k = kernels or GpuKernels()
+    world = dist.get_world_size(group)
+    glu_shard = k.gate_up(x, wg_shard, wu_shard, n_ff // world, n_embd)
+    glu = _all_gather_cols(glu_shard, world, group)
+    y_shard = k.down(glu, wd_shard, n_embd // world, n_ff)
+    return _all_gather_cols(y_shard, world, group)
+
+
+def _exchange(send: torch.Tensor, send_counts, recv_counts, group=None) -> torch.Tensor:
+    """Variable-size all-to-all of rows (counts are per peer, in rows)."""
+    world = len(send_counts)
+    width = send.shape[1:] if send.dim() > 1 else ()
+    out = torch.empty((int(sum(recv_counts)),) + tuple(width), dtype=send.dtype, device=send.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_to_all_single(out, send.contiguous(), output_split_sizes=list(recv_counts),
+                               input_split_sizes=list(send_counts), group=group)
+        return out
+    # backends without all_to_all: every rank gathers the padded send buffers
+    mx = max(1, max(int(c) for c in send_counts), max(int(c) for c in recv_counts))
+    pad = torch.zeros((world, mx) + tuple(width), dtype=send.dtype, device=send.device)
+    offs = [0]
+    for c in send_counts:
+        offs.append(offs[-1] + int(c))
+    rank = dist.get_rank(group)
+    gathered = torch.empty((world, world, mx) + tuple(width), dtype=send.dtype, device=send.device)
+    for p in range(world):
+        pad[p, :int(send_counts[p])] = send[offs[p]:offs[p + 1]]
+    dist.all_gather_into_tensor(gathered.view(world * world, mx, *width), pad.view(world, mx, *width), group=group)
+    pieces = [gathered[src, rank, :int(recv_counts[src])] for src in range(world)]
+    out.copy_(torch.cat(pieces, 0) if pieces else out)
+    return out
+
+
+def ep_moe(x, w_r, wg_local, wu_local, wd_local, n_embd, n_ff, E, n_used, resid=None,
+           clamp=6.103515625e-5, group=None, kernels=None):
+    """Expert-parallel MoE layer for this rank's tokens x [T, n_embd].
+    wg/wu/wd_local hold this rank's E/P experts.  Returns [T, n_embd]."""
+    k = kernels or GpuKernels()
+    world = dist.get_world_size(group)
+    E_p = E // world
+    T = x.shape[0]
+    ids, wts = k.route(x, w_r, n_used, clamp)                    # [T, n_used] global expert ids
+    flat = ids.reshape(-1).long()
+    dest = torch.div(flat, E_p, rounding_mode="floor")
+    # stable order of the slots by destination rank (slot order inside a rank)
+    order = torch.argsort(dest * (T * n_used) + torch.arange(T * n_used, device=flat.device))
+    send_counts = torch.bincount(dest, minlength=world)
+    counts = torch.empty((world, world), dtype=torch.int64, device=flat.device)
+    dist.all_gather_into_tensor(counts.view(-1), send_counts.to(torch.int64).contiguous(), group=group)
+    rank = dist.get_rank(group)
+    sc = [int(v) for v in counts[rank].tolist()]
+    rc = [int(v) for v in counts[:, rank].tolist()]
+    tok = torch.div(order, n_used, rounding_mode="floor")
+    send_x = x[tok]                                               # [S, n_embd] in send order
+    send_e = (flat[order] - dest[order] * E_p).to(torch.int32)
+    recv_x = _exchange(send_x, sc, rc, group)
+    recv_e = _exchange(send_e.view(-1, 1), sc, rc, group).view(-1)
+    y_recv = k.experts(recv_x.contiguous(), recv_e.contiguous(), wg_local, wu_local, wd_local, n_embd, n_ff, E_p)
+    back = _exchange(y_recv, rc, sc, group)                       # rows in our send order
+    part = torch.empty((T * n_used, n_embd), dtype=back.dtype, device=back.device)
+    part[order] = back
+    return k.combine(part, wts, n_embd, resid=resid)

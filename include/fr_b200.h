@@ -188,6 +188,24 @@ int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const voi
                      int32_t *chk_ids, float *chk_wts, float *chk_glu, float *chk_part,
                      cudaStream_t stream);
 
+/* Expert FFN over pre-routed rows (the expert-parallel building block): row s
+ * of x [S, ldx] goes through expert eid[s] (0 <= eid < E): SwiGLU of the
+ * grouped gate/up matvecs, q8_1 of the GLU, grouped down matvec, scaled by
+ * sd[e]: out[s] = sd[e] * Wd[e] . q8(swiglu(...)).  Every expert that appears
+ * is read once.  Rows with an out-of-range id are flagged (status bit 1) and
+ * left untouched.  The routed/shared MOEFFN window's expert part,
+ * src/fr_win_flint_sm120.cu:1890-2094. */
+int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S,
+                         const void *wg, const void *wu, const void *wd,
+                         const float *sg, const float *su, const float *sd,
+                         float *out, int64_t ldo, int n_embd, int n_ff, int E, cudaStream_t stream);
+
+/* Weighted slot-order combine: out[t] = sum_k w[t,k] * part[t*n_used + k]
+ * (k ascending) (+ resid[t]); part rows n_embd floats, out / resid [T, n_embd]
+ * (src/fr_win_flint_batched_moe.cuh:342-379). */
+int fr_moe_combine(const float *part, const float *wts, const float *resid, float *out,
+                   int T, int n_used, int n_embd, cudaStream_t stream);
+
 /* ------------------------------------------------- (a5/a6) W4A4 tcgen05 path
  * The reference's Thor launch interface (include/fr_kernels.h:21-57), same
  * arguments, same meaning, same return codes; C++ callers also get the
