@@ -167,10 +167,27 @@ def run_reference(args):
 
 # ---------------------------------------------------------------- our arm
 
+def _moe_sets(frb200, torch, dev, rank, world, n_sets):
+    """Config 3 experts (E=128, hidden 2048, FFN 768): this rank's E/world."""
+    E, ne, nf = 128, 2048, 768
+    Ep = E // world
+    sets = []
+    for s in range(n_sets):
+        base = 0x5EED2000 + 100 * s
+        wr = torch.from_numpy(frb200.synth_normal(base, E * ne, 0.0, 0.02).reshape(E, ne)).to(dev)
+        # full-model expert tensors are generated per expert id, so each rank
+        # holds exactly the rows of its experts
+        wg = torch.from_numpy(frb200.synth_nvfp4(base + 1, E * nf, ne)[rank * Ep * nf:(rank + 1) * Ep * nf]).to(dev)
+        wu = torch.from_numpy(frb200.synth_nvfp4(base + 2, E * nf, ne)[rank * Ep * nf:(rank + 1) * Ep * nf]).to(dev)
+        wd = torch.from_numpy(frb200.synth_nvfp4(base + 3, E * ne, nf)[rank * Ep * ne:(rank + 1) * Ep * ne]).to(dev)
+        sets.append((wr, wg, wu, wd))
+    return sets
+
+
 def run_ours(args):
-    import numpy as np
     import torch
     import frb200
+    from frb200 import parallel as P
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -184,37 +201,8 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = dist
     frb200.lib()
-
     hbm, peak_kind = _peaks()
-    rb_e, rb_f = N_EMBD // 64 * 36, N_FF // 64 * 36
-    sets = []
-    for s in range(N_SETS):
-        base = 0x5EED0000 + 100 * s + 1000 * rank
-        wg = torch.from_numpy(frb200.synth_nvfp4(base + 1, N_FF, N_EMBD)).to(dev)
-        wu = torch.from_numpy(frb200.synth_nvfp4(base + 2, N_FF, N_EMBD)).to(dev)
-        wd = torch.from_numpy(frb200.synth_nvfp4(base + 3, N_EMBD, N_FF)).to(dev)
-        sets.append((wg, wu, wd))
     stream = torch.cuda.Stream(dev)
-    Tmax = 64
-    x_all = torch.from_numpy(frb200.synth_normal(0x5EED0000 + 10, Tmax * N_EMBD).reshape(Tmax, N_EMBD)).to(dev)
-    outs = [torch.empty((Tmax, N_EMBD), dtype=torch.float32, device=dev) for _ in range(N_SETS)]
-
-    def step(i, T, strm):
-        wg, wu, wd = sets[i % N_SETS]
-        frb200.ffn(x_all[:T], wg, wu, wd, N_EMBD, N_FF, out=outs[i % N_SETS][:T], stream=strm)
-
-    def graphs_for(T):
-        gs = []
-        with torch.cuda.stream(stream):
-            for i in range(N_SETS):       # eager warm-up sizes the workspaces
-                step(i, T, stream)
-        stream.synchronize()
-        for i in range(N_SETS):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                step(i, T, stream)
-            gs.append(g)
-        return gs
 
     def barrier():
         torch.cuda.synchronize()
@@ -222,32 +210,70 @@ def run_ours(args):
             pg.barrier()
         torch.cuda.synchronize()
 
-    def time_steps(gs, K, W):
+    def max_over_ranks(v):
+        if pg is None:
+            return v
+        t = torch.tensor([v], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def time_fn(fn, K, W):
         with torch.cuda.stream(stream):
             for i in range(W):
-                gs[i % N_SETS].replay()
+                fn(i)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             e0.record(stream)
             for i in range(K):
-                gs[i % N_SETS].replay()
+                fn(i)
             e1.record(stream)
         e1.synchronize()
         barrier()
-        ms = e0.elapsed_time(e1)
-        if pg is not None:
-            t = torch.tensor([ms], device=dev)
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms / K
+        return max_over_ranks(e0.elapsed_time(e1)) / K
+
+    # ---------------- dense FFN (config 2): single GPU, or row-sharded over the ranks
+    f0, f1 = P.shard_range(N_FF, rank, world)
+    e0_, e1_ = P.shard_range(N_EMBD, rank, world)
+    sets = []
+    for s in range(N_SETS):
+        base = 0x5EED0000 + 100 * s
+        wg = frb200.synth_nvfp4(base + 1, N_FF, N_EMBD)[f0:f1]
+        wu = frb200.synth_nvfp4(base + 2, N_FF, N_EMBD)[f0:f1]
+        wd = frb200.synth_nvfp4(base + 3, N_EMBD, N_FF)[e0_:e1_]
+        sets.append(tuple(torch.from_numpy(w.copy()).to(dev) for w in (wg, wu, wd)))
+    Tmax = 64
+    x_all = torch.from_numpy(frb200.synth_normal(0x5EED0000 + 10, Tmax * N_EMBD).reshape(Tmax, N_EMBD)).to(dev)
+    outs = [torch.empty((Tmax, N_EMBD), dtype=torch.float32, device=dev) for _ in range(N_SETS)]
+
+    tp = P.TpFfn(Tmax, N_EMBD, N_FF) if world > 1 else None
+
+    def ffn_step(i, T, x=None, out=None):
+        wg, wu, wd = sets[i % N_SETS]
+        xx = x_all[:T] if x is None else x
+        if world == 1:
+            frb200.ffn(xx, wg, wu, wd, N_EMBD, N_FF, out=(outs[i % N_SETS][:T] if out is None else out), stream=stream)
+        else:
+            tp(xx, wg, wu, wd, out=(outs[i % N_SETS][:T] if out is None else out), stream=stream)
+
+    def graphs_for(fn):
+        with torch.cuda.stream(stream):
+            for i in range(N_SETS):           # eager warm-up sizes workspaces, initialises NCCL
+                fn(i)
+        barrier()
+        gs = []
+        for i in range(N_SETS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                fn(i)
+            gs.append(g)
+        return gs
 
     launches0 = frb200.lib().fr_kernel_launches()
-    g1 = graphs_for(1)
+    g1 = graphs_for(lambda i: ffn_step(i, 1))
     launches_per_step = (frb200.lib().fr_kernel_launches() - launches0) // (2 * N_SETS)
 
-    # clocks: sample over a load window that contains the timed region
     sampler = ClockSampler(local)
     sampler.start()
     t_end = time.time() + 1.5
@@ -258,87 +284,94 @@ def run_ours(args):
                 g1[i % N_SETS].replay()
                 i += 1
             stream.synchronize()
-    ms1 = time_steps(g1, args.steps, max(args.warmup, 3))
+    ms1 = time_fn(lambda i: g1[i % N_SETS].replay(), args.steps, max(args.warmup, 3))
     clocks = sampler.stop()
 
-    # extra batch sizes on the same path
     extra = {}
     for T in (8, 64):
-        gT = graphs_for(T)
-        msT = time_steps(gT, max(10, args.steps // 8), max(args.warmup, 3))
-        extra[f"ffn_T{T}_gbs"] = round(world * ffn_bytes(T) / (msT * 1e-3) / 1e9, 1)
+        gT = graphs_for(lambda i, T=T: ffn_step(i, T))
+        msT = time_fn(lambda i: gT[i % N_SETS].replay(), max(10, args.steps // 8), max(args.warmup, 3))
+        extra[f"ffn_T{T}_gbs"] = round(ffn_bytes(T) / (msT * 1e-3) / 1e9, 1)
         extra[f"ffn_T{T}_ms_per_step"] = round(msT, 5)
         del gT
 
-    # dominant kernel: gate/up SwiGLU matvec timed alone (events on its stream)
-    q8x = frb200.quantize_q8_1(x_all[:1], stream=stream)
-    glu = torch.empty((1, N_FF), dtype=torch.float32, device=dev)
-    kgs = []
-    for i in range(N_SETS):
-        wg, wu, _ = sets[i]
-        frb200.gemv_swiglu(wg, wu, q8x, N_FF, N_EMBD, 1, out=glu, stream=stream)
-    stream.synchronize()
-    for i in range(N_SETS):
-        wg, wu, _ = sets[i]
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            frb200.gemv_swiglu(wg, wu, q8x, N_FF, N_EMBD, 1, out=glu, stream=stream)
-        kgs.append(g)
-    k_ms = time_steps(kgs, max(args.steps, 20), 5)
-    k_gbs = gateup_bytes(1) / (k_ms * 1e-3) / 1e9
+    # dominant kernel (single GPU): gate/up SwiGLU matvec, timed alone on its stream
+    roof = None
+    if world == 1:
+        q8x = frb200.quantize_q8_1(x_all[:1], stream=stream)
+        glu = torch.empty((1, N_FF), dtype=torch.float32, device=dev)
+        kgs = graphs_for(lambda i: frb200.gemv_swiglu(sets[i][0], sets[i][1], q8x, N_FF, N_EMBD, 1, out=glu,
+                                                       stream=stream))
+        k_ms = time_fn(lambda i: kgs[i % N_SETS].replay(), max(args.steps, 20), 5)
+        k_gbs = gateup_bytes(1) / (k_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "k_gemv<32,1,SWIGLU,1,16> (gate/up, T=1)", "achieved": round(k_gbs, 1),
+                "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(k_gbs / hbm, 4),
+                "traffic": TRAFFIC_GATEUP, "algorithmic_bytes": gateup_bytes(1), "ms_per_launch": round(k_ms, 5)}
+        del kgs
 
-    # e2e through the public C entry point: pinned H2D of x, the FFN, D2H of out
+    # e2e through the public entry point: pinned H2D of x, the FFN, D2H of out
     x_host = torch.from_numpy(frb200.synth_normal(0x5EED0000 + 10, N_EMBD).reshape(1, N_EMBD)).pin_memory()
     o_host = torch.empty((1, N_EMBD), dtype=torch.float32).pin_memory()
     x_dev = torch.empty((1, N_EMBD), dtype=torch.float32, device=dev)
-    egs = []
-    for i in range(N_SETS):
-        with torch.cuda.stream(stream):
-            x_dev.copy_(x_host, non_blocking=True)
-            wg, wu, wd = sets[i]
-            frb200.ffn(x_dev, wg, wu, wd, N_EMBD, N_FF, out=outs[i][:1], stream=stream)
-            o_host.copy_(outs[i][:1], non_blocking=True)
-    stream.synchronize()
-    for i in range(N_SETS):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            x_dev.copy_(x_host, non_blocking=True)
-            wg, wu, wd = sets[i]
-            frb200.ffn(x_dev, wg, wu, wd, N_EMBD, N_FF, out=outs[i][:1], stream=stream)
-            o_host.copy_(outs[i][:1], non_blocking=True)
-        egs.append(g)
-    e_ms = time_steps(egs, args.steps, max(args.warmup, 3))
+
+    def e2e_step(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        ffn_step(i, 1, x=x_dev, out=outs[i % N_SETS][:1])
+        o_host.copy_(outs[i % N_SETS][:1], non_blocking=True)
+
+    egs = graphs_for(e2e_step)
+    e_ms = time_fn(lambda i: egs[i % N_SETS].replay(), args.steps, max(args.warmup, 3))
+
+    # ---------------- MoE layer (config 3): fused on one GPU, expert-parallel over ranks
+    msets = _moe_sets(frb200, torch, dev, rank, world, 2)
+    for T in (1, 64):
+        xm = torch.from_numpy(frb200.synth_normal(0x5EED3000 + rank * 131 + T, T * 2048).reshape(T, 2048)).to(dev)
+        om = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+        if world == 1:
+            mg = graphs_for(lambda i, xm=xm, om=om: frb200.moe_ffn(xm, *msets[i % 2], 2048, 768, 128, 8, out=om,
+                                                                  stream=stream))
+            mms = time_fn(lambda i: mg[i % N_SETS].replay(), max(20, args.steps // 4), max(args.warmup, 3))
+            del mg
+        else:
+            with torch.cuda.stream(stream):
+                mms = time_fn(lambda i, xm=xm: P.ep_moe(xm, *msets[i % 2], 2048, 768, 128, 8),
+                              max(10, args.steps // 10), max(args.warmup, 3))
+        extra[f"moe_T{T}_tok_s"] = round(world * T / (mms * 1e-3), 1)
+        extra[f"moe_T{T}_ms_per_layer"] = round(mms, 5)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, cores, sample = cpu_reference_line(args, budget_s=10.0)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
 
-    value = world * ffn_bytes(1) / (ms1 * 1e-3) / 1e9
+    value = ffn_bytes(1) / (ms1 * 1e-3) / 1e9 if world > 1 else ffn_bytes(1) / (ms1 * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms1, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8xe2m1 (q8_1 x NVFP4, int32 sub-block sums, fp32 scale)",
+        "warmup": args.warmup, "ms_per_step": round(ms1, 5), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "int8xe2m1 (q8_1 x NVFP4, exact sub-block sums, fp32 scale)",
         "data": "synthetic (seeded splitmix64 / Box-Muller; BASELINE configs)",
         "config": {"workload": "dense FFN gate/up 14336x4096 + down 4096x14336 NVFP4 x q8_1, T=1 (configs[1])",
-                   "global_batch": world, "seq_len": 1,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "global_batch": 1, "seq_len": 1,
+                   "parallelism": f"tp{world} (row-sharded; GLU and output rows stored into every rank by the matvec "
+                                  f"epilogues over NVLink, bounded flag waits)" if world > 1
+                   else "single GPU",
                    "l2": f"rotating {N_SETS} weight sets ({N_SETS * ffn_bytes(0) / 1e6:.0f} MB > L2)",
-                   "graph": "one CUDA graph per step, PDL edges between kernels"},
+                   "graph": "one CUDA graph per step (PDL edges between kernels; no NCCL call on the tp step)",
+                   "moe": "config 3 layer (E=128, top-8, hidden 2048, FFN 768): fused on 1 GPU, expert-parallel "
+                          "(E/N experts per rank, all-to-all of routed rows, per-rank tokens) for N > 1"},
         "clocks": clocks,
-        "e2e": {"value": round(world * ffn_bytes(1) / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+        "e2e": {"value": round(ffn_bytes(1) / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": N_EMBD * 4, "d2h_bytes_per_step": N_EMBD * 4,
-                "ms_per_step": round(e_ms, 5)},
+                "ms_per_step": round(e_ms, 5), "note": "per rank copies, in the step's CUDA graph"},
         "gpu_launches": int(launches_per_step * args.steps),
-        "roofline": {"bound": "hbm", "kernel": "k_gemv<32,1,SWIGLU> (gate/up, T=1)", "achieved": round(k_gbs, 1),
-                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(k_gbs / hbm, 4),
-                     "traffic": TRAFFIC_GATEUP, "algorithmic_bytes": gateup_bytes(1),
-                     "ms_per_launch": round(k_ms, 5)},
+        "roofline": roof,
         "cpu_baseline": cpu,
     }
     line.update(extra)
-    for g in g1 + kgs + egs:
-        del g
+    del g1, egs
+    if tp is not None:
+        tp.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:

@@ -83,6 +83,13 @@ struct GvParams {
     int n_slots;            // ring slots (multiple of GV_CWARPS)
     int slot_bytes;         // bytes per slot (both operands)
     int word_mode;          // rows not 16-byte aligned: producer warp copies words
+    // tensor-parallel epilogue (npeers > 0): every output value is also stored
+    // into each rank's copy of the output (peer_base[p] + peer_off bytes, row
+    // offset col_off), and when the CTA is done it adds 1 to its rank's slot
+    // of every peer's flag array (peer_base[p] + flag_off bytes)
+    uint8_t *const *peer_base;
+    int npeers, rank;
+    int64_t peer_off, flag_off, col_off;
 };
 
 // Byte position inside a sub-block's 16 activation bytes of value j (0..15),
@@ -336,7 +343,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
 
     for (int i = 0; i < n_st; ++i) {
         const int s = i % NS;
-        if (!mbar_wait(&full[s], (i / NS) & 1, 2)) return;
+        if (!mbar_wait(&full[s], (i / NS) & 1, 2)) break;
         const int rows = min(SR, n_rows - i * SR);
         const uint8_t *st = ring + static_cast<size_t>(s) * p.slot_bytes;
         float acc0[R2][TT], acc1[R2][TT];
@@ -407,13 +414,60 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
                                 v = acc0[r][t] * sc0;
                                 if (p.resid) v += p.resid[tt * p.ldr + row];
                             }
-                            p.y[tt * p.ldy + row] = v;
+                            if (p.npeers > 0) {
+                                for (int q = 0; q < p.npeers; ++q) {
+                                    float *py = reinterpret_cast<float *>(p.peer_base[q] + p.peer_off);
+                                    py[tt * p.ldy + p.col_off + row] = v;
+                                }
+                            } else {
+                                p.y[tt * p.ldy + row] = v;
+                            }
                         }
                     }
                 }
             }
         }
     }
+    if (p.npeers > 0) {
+        // publish this CTA's rows to every rank: each storing thread fences at
+        // system scope, the consumer warps meet, one thread bumps the flags
+        __threadfence_system();
+        named_bar(2, CW * 32);
+        if (warp == 0 && lane == 0) {
+            for (int q = 0; q < p.npeers; ++q) {
+                unsigned int *fl = reinterpret_cast<unsigned int *>(p.peer_base[q] + p.flag_off);
+                atomicAdd_system(fl + p.rank, 1u);
+            }
+        }
+    }
+}
+
+// Tensor-parallel completion wait: one warp waits until every rank's flag
+// counter reached the number this rank has consumed so far plus `expect`
+// (the producer kernel's CTA count), then records the new consumed count.
+// Counters only grow, so CUDA-graph replays need no reset.  The wait is
+// bounded (status bit 0, site 30) and never traps.
+__global__ void __launch_bounds__(32) k_tp_wait(const unsigned int *flags, unsigned int *seen, int nranks,
+                                                unsigned int expect) {
+    fr_pdl_wait();
+    const int lane = threadIdx.x;
+    if (lane < nranks) {
+        const unsigned int target = seen[lane] + expect;
+        const uint64_t t0 = fr_now_ns();
+        for (;;) {
+            unsigned int v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + lane) : "memory");
+            if (static_cast<int>(v - target) >= 0) break;
+            if (fr_now_ns() - t0 > FR_WAIT_NS) {
+                fr_flag(FR_ST_TIMEOUT | (30u << FR_ST_SITE_SHIFT));
+                break;
+            }
+        }
+        seen[lane] = target;
+    }
+    __syncwarp();
+    __threadfence_system();
+    fr_pdl_trigger();
 }
 
 } // namespace frb

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 
 #include "fr_common.cuh"
 #include "fr_runtime.cuh"
@@ -1175,6 +1176,155 @@ int fr_moe_combine(const float *part, const float *wts, const float *resid, floa
     if (!part || !wts || !out) return FR_EINVAL;
     return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream, part, wts, resid, out, n_used,
                       n_embd);
+}
+
+} // extern "C"
+
+// ======================================================================
+// Tensor-parallel FFN over NVLink peer stores
+// ======================================================================
+namespace frb {
+
+// symmetric buffer layout: [flags1 P | flags2 P | seen1 P | seen2 P] u32, then
+// (256-byte aligned) the GLU copy [T, n_ff] and the output copy [T, n_embd]
+struct TpLayout {
+    int64_t flags1, flags2, seen1, seen2, glu, y, total;
+};
+static TpLayout tp_layout(int T, int n_embd, int n_ff, int P) {
+    TpLayout l{};
+    l.flags1 = 0;
+    l.flags2 = 4LL * P;
+    l.seen1 = 8LL * P;
+    l.seen2 = 12LL * P;
+    l.glu = (16LL * P + 255) / 256 * 256;
+    l.y = l.glu + (static_cast<int64_t>(T) * n_ff * 4 + 255) / 256 * 256;
+    l.total = l.y + (static_cast<int64_t>(T) * n_embd * 4 + 255) / 256 * 256;
+    return l;
+}
+
+// CTAs the matvec launches for (N, K, T) -- what each rank counts into the flags
+static unsigned gemv_ctas(int N, int K, int64_t w_ld, int T, bool dual) {
+    const GvPlan pl = gv_plan(N, K, w_ld, T, dual);
+    const int windows = (T + pl.TT - 1) / pl.TT;
+    return static_cast<unsigned>(pl.grid * windows);
+}
+
+} // namespace frb
+
+extern "C" {
+
+int fr_ipc_alloc(int64_t bytes, void **dev_ptr, void *handle64) {
+    if (bytes <= 0 || !dev_ptr || !handle64) return FR_EINVAL;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    void *p = nullptr;
+    int rc = cuda_rc(cudaMalloc(&p, static_cast<size_t>(bytes)));
+    if (rc != FR_OK) return rc;
+    rc = cuda_rc(cudaMemset(p, 0, static_cast<size_t>(bytes)));
+    cudaIpcMemHandle_t h;
+    if (rc == FR_OK) rc = cuda_rc(cudaIpcGetMemHandle(&h, p));
+    if (rc != FR_OK) {
+        cudaFree(p);
+        return rc;
+    }
+    std::memcpy(handle64, &h, sizeof(h));
+    *dev_ptr = p;
+    return FR_OK;
+}
+
+int fr_ipc_open(const void *handle64, void **dev_ptr) {
+    if (!handle64 || !dev_ptr) return FR_EINVAL;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle64, sizeof(h));
+    return cuda_rc(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int fr_ipc_close(void *dev_ptr) { return dev_ptr ? cuda_rc(cudaIpcCloseMemHandle(dev_ptr)) : FR_EINVAL; }
+
+int fr_ipc_free(void *dev_ptr) { return dev_ptr ? cuda_rc(cudaFree(dev_ptr)) : FR_EINVAL; }
+
+int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks) {
+    if (T <= 0 || n_embd <= 0 || n_ff <= 0 || nranks <= 0) return -1;
+    return tp_layout(T, n_embd, n_ff, nranks).total;
+}
+
+int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard, const float *sg,
+                    const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                    int nranks, int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes,
+                    cudaStream_t stream) {
+    if (fault_hit("fr_tp_ffn_nvfp4")) return FR_EINJECTED;
+    if (!x || !wg_shard || !wu_shard || !wd_shard || !out || !peer_base || !local_base) return FR_EINVAL;
+    if (T <= 0 || nranks <= 0 || nranks > 32 || rank < 0 || rank >= nranks) return FR_EINVAL;
+    // shard boundaries on q8_1 block (32) boundaries, rows whole NVFP4 blocks
+    if (n_embd % 64 != 0 || n_ff % 64 != 0 || n_embd % (32 * nranks) != 0 || n_ff % (32 * nranks) != 0)
+        return FR_EINVAL;
+    const TpLayout L = tp_layout(T, n_embd, n_ff, nranks);
+    if (buffer_bytes < L.total) return FR_EINVAL;
+    uint8_t *base = static_cast<uint8_t *>(local_base);
+    const int F_p = n_ff / nranks, D_p = n_embd / nranks;
+    const int64_t ld_gu = static_cast<int64_t>(n_embd) / 64 * NV_BYTES;
+    const int64_t ld_d = static_cast<int64_t>(n_ff) / 64 * NV_BYTES;
+    void *q8x = nullptr, *q8g = nullptr;
+    int rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES, stream, &q8x);
+    if (rc != FR_OK) return rc;
+    rc = workspace_get(WS_GLUQ8, static_cast<size_t>(T) * (n_ff / 32) * Q8_BYTES, stream, &q8g);
+    if (rc != FR_OK) return rc;
+    rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
+    if (rc != FR_OK) return rc;
+    // gate/up shard -> every rank's GLU copy, columns [rank*F_p, (rank+1)*F_p)
+    GvParams p{};
+    p.w0 = static_cast<const uint8_t *>(wg_shard);
+    p.w1 = static_cast<const uint8_t *>(wu_shard);
+    p.w_ld = ld_gu;
+    p.q8 = static_cast<const uint8_t *>(q8x);
+    p.ldq = n_embd / 32;
+    p.s0 = sg;
+    p.s1 = su;
+    p.y = nullptr;
+    p.ldy = n_ff;
+    p.N = F_p;
+    p.K = n_embd;
+    p.peer_base = reinterpret_cast<uint8_t *const *>(peer_base);
+    p.npeers = nranks;
+    p.rank = rank;
+    p.peer_off = L.glu;
+    p.flag_off = L.flags1;
+    p.col_off = static_cast<int64_t>(rank) * F_p;
+    rc = gemv_run(p, T, true, stream);
+    if (rc != FR_OK) return rc;
+    const unsigned exp1 = gemv_ctas(F_p, n_embd, ld_gu, T, true);
+    rc = launch_pdl(k_tp_wait, dim3(1), dim3(32), 0, stream, reinterpret_cast<const unsigned int *>(base + L.flags1),
+                    reinterpret_cast<unsigned int *>(base + L.seen1), nranks, exp1);
+    if (rc != FR_OK) return rc;
+    const float *glu = reinterpret_cast<const float *>(base + L.glu);
+    rc = quantize_launch(glu, n_ff, q8g, n_ff / 32, T, n_ff, stream);
+    if (rc != FR_OK) return rc;
+    // down shard -> every rank's output copy, columns [rank*D_p, (rank+1)*D_p)
+    GvParams q{};
+    q.w0 = static_cast<const uint8_t *>(wd_shard);
+    q.w_ld = ld_d;
+    q.q8 = static_cast<const uint8_t *>(q8g);
+    q.ldq = n_ff / 32;
+    q.s0 = sd;
+    q.resid = resid ? resid + static_cast<int64_t>(rank) * D_p : nullptr;
+    q.ldr = n_embd;
+    q.y = nullptr;
+    q.ldy = n_embd;
+    q.N = D_p;
+    q.K = n_ff;
+    q.peer_base = reinterpret_cast<uint8_t *const *>(peer_base);
+    q.npeers = nranks;
+    q.rank = rank;
+    q.peer_off = L.y;
+    q.flag_off = L.flags2;
+    q.col_off = static_cast<int64_t>(rank) * D_p;
+    rc = gemv_run(q, T, false, stream);
+    if (rc != FR_OK) return rc;
+    const unsigned exp2 = gemv_ctas(D_p, n_ff, ld_d, T, false);
+    rc = launch_pdl(k_tp_wait, dim3(1), dim3(32), 0, stream, reinterpret_cast<const unsigned int *>(base + L.flags2),
+                    reinterpret_cast<unsigned int *>(base + L.seen2), nranks, exp2);
+    if (rc != FR_OK) return rc;
+    return cuda_rc(cudaMemcpyAsync(out, base + L.y, static_cast<size_t>(T) * n_embd * 4, cudaMemcpyDeviceToDevice,
+                                   stream));
 }
 
 } // extern "C"

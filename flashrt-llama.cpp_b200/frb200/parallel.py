@@ -25,7 +25,9 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from . import (gemv_swiglu, moe_combine, moe_experts, moe_route, mul_mat, quantize_q8_1)
+import ctypes as C
+
+from . import (_ptr, _stream, call, gemv_swiglu, lib, moe_combine, moe_experts, moe_route, mul_mat, quantize_q8_1)
 
 
 class GpuKernels:
@@ -74,6 +76,75 @@ def tp_ffn(x, wg_shard, wu_shard, wd_shard, n_embd, n_ff, group=None, kernels=No
     glu = _all_gather_cols(glu_shard, world, group)
     y_shard = k.down(glu, wd_shard, n_embd // world, n_ff)
     return _all_gather_cols(y_shard, world, group)
+
+
+class TpFfn:
+    """Tensor-parallel dense FFN with the all-gathers fused into the matvec
+    epilogues: each rank's gate/up and down matvecs store their output rows
+    straight into every rank's copy over NVLink (CUDA IPC peer mappings, no
+    multicast object) and count finished CTAs into per-rank flags, which a
+    bounded one-warp wait consumes.  No NCCL call on the step; the step is one
+    stream of kernels and is CUDA-graph capturable.
+
+    `max_tokens` sizes the shared buffer; every call must use the same token
+    count on all ranks (ranks advance in lock step)."""
+
+    def __init__(self, max_tokens, n_embd, n_ff, group=None):
+        import torch
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_embd, self.n_ff, self.max_tokens = n_embd, n_ff, max_tokens
+        L = lib()
+        self.nbytes = int(L.fr_tp_buffer_bytes(max_tokens, n_embd, n_ff, self.world))
+        if self.nbytes <= 0:
+            raise ValueError("bad tensor-parallel FFN shape")
+        local = C.c_void_p()
+        handle = (C.c_ubyte * 64)()
+        call("fr_ipc_alloc", self.nbytes, C.byref(local), handle)
+        self.local = local.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self.local)
+                continue
+            p = C.c_void_p()
+            hb = (C.c_ubyte * 64).from_buffer_copy(h)
+            call("fr_ipc_open", hb, C.byref(p))
+            self.opened.append(p.value)
+            ptrs.append(p.value)
+        self.peer_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=torch.cuda.current_device())
+        dist.barrier(group=group)
+
+    def __call__(self, x, wg_shard, wu_shard, wd_shard, sg=None, su=None, sd=None, resid=None, out=None,
+                 stream=None):
+        import torch
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
+        call("fr_tp_ffn_nvfp4", _ptr(x), _ptr(wg_shard), _ptr(wu_shard), _ptr(wd_shard), _ptr(sg), _ptr(su),
+             _ptr(sd), _ptr(resid), _ptr(out), T, self.n_embd, self.n_ff, self.world, self.rank,
+             _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes, _stream(stream))
+        return out
+
+    def close(self):
+        """Release the mappings (all ranks, after their last step has finished)."""
+        import torch
+        if self.local is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            call("fr_ipc_close", C.c_void_p(p))
+        self.opened = []
+        dist.barrier(group=self.group)
+        call("fr_ipc_free", C.c_void_p(self.local))
+        self.local = None
 
 
 def _exchange(send: torch.Tensor, send_counts, recv_counts, group=None) -> torch.Tensor:

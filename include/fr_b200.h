@@ -206,6 +206,34 @@ int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S,
 int fr_moe_combine(const float *part, const float *wts, const float *resid, float *out,
                    int T, int n_used, int n_embd, cudaStream_t stream);
 
+/* ------------------------------------------------------ (e) tensor parallel
+ * One rank's step of the row-sharded dense FFN with the all-gathers fused
+ * into the matvec epilogues over NVLink peer stores.  Rank r holds gate/up
+ * rows [r*F/P, (r+1)*F/P) and down rows [r*D/P, (r+1)*D/P) (F = n_ff,
+ * D = n_embd, P = nranks).  Its gate/up matvec stores its GLU columns into
+ * every rank's GLU copy and counts its finished CTAs into every rank's flags;
+ * after a bounded wait for all ranks' flags each rank quantizes the full GLU,
+ * its down matvec stores its output columns into every rank's output copy,
+ * and after a second wait the full output is copied to `out` on every rank.
+ * peer_base is a device array of the P ranks' base addresses of one
+ * symmetric buffer of fr_tp_buffer_bytes(T, n_embd, n_ff, P) bytes, zeroed
+ * once before first use; local_base is this rank's own base.  The reference
+ * is single-device; no counterpart. */
+int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks);
+int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard,
+                    const float *sg, const float *su, const float *sd, const float *resid, float *out,
+                    int T, int n_embd, int n_ff, int nranks, int rank,
+                    void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream);
+
+/* Peer buffers for fr_tp_ffn_nvfp4 without any library-side multicast
+ * object: fr_ipc_alloc returns a zeroed device buffer and its 64-byte CUDA
+ * IPC handle (exchanged between the ranks by the host), fr_ipc_open maps a
+ * peer's handle into this process, fr_ipc_close / fr_ipc_free release them. */
+int fr_ipc_alloc(int64_t bytes, void **dev_ptr, void *handle64);
+int fr_ipc_open(const void *handle64, void **dev_ptr);
+int fr_ipc_close(void *dev_ptr);
+int fr_ipc_free(void *dev_ptr);
+
 /* ------------------------------------------------- (a5/a6) W4A4 tcgen05 path
  * The reference's Thor launch interface (include/fr_kernels.h:21-57), same
  * arguments, same meaning, same return codes; C++ callers also get the
