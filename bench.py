@@ -235,13 +235,12 @@ def run_ours(args):
 
     # ---------------- dense FFN (config 2): single GPU, or row-sharded over the ranks
     f0, f1 = P.shard_range(N_FF, rank, world)
-    e0_, e1_ = P.shard_range(N_EMBD, rank, world)
     sets = []
     for s in range(N_SETS):
         base = 0x5EED0000 + 100 * s
         wg = frb200.synth_nvfp4(base + 1, N_FF, N_EMBD)[f0:f1]
         wu = frb200.synth_nvfp4(base + 2, N_FF, N_EMBD)[f0:f1]
-        wd = frb200.synth_nvfp4(base + 3, N_EMBD, N_FF)[e0_:e1_]
+        wd = P.down_shard(frb200.synth_nvfp4(base + 3, N_EMBD, N_FF), N_EMBD, N_FF, rank, world)
         sets.append(tuple(torch.from_numpy(w.copy()).to(dev) for w in (wg, wu, wd)))
     Tmax = 64
     x_all = torch.from_numpy(frb200.synth_normal(0x5EED0000 + 10, Tmax * N_EMBD).reshape(Tmax, N_EMBD)).to(dev)
@@ -353,8 +352,8 @@ def run_ours(args):
         "data": "synthetic (seeded splitmix64 / Box-Muller; BASELINE configs)",
         "config": {"workload": "dense FFN gate/up 14336x4096 + down 4096x14336 NVFP4 x q8_1, T=1 (configs[1])",
                    "global_batch": 1, "seq_len": 1,
-                   "parallelism": f"tp{world} (row-sharded; GLU and output rows stored into every rank by the matvec "
-                                  f"epilogues over NVLink, bounded flag waits)" if world > 1
+                   "parallelism": f"tp{world} (sharded over n_ff; the down matvec's epilogue stores its partial rows "
+                                  f"into every rank over NVLink, one bounded wait + rank-order sum)" if world > 1
                    else "single GPU",
                    "l2": f"rotating {N_SETS} weight sets ({N_SETS * ffn_bytes(0) / 1e6:.0f} MB > L2)",
                    "graph": "one CUDA graph per step (PDL edges between kernels; no NCCL call on the tp step)",

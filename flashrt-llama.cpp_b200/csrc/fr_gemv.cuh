@@ -92,6 +92,24 @@ struct GvParams {
     int64_t peer_off, flag_off, col_off;
 };
 
+// Bounded wait of one lane for flags[r] to reach seen + expect (counters only
+// grow; the difference is compared signed so the counters may wrap).
+__device__ __forceinline__ void tp_flag_wait(const unsigned int *flags, unsigned int *seen, int r,
+                                             unsigned int expect) {
+    const unsigned int target = *seen + expect;
+    const uint64_t t0 = fr_now_ns();
+    for (;;) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+        if (static_cast<int>(v - target) >= 0) break;
+        if (fr_now_ns() - t0 > FR_WAIT_NS) {
+            fr_flag(FR_ST_TIMEOUT | (30u << FR_ST_SITE_SHIFT));
+            break;
+        }
+    }
+    *seen = target;
+}
+
 // Byte position inside a sub-block's 16 activation bytes of value j (0..15),
 // matching the order nv_decode emits: words (j,j+8,j+1,j+9), (j+2,..), ...
 __device__ __forceinline__ int act_perm(int j) {
@@ -429,11 +447,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
         }
     }
     if (p.npeers > 0) {
-        // publish this CTA's rows to every rank: each storing thread fences at
-        // system scope, the consumer warps meet, one thread bumps the flags
-        __threadfence_system();
+        // publish this CTA's rows to every rank: the consumer warps meet (the
+        // barrier orders their stores before thread 0's), then one system-scope
+        // fence and one flag increment per peer
         named_bar(2, CW * 32);
         if (warp == 0 && lane == 0) {
+            __threadfence_system();
             for (int q = 0; q < p.npeers; ++q) {
                 unsigned int *fl = reinterpret_cast<unsigned int *>(p.peer_base[q] + p.flag_off);
                 atomicAdd_system(fl + p.rank, 1u);
@@ -442,32 +461,65 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
     }
 }
 
-// Tensor-parallel completion wait: one warp waits until every rank's flag
-// counter reached the number this rank has consumed so far plus `expect`
-// (the producer kernel's CTA count), then records the new consumed count.
-// Counters only grow, so CUDA-graph replays need no reset.  The wait is
-// bounded (status bit 0, site 30) and never traps.
-__global__ void __launch_bounds__(32) k_tp_wait(const unsigned int *flags, unsigned int *seen, int nranks,
-                                                unsigned int expect) {
+// Tensor-parallel push: copy this rank's [T, cols] block (row stride ld, at
+// column col_off of the buffer at byte offset buf_off) from its own copy into
+// every other rank's copy, then count the CTA into every rank's flag[rank]
+// (same publication protocol as the matvec epilogue).
+__global__ void __launch_bounds__(256) k_tp_push(uint8_t *const *peer_base, int npeers, int rank, int64_t buf_off,
+                                                 int64_t ld, int64_t col_off, int T, int cols, int64_t flag_off) {
     fr_pdl_wait();
-    const int lane = threadIdx.x;
-    if (lane < nranks) {
-        const unsigned int target = seen[lane] + expect;
-        const uint64_t t0 = fr_now_ns();
-        for (;;) {
-            unsigned int v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + lane) : "memory");
-            if (static_cast<int>(v - target) >= 0) break;
-            if (fr_now_ns() - t0 > FR_WAIT_NS) {
-                fr_flag(FR_ST_TIMEOUT | (30u << FR_ST_SITE_SHIFT));
-                break;
-            }
+    const float *src = reinterpret_cast<const float *>(peer_base[rank] + buf_off);
+    const int64_t n = static_cast<int64_t>(T) * cols;
+    const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+    const int64_t lo = blockIdx.x * per, hi = min(n, lo + per);
+    for (int q = 0; q < npeers; ++q) {
+        if (q == rank) continue;
+        float *dst = reinterpret_cast<float *>(peer_base[q] + buf_off);
+        for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            const int64_t t = i / cols, c = i % cols;
+            dst[t * ld + col_off + c] = src[t * ld + col_off + c];
         }
-        seen[lane] = target;
     }
-    __syncwarp();
-    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < npeers; ++q)
+            atomicAdd_system(reinterpret_cast<unsigned int *>(peer_base[q] + flag_off) + rank, 1u);
+    }
     fr_pdl_trigger();
+}
+
+// Tensor-parallel completion wait and reduction: in every CTA, lane r waits
+// until rank r's flag counter reached this CTA's consumed count plus `expect`
+// (the producer kernels' CTA count) and records the new count in the CTA's
+// own row of `seen` (seen[blockIdx.x * 32 + r]; counters only grow, so
+// CUDA-graph replays need no reset).  Then the CTA sums its slice of the
+// ranks' partial outputs in rank order (identical on every rank), adds the
+// residual and writes `out`.  The wait is bounded (status bit 0, site 30).
+//
+// The kernel releases its dependents at once and does not wait for the
+// previous kernel: it may poll while the producing matvec still runs -- all of
+// whose CTAs are resident by then, since a PDL dependent launches only after
+// every CTA of its primary has triggered -- and the kernel after it waits for
+// this one to complete.  The consumed counts are ordered between steps because
+// every later kernel of a step waits for its predecessor's completion.
+__global__ void __launch_bounds__(256) k_tp_reduce(const unsigned int *flags, unsigned int *seen, int nranks,
+                                                   unsigned int expect, const float *parts, int64_t n,
+                                                   const float *resid, int64_t ldr, int64_t width, float *out,
+                                                   int64_t ldo) {
+    fr_pdl_trigger();
+    if (threadIdx.x < static_cast<unsigned>(nranks))
+        tp_flag_wait(flags, seen + blockIdx.x * 32 + threadIdx.x, threadIdx.x, expect);
+    __syncthreads();
+    const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+    const int64_t lo = blockIdx.x * per, hi = min(n, lo + per);
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        float v = parts[i];
+        for (int r = 1; r < nranks; ++r) v += parts[r * n + i];
+        const int64_t t = i / width, c = i % width;
+        if (resid) v += resid[t * ldr + c];
+        out[t * ldo + c] = v;
+    }
 }
 
 } // namespace frb

@@ -1185,20 +1185,19 @@ int fr_moe_combine(const float *part, const float *wts, const float *resid, floa
 // ======================================================================
 namespace frb {
 
-// symmetric buffer layout: [flags1 P | flags2 P | seen1 P | seen2 P] u32, then
-// (256-byte aligned) the GLU copy [T, n_ff] and the output copy [T, n_embd]
+// shared buffer layout: [flags 32] u32, the reduce kernel's per-CTA consumed
+// counts [TP_WAIT_CTAS][32] u32, then (256-byte aligned) the ranks' partial
+// outputs [P][T][n_embd] f32 -- slot r written by rank r
+constexpr int TP_WAIT_CTAS = 32;
 struct TpLayout {
-    int64_t flags1, flags2, seen1, seen2, glu, y, total;
+    int64_t flags, seen, part, total;
 };
-static TpLayout tp_layout(int T, int n_embd, int n_ff, int P) {
+static TpLayout tp_layout(int T, int n_embd, int P) {
     TpLayout l{};
-    l.flags1 = 0;
-    l.flags2 = 4LL * P;
-    l.seen1 = 8LL * P;
-    l.seen2 = 12LL * P;
-    l.glu = (16LL * P + 255) / 256 * 256;
-    l.y = l.glu + (static_cast<int64_t>(T) * n_ff * 4 + 255) / 256 * 256;
-    l.total = l.y + (static_cast<int64_t>(T) * n_embd * 4 + 255) / 256 * 256;
+    l.flags = 0;
+    l.seen = 4LL * 32;
+    l.part = (l.seen + 4LL * 32 * TP_WAIT_CTAS + 255) / 256 * 256;
+    l.total = l.part + static_cast<int64_t>(P) * T * n_embd * 4;
     return l;
 }
 
@@ -1244,7 +1243,7 @@ int fr_ipc_free(void *dev_ptr) { return dev_ptr ? cuda_rc(cudaFree(dev_ptr)) : F
 
 int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks) {
     if (T <= 0 || n_embd <= 0 || n_ff <= 0 || nranks <= 0) return -1;
-    return tp_layout(T, n_embd, n_ff, nranks).total;
+    return tp_layout(T, n_embd, nranks).total;
 }
 
 int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard, const float *sg,
@@ -1254,77 +1253,93 @@ int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, 
     if (fault_hit("fr_tp_ffn_nvfp4")) return FR_EINJECTED;
     if (!x || !wg_shard || !wu_shard || !wd_shard || !out || !peer_base || !local_base) return FR_EINVAL;
     if (T <= 0 || nranks <= 0 || nranks > 32 || rank < 0 || rank >= nranks) return FR_EINVAL;
-    // shard boundaries on q8_1 block (32) boundaries, rows whole NVFP4 blocks
-    if (n_embd % 64 != 0 || n_ff % 64 != 0 || n_embd % (32 * nranks) != 0 || n_ff % (32 * nranks) != 0)
-        return FR_EINVAL;
-    const TpLayout L = tp_layout(T, n_embd, n_ff, nranks);
+    // the n_ff shard boundary falls on NVFP4 block (64) boundaries, so the
+    // GLU's q8_1 blocks and the down rows' NVFP4 blocks never straddle it
+    if (n_embd % 64 != 0 || n_ff % (64 * nranks) != 0) return FR_EINVAL;
+    const TpLayout L = tp_layout(T, n_embd, nranks);
     if (buffer_bytes < L.total) return FR_EINVAL;
     uint8_t *base = static_cast<uint8_t *>(local_base);
-    const int F_p = n_ff / nranks, D_p = n_embd / nranks;
+    uint8_t *const *pb = reinterpret_cast<uint8_t *const *>(peer_base);
+    const int F_p = n_ff / nranks;
     const int64_t ld_gu = static_cast<int64_t>(n_embd) / 64 * NV_BYTES;
-    const int64_t ld_d = static_cast<int64_t>(n_ff) / 64 * NV_BYTES;
-    void *q8x = nullptr, *q8g = nullptr;
-    int rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES, stream, &q8x);
+    const int64_t ld_d = static_cast<int64_t>(F_p) / 64 * NV_BYTES;
+    const int64_t slot_off = L.part + static_cast<int64_t>(rank) * T * n_embd * 4;
+    const unsigned int *flags = reinterpret_cast<const unsigned int *>(base + L.flags);
+    unsigned int *seen = reinterpret_cast<unsigned int *>(base + L.seen);
+    const float *parts = reinterpret_cast<const float *>(base + L.part);
+    const int64_t n_out = static_cast<int64_t>(T) * n_embd;
+    void *glu_p = nullptr;
+    int rc = workspace_get(WS_GLU, static_cast<size_t>(T) * F_p * sizeof(float), stream, &glu_p);
     if (rc != FR_OK) return rc;
-    rc = workspace_get(WS_GLUQ8, static_cast<size_t>(T) * (n_ff / 32) * Q8_BYTES, stream, &q8g);
-    if (rc != FR_OK) return rc;
-    rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
-    if (rc != FR_OK) return rc;
-    // gate/up shard -> every rank's GLU copy, columns [rank*F_p, (rank+1)*F_p)
-    GvParams p{};
-    p.w0 = static_cast<const uint8_t *>(wg_shard);
-    p.w1 = static_cast<const uint8_t *>(wu_shard);
-    p.w_ld = ld_gu;
-    p.q8 = static_cast<const uint8_t *>(q8x);
-    p.ldq = n_embd / 32;
-    p.s0 = sg;
-    p.s1 = su;
-    p.y = nullptr;
-    p.ldy = n_ff;
-    p.N = F_p;
-    p.K = n_embd;
-    p.peer_base = reinterpret_cast<uint8_t *const *>(peer_base);
-    p.npeers = nranks;
-    p.rank = rank;
-    p.peer_off = L.glu;
-    p.flag_off = L.flags1;
-    p.col_off = static_cast<int64_t>(rank) * F_p;
-    rc = gemv_run(p, T, true, stream);
-    if (rc != FR_OK) return rc;
-    const unsigned exp1 = gemv_ctas(F_p, n_embd, ld_gu, T, true);
-    rc = launch_pdl(k_tp_wait, dim3(1), dim3(32), 0, stream, reinterpret_cast<const unsigned int *>(base + L.flags1),
-                    reinterpret_cast<unsigned int *>(base + L.seen1), nranks, exp1);
-    if (rc != FR_OK) return rc;
-    const float *glu = reinterpret_cast<const float *>(base + L.glu);
-    rc = quantize_launch(glu, n_ff, q8g, n_ff / 32, T, n_ff, stream);
-    if (rc != FR_OK) return rc;
-    // down shard -> every rank's output copy, columns [rank*D_p, (rank+1)*D_p)
-    GvParams q{};
-    q.w0 = static_cast<const uint8_t *>(wd_shard);
-    q.w_ld = ld_d;
-    q.q8 = static_cast<const uint8_t *>(q8g);
-    q.ldq = n_ff / 32;
-    q.s0 = sd;
-    q.resid = resid ? resid + static_cast<int64_t>(rank) * D_p : nullptr;
-    q.ldr = n_embd;
-    q.y = nullptr;
-    q.ldy = n_embd;
-    q.N = D_p;
-    q.K = n_ff;
-    q.peer_base = reinterpret_cast<uint8_t *const *>(peer_base);
-    q.npeers = nranks;
-    q.rank = rank;
-    q.peer_off = L.y;
-    q.flag_off = L.flags2;
-    q.col_off = static_cast<int64_t>(rank) * D_p;
-    rc = gemv_run(q, T, false, stream);
-    if (rc != FR_OK) return rc;
-    const unsigned exp2 = gemv_ctas(D_p, n_ff, ld_d, T, false);
-    rc = launch_pdl(k_tp_wait, dim3(1), dim3(32), 0, stream, reinterpret_cast<const unsigned int *>(base + L.flags2),
-                    reinterpret_cast<unsigned int *>(base + L.seen2), nranks, exp2);
-    if (rc != FR_OK) return rc;
-    return cuda_rc(cudaMemcpyAsync(out, base + L.y, static_cast<size_t>(T) * n_embd * 4, cudaMemcpyDeviceToDevice,
-                                   stream));
+    float *glu = static_cast<float *>(glu_p);
+
+    unsigned expect;
+    if (use_tc(wg_shard, wu_shard, ld_gu, n_embd, T) && use_tc(wd_shard, nullptr, ld_d, F_p, T)) {
+        // batches: tensor-core matvecs, the partial output into this rank's
+        // own slot, then a push kernel stores it into every peer's slot
+        constexpr int PUSH_CTAS = 64;
+        rc = tc_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), ld_gu, F_p,
+                       n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
+        if (rc != FR_OK) return rc;
+        rc = tc_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, ld_d, n_embd, F_p, glu, F_p, nullptr, 0, T,
+                       sd, nullptr, nullptr, 0, reinterpret_cast<float *>(base + slot_off), n_embd, false, stream);
+        if (rc != FR_OK) return rc;
+        rc = launch_pdl(k_tp_push, dim3(PUSH_CTAS), dim3(256), 0, stream, pb, nranks, rank, slot_off,
+                        static_cast<int64_t>(n_embd), static_cast<int64_t>(0), T, n_embd, L.flags);
+        if (rc != FR_OK) return rc;
+        expect = PUSH_CTAS;
+    } else {
+        void *q8x = nullptr, *q8g = nullptr;
+        rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES, stream, &q8x);
+        if (rc != FR_OK) return rc;
+        rc = workspace_get(WS_GLUQ8, static_cast<size_t>(T) * (F_p / 32) * Q8_BYTES, stream, &q8g);
+        if (rc != FR_OK) return rc;
+        rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
+        if (rc != FR_OK) return rc;
+        // gate/up: this rank's GLU columns, locally
+        GvParams p{};
+        p.w0 = static_cast<const uint8_t *>(wg_shard);
+        p.w1 = static_cast<const uint8_t *>(wu_shard);
+        p.w_ld = ld_gu;
+        p.q8 = static_cast<const uint8_t *>(q8x);
+        p.ldq = n_embd / 32;
+        p.s0 = sg;
+        p.s1 = su;
+        p.y = glu;
+        p.ldy = F_p;
+        p.N = F_p;
+        p.K = n_embd;
+        rc = gemv_run(p, T, true, stream);
+        if (rc != FR_OK) return rc;
+        rc = quantize_launch(glu, F_p, q8g, F_p / 32, T, F_p, stream);
+        if (rc != FR_OK) return rc;
+        // down over this rank's K range: the partial output of every row goes
+        // into this rank's slot on every rank, then the flags are raised
+        GvParams q{};
+        q.w0 = static_cast<const uint8_t *>(wd_shard);
+        q.w_ld = ld_d;
+        q.q8 = static_cast<const uint8_t *>(q8g);
+        q.ldq = F_p / 32;
+        q.s0 = sd;
+        q.y = nullptr;
+        q.ldy = n_embd;
+        q.N = n_embd;
+        q.K = F_p;
+        q.peer_base = pb;
+        q.npeers = nranks;
+        q.rank = rank;
+        q.peer_off = slot_off;
+        q.flag_off = L.flags;
+        q.col_off = 0;
+        rc = gemv_run(q, T, false, stream);
+        if (rc != FR_OK) return rc;
+        expect = gemv_ctas(n_embd, F_p, ld_d, T, false);
+    }
+    // wait for every rank's partial, sum them in rank order, add the residual.
+    // Always TP_WAIT_CTAS CTAs: each keeps its own consumed count.
+    return launch_pdl(k_tp_reduce, dim3(TP_WAIT_CTAS), dim3(256), 0, stream, flags, seen, nranks, expect, parts,
+                      n_out, resid, static_cast<int64_t>(n_embd), static_cast<int64_t>(n_embd), out,
+                      static_cast<int64_t>(n_embd));
 }
 
 } // extern "C"

@@ -4,11 +4,15 @@ NVLink / NVSwitch) for the exchanges, the library's kernels for the compute.
 The reference runs on one device only (its fusion windows bind to the first
 SM120 device that runs a graph); tensor and expert parallelism are new here.
 
-* Tensor-parallel dense FFN (config 2): rank r owns gate/up rows
-  [r*F/P, (r+1)*F/P) and down rows [r*D/P, (r+1)*D/P).  The GLU shards are
-  all-gathered before the down projection and the output shards after it.
-  q8_1 blocks cover 32 consecutive values and shard boundaries are multiples
-  of 32, so every rank quantizes the gathered GLU exactly as one GPU would.
+* Tensor-parallel dense FFN (config 2), sharded over the FFN width F = n_ff:
+  rank r owns gate/up rows [r*F/P, (r+1)*F/P) and, of every down row, the
+  NVFP4 blocks of columns [r*F/P, (r+1)*F/P).  Each rank computes its GLU
+  columns and the down product over its K range locally; the P partial
+  outputs are summed in rank order (one exchange per layer).  F/P is a
+  multiple of 64, so the GLU's q8_1 blocks are the ones one GPU would make.
+  `TpFfn` runs the step through the library (the partial outputs travel by
+  NVLink peer stores from the down matvec's epilogue); `tp_ffn` is the same
+  sharding over torch.distributed collectives with pluggable kernels.
 * Expert-parallel MoE (config 3): rank r owns experts [r*E/P, (r+1)*E/P) and
   its own tokens.  Routing is computed locally (replicated router weights);
   each routed slot's activation row goes to the expert's owner (all-to-all),
@@ -26,6 +30,8 @@ import torch
 import torch.distributed as dist
 
 import ctypes as C
+
+import numpy as np
 
 from . import (_ptr, _stream, call, gemv_swiglu, lib, moe_combine, moe_experts, moe_route, mul_mat, quantize_q8_1)
 
@@ -59,32 +65,49 @@ def shard_range(n: int, rank: int, world: int):
     return rank * per, (rank + 1) * per
 
 
-def _all_gather_cols(t: torch.Tensor, world: int, group=None) -> torch.Tensor:
-    """[T, n] on every rank -> [T, world*n], shards in rank order."""
-    T, n = t.shape
-    buf = torch.empty((world * T, n), dtype=t.dtype, device=t.device)
-    dist.all_gather_into_tensor(buf, t.contiguous(), group=group)
-    return buf.view(world, T, n).permute(1, 0, 2).reshape(T, world * n)
+def down_shard(wd, n_embd: int, n_ff: int, rank: int, world: int):
+    """The K-shard of the down matrix [n_embd, n_ff/64 blocks of 36 bytes]
+    that rank `rank` holds: blocks [rank*nb, (rank+1)*nb), nb = n_ff/64/world,
+    as a contiguous [n_embd, nb*36] byte matrix (numpy or torch)."""
+    if n_ff % (64 * world):
+        raise ValueError(f"n_ff={n_ff} does not split into whole NVFP4 blocks over {world} ranks")
+    nb = n_ff // 64 // world
+    v = wd.reshape(n_embd, n_ff // 64, 36)[:, rank * nb:(rank + 1) * nb, :]
+    if isinstance(v, torch.Tensor):
+        return v.contiguous().reshape(n_embd, nb * 36)
+    return np.ascontiguousarray(v).reshape(n_embd, nb * 36)
 
 
-def tp_ffn(x, wg_shard, wu_shard, wd_shard, n_embd, n_ff, group=None, kernels=None):
-    """Row-sharded dense SwiGLU FFN; x [T, n_embd] replicated, returns the full
-    output [T, n_embd] on every rank."""
+def _sum_over_ranks(part: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """Sum of every rank's `part`, added in rank order (the same result on
+    every rank)."""
+    buf = torch.empty((world,) + tuple(part.shape), dtype=part.dtype, device=part.device)
+    dist.all_gather_into_tensor(buf.view(world * part.shape[0], *part.shape[1:]), part.contiguous(), group=group)
+    out = buf[0].clone()
+    for r in range(1, world):
+        out += buf[r]
+    return out
+
+
+def tp_ffn(x, wg_shard, wu_shard, wd_kshard, n_embd, n_ff, resid=None, group=None, kernels=None):
+    """FFN sharded over n_ff; x [T, n_embd] replicated, wd_kshard from
+    `down_shard`.  Returns the full output [T, n_embd] on every rank."""
     k = kernels or GpuKernels()
     world = dist.get_world_size(group)
-    glu_shard = k.gate_up(x, wg_shard, wu_shard, n_ff // world, n_embd)
-    glu = _all_gather_cols(glu_shard, world, group)
-    y_shard = k.down(glu, wd_shard, n_embd // world, n_ff)
-    return _all_gather_cols(y_shard, world, group)
+    F_p = n_ff // world
+    glu_shard = k.gate_up(x, wg_shard, wu_shard, F_p, n_embd)
+    part = k.down(glu_shard, wd_kshard, n_embd, F_p)
+    y = _sum_over_ranks(part, world, group)
+    return y if resid is None else y + resid
 
 
 class TpFfn:
-    """Tensor-parallel dense FFN with the all-gathers fused into the matvec
-    epilogues: each rank's gate/up and down matvecs store their output rows
-    straight into every rank's copy over NVLink (CUDA IPC peer mappings, no
-    multicast object) and count finished CTAs into per-rank flags, which a
-    bounded one-warp wait consumes.  No NCCL call on the step; the step is one
-    stream of kernels and is CUDA-graph capturable.
+    """Tensor-parallel dense FFN with the reduction fused into the down
+    matvec's epilogue: each rank's down matvec stores its partial output rows
+    straight into its slot on every rank over NVLink (CUDA IPC peer mappings,
+    no multicast object) and counts finished CTAs into per-rank flags; a
+    bounded wait kernel sums the slots in rank order.  No NCCL call on the
+    step; the step is one stream of kernels and is CUDA-graph capturable.
 
     `max_tokens` sizes the shared buffer; every call must use the same token
     count on all ranks (ranks advance in lock step)."""
@@ -119,7 +142,7 @@ class TpFfn:
         self.peer_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=torch.cuda.current_device())
         dist.barrier(group=group)
 
-    def __call__(self, x, wg_shard, wu_shard, wd_shard, sg=None, su=None, sd=None, resid=None, out=None,
+    def __call__(self, x, wg_shard, wu_shard, wd_kshard, sg=None, su=None, sd=None, resid=None, out=None,
                  stream=None):
         import torch
         T = x.shape[0]
@@ -127,7 +150,7 @@ class TpFfn:
             raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
         if out is None:
             out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
-        call("fr_tp_ffn_nvfp4", _ptr(x), _ptr(wg_shard), _ptr(wu_shard), _ptr(wd_shard), _ptr(sg), _ptr(su),
+        call("fr_tp_ffn_nvfp4", _ptr(x), _ptr(wg_shard), _ptr(wu_shard), _ptr(wd_kshard), _ptr(sg), _ptr(su),
              _ptr(sd), _ptr(resid), _ptr(out), T, self.n_embd, self.n_ff, self.world, self.rank,
              _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes, _stream(stream))
         return out

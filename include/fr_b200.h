@@ -207,18 +207,20 @@ int fr_moe_combine(const float *part, const float *wts, const float *resid, floa
                    int T, int n_used, int n_embd, cudaStream_t stream);
 
 /* ------------------------------------------------------ (e) tensor parallel
- * One rank's step of the row-sharded dense FFN with the all-gathers fused
- * into the matvec epilogues over NVLink peer stores.  Rank r holds gate/up
- * rows [r*F/P, (r+1)*F/P) and down rows [r*D/P, (r+1)*D/P) (F = n_ff,
- * D = n_embd, P = nranks).  Its gate/up matvec stores its GLU columns into
- * every rank's GLU copy and counts its finished CTAs into every rank's flags;
- * after a bounded wait for all ranks' flags each rank quantizes the full GLU,
- * its down matvec stores its output columns into every rank's output copy,
- * and after a second wait the full output is copied to `out` on every rank.
- * peer_base is a device array of the P ranks' base addresses of one
- * symmetric buffer of fr_tp_buffer_bytes(T, n_embd, n_ff, P) bytes, zeroed
- * once before first use; local_base is this rank's own base.  The reference
- * is single-device; no counterpart. */
+ * One rank's step of the dense FFN sharded over n_ff (P = nranks ranks, shard
+ * F_p = n_ff / P): rank r holds gate/up rows [r*F_p, (r+1)*F_p) and, of every
+ * down row, the NVFP4 blocks of columns [r*F_p, (r+1)*F_p) (wd_shard is
+ * [n_embd rows][F_p/64 blocks], rows F_p/64*36 bytes apart).  Each rank
+ * computes its GLU columns and its partial down output locally; the down
+ * matvec's epilogue stores the partial rows into this rank's slot of every
+ * rank's partial array over NVLink and counts its CTAs into every rank's
+ * flags; a bounded wait then sums the P partials in rank order (the same
+ * order on every rank), adds `resid` and writes `out` [T, n_embd] on every
+ * rank.  n_ff % (64 * P) == 0, so no q8_1 or NVFP4 block straddles a shard.
+ * peer_base is a device array of the P ranks' base addresses of one shared
+ * buffer of fr_tp_buffer_bytes(T, n_embd, n_ff, P) bytes, zeroed once before
+ * first use; local_base is this rank's own base.  All ranks call with the
+ * same T.  The reference is single-device; no counterpart. */
 int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks);
 int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard,
                     const float *sg, const float *su, const float *sd, const float *resid, float *out,

@@ -1,7 +1,8 @@
 """Multi-rank exchange logic of frb200.parallel on CPU: world_size 2 over gloo,
-with the CPU oracle standing in for the kernels.  Tensor-parallel FFN and
-expert-parallel MoE must give exactly the single-rank result (same arithmetic
-per row and per slot, combine in slot order)."""
+with the CPU oracle standing in for the kernels.  Expert-parallel MoE must give
+exactly the single-rank result (same arithmetic per slot, combine in slot
+order); the n_ff-sharded FFN gives the same result on every rank and the
+single-rank result up to the f32 rounding of the partial sums."""
 import os
 import socket
 
@@ -92,9 +93,9 @@ def _worker(rank, port, q):
         # --- tensor parallel: first expert's matrices as a dense FFN
         wg, wu, wd = d["wg"][:nf], d["wu"][:nf], d["wd"][:ne]
         f0, f1 = P.shard_range(nf, rank, WORLD)
-        e0, e1 = P.shard_range(ne, rank, WORLD)
         x = d["x"][:2]
-        y_tp = P.tp_ffn(x, wg[f0:f1], wu[f0:f1], wd[e0:e1], ne, nf, kernels=K)
+        y_tp = P.tp_ffn(x, wg[f0:f1], wu[f0:f1], P.down_shard(wd, ne, nf, rank, WORLD), ne, nf, resid=d["r"][:2],
+                        kernels=K)
         # --- expert parallel: this rank's tokens, this rank's experts
         T = d["T"]
         xs = d["x"][rank * T:(rank + 1) * T]
@@ -118,7 +119,7 @@ def _reference(O):
     ne, nf, E, n_used, T = d["n_embd"], d["n_ff"], d["E"], d["n_used"], d["T"]
     x = d["x"][:2]
     glu = K.gate_up(x, d["wg"][:nf], d["wu"][:nf], nf, ne)
-    y_tp = K.down(glu, d["wd"][:ne], ne, nf)
+    y_tp = K.down(glu, d["wd"][:ne], ne, nf) + d["r"][:2]
     outs = []
     for rank in range(WORLD):
         xs = d["x"][rank * T:(rank + 1) * T]
@@ -146,8 +147,11 @@ def test_tp_ffn_and_ep_moe_match_single_rank(O, fr):
         p.join(timeout=60)
         assert p.exitcode == 0
     ref_tp, ref_ep = _reference(O)
+    # TP: the ranks agree exactly; the rank-order sum of the K-range partials
+    # matches the single-rank product to f32 rounding
+    np.testing.assert_array_equal(res[0][0], res[1][0])
+    np.testing.assert_allclose(res[0][0], ref_tp, rtol=1e-5, atol=1e-5)
     for rank in range(WORLD):
-        np.testing.assert_array_equal(res[rank][0], ref_tp)
         np.testing.assert_array_equal(res[rank][1], ref_ep[rank])
 
 
@@ -156,3 +160,17 @@ def test_shard_range():
     assert shard_range(14336, 3, 8) == (5376, 7168)
     with pytest.raises(ValueError):
         shard_range(100, 0, 8)
+
+
+def test_down_shard_blocks():
+    """The K-shards of a down matrix, put side by side, are the matrix."""
+    import frb200
+    from frb200.parallel import down_shard
+    ne, nf, world = 8, 512, 4
+    wd = frb200.synth_nvfp4(3, ne, nf)
+    parts = [down_shard(wd, ne, nf, r, world).reshape(ne, -1, 36) for r in range(world)]
+    np.testing.assert_array_equal(np.concatenate(parts, axis=1).reshape(ne, -1), wd)
+    wt = torch.from_numpy(wd)
+    np.testing.assert_array_equal(down_shard(wt, ne, nf, 1, world).numpy(), down_shard(wd, ne, nf, 1, world))
+    with pytest.raises(ValueError):
+        down_shard(wd, ne, nf, 0, 3)

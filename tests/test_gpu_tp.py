@@ -1,9 +1,13 @@
-"""Tensor-parallel dense FFN with the all-gathers fused into the matvec
-epilogues (fr_tp_ffn_nvfp4, frb200.parallel.TpFfn): every rank's output must
-equal, bit for bit, the single-GPU FFN on the unsharded weights (each output
-row is the same dot product in the same order; q8_1 blocks never straddle a
-shard boundary).  Runs one rank per visible GPU, at most 2 (world 1 on a
-one-GPU box exercises the same peer-store and flag code with one peer)."""
+"""Tensor-parallel dense FFN sharded over n_ff with the reduction fused into
+the down matvec's epilogue (fr_tp_ffn_nvfp4, frb200.parallel.TpFfn).  Every
+rank must produce the same output, and it must match the single-GPU FFN on
+the unsharded weights: the GLU bit for bit (the same dot products; q8_1 blocks
+never straddle a shard), the output up to the f32 rounding of summing the
+ranks' K-range partials (max |d| <= 1e-5 * max|ref| on the dp4a matvec;
+normwise 1e-4 on the tensor-core matvec, whose split-K order differs too).
+Runs one rank per visible GPU, at most 2 (world 1 on a one-GPU box exercises
+the same peer-store, flag and reduce code with one peer), including CUDA-graph
+replays with new inputs."""
 import os
 import socket
 
@@ -36,30 +40,45 @@ def _worker(rank, world, port, q):
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
-    tp = None
+    tps = []
+    bad, sums = [], []
     try:
-        frb200.set_matvec_path(1)
         ne, nf = 1024, 2048
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
         wg = t(frb200.synth_nvfp4(41, nf, ne))
         wu = t(frb200.synth_nvfp4(42, nf, ne))
         wd = t(frb200.synth_nvfp4(43, ne, nf))
         f0, f1 = P.shard_range(nf, rank, world)
-        e0, e1 = P.shard_range(ne, rank, world)
-        shards = (wg[f0:f1].contiguous(), wu[f0:f1].contiguous(), wd[e0:e1].contiguous())
+        shards = (wg[f0:f1].contiguous(), wu[f0:f1].contiguous(), P.down_shard(wd, ne, nf, rank, world))
         sc = t(np.array([0.75, 1.25, 0.5], np.float32))
-        tp = P.TpFfn(8, ne, nf)
-        bad = []
-        for i, T in enumerate((1, 3, 8, 1, 2)):
-            x = t(frb200.synth_normal(50 + i, T * ne).reshape(T, ne))
-            r = t(frb200.synth_normal(60 + i, T * ne).reshape(T, ne)) if i % 2 else None
-            kw = dict(sg=sc[0:1], su=sc[1:2], sd=sc[2:3]) if i == 2 else {}
-            y = tp(x, *shards, resid=r, **kw)
-            ref = frb200.ffn(x, wg, wu, wd, ne, nf, resid=r, **kw)
+
+        def check(y, ref, what, tc):
             torch.cuda.synchronize()
-            if not torch.equal(y, ref):
-                bad.append(f"T={T}: max |d| {float((y - ref).abs().max()):.3e}")
+            sums.append(float(y.double().sum()))
+            if not bool(torch.isfinite(y).all()):
+                bad.append(f"{what}: non-finite")
+            elif tc:
+                nerr = float((y - ref).double().norm() / ref.double().norm())
+                if nerr > 1e-4:
+                    bad.append(f"{what}: norm err {nerr:.3e}")
+            else:
+                err = float((y - ref).abs().max() / ref.abs().max())
+                if err > 1e-5:
+                    bad.append(f"{what}: max err {err:.3e}")
+
+        for path, Ts in ((1, (1, 3, 8, 1, 2, 12)), (2, (3, 16, 64))):
+            frb200.set_matvec_path(path)
+            tp = P.TpFfn(max(Ts), ne, nf)
+            tps.append(tp)
+            for i, T in enumerate(Ts):
+                x = t(frb200.synth_normal(50 + i, T * ne).reshape(T, ne))
+                r = t(frb200.synth_normal(60 + i, T * ne).reshape(T, ne)) if i % 2 else None
+                kw = dict(sg=sc[0:1], su=sc[1:2], sd=sc[2:3]) if i == 2 else {}
+                y = tp(x, *shards, resid=r, **kw)
+                check(y, frb200.ffn(x, wg, wu, wd, ne, nf, resid=r, **kw), f"path {path} T={T}", path == 2)
         # the step captured in a CUDA graph and replayed with new inputs
+        frb200.set_matvec_path(0)
+        tp = tps[0]
         xg = torch.empty((2, ne), dtype=torch.float32, device=dev)
         yg = torch.empty((2, ne), dtype=torch.float32, device=dev)
         s = torch.cuda.Stream(dev)
@@ -73,24 +92,20 @@ def _worker(rank, world, port, q):
             xi = t(frb200.synth_normal(80 + i, 2 * ne).reshape(2, ne))
             xg.copy_(xi)
             g.replay()
-            torch.cuda.synchronize()
-            ref = frb200.ffn(xi, wg, wu, wd, ne, nf)
-            torch.cuda.synchronize()
-            if not torch.equal(yg, ref):
-                bad.append(f"graph replay {i}: max |d| {float((yg - ref).abs().max()):.3e}")
+            check(yg, frb200.ffn(xi, wg, wu, wd, ne, nf), f"graph replay {i}", False)
         del g
-        status = frb200.device_status()
-        q.put((rank, bad, status))
+        torch.cuda.synchronize()
+        q.put((rank, bad, frb200.device_status(), sums))
     except Exception as e:  # noqa: BLE001 - report to the parent instead of hanging it
-        q.put((rank, [repr(e)], -1))
+        q.put((rank, bad + [repr(e)], -1, sums))
         raise
     finally:
-        if tp is not None:
+        for tp in tps:
             tp.close()
         dist.destroy_process_group()
 
 
-def test_tp_ffn_fused_epilogue_matches_single_gpu():
+def test_tp_ffn_fused_reduce_matches_single_gpu():
     import torch
     world = min(2, torch.cuda.device_count())
     ctx = mp.get_context("spawn")
@@ -101,13 +116,14 @@ def test_tp_ffn_fused_epilogue_matches_single_gpu():
         p.start()
     res = {}
     for _ in range(world):
-        rank, bad, status = q.get(timeout=300)
-        res[rank] = (bad, status)
+        rank, bad, status, sums = q.get(timeout=300)
+        res[rank] = (bad, status, sums)
     for p in procs:
         p.join(timeout=60)
     for rank in range(world):
-        bad, status = res[rank]
+        bad, status, sums = res[rank]
         assert not bad, f"rank {rank}: {bad}"
         assert status == 0, f"rank {rank}: device status {status:#x}"
+        assert sums == res[0][2], "ranks disagree"
     for p in procs:
         assert p.exitcode == 0
