@@ -378,6 +378,41 @@ def run_ours(args):
         pg.destroy_process_group()
 
 
+def run_profile_case(args):
+    """A short, fixed sequence of the hot kernels for profiler captures: four
+    rotating weight sets (> L2) of config 2, `--steps` dense FFN steps at
+    T = --tokens (the q8_1 / activation-column kernel, the gate/up SwiGLU
+    matvec, the down matvec), synchronised after each step.  Prints nothing
+    but a done line; never a benchmark number."""
+    import torch
+    import frb200
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.matvec is not None:
+        frb200.set_matvec_path(args.matvec)
+    sets = []
+    for s in range(N_SETS):
+        base = 0x5EED0000 + 100 * s
+        sets.append(tuple(torch.from_numpy(w).to(dev) for w in (frb200.synth_nvfp4(base + 1, N_FF, N_EMBD),
+                                                                 frb200.synth_nvfp4(base + 2, N_FF, N_EMBD),
+                                                                 frb200.synth_nvfp4(base + 3, N_EMBD, N_FF))))
+    if args.layout == "tiled":
+        sets = [(frb200.tile_nvfp4(wg, N_FF, N_EMBD), frb200.tile_nvfp4(wu, N_FF, N_EMBD),
+                 frb200.tile_nvfp4(wd, N_EMBD, N_FF)) for wg, wu, wd in sets]
+        torch.cuda.synchronize()
+    T = args.tokens
+    x = torch.from_numpy(frb200.synth_normal(0x5EED0000 + 10, T * N_EMBD).reshape(T, N_EMBD)).to(dev)
+    out = torch.empty((T, N_EMBD), dtype=torch.float32, device=dev)
+    for i in range(args.steps):
+        wg, wu, wd = sets[i % N_SETS]
+        if args.layout == "tiled":
+            frb200.ffn_tiled(x, wg, wu, wd, N_EMBD, N_FF, out=out)
+        else:
+            frb200.ffn(x, wg, wu, wd, N_EMBD, N_FF, out=out)
+        torch.cuda.synchronize()
+    print(f"profile case done: {args.steps} FFN steps, T={T}, status {frb200.device_status()}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -385,8 +420,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="run a short fixed kernel sequence for profiler captures (no benchmark line)")
+    ap.add_argument("--tokens", type=int, default=1, help="tokens per step of --profile-case")
+    ap.add_argument("--matvec", type=int, default=None, help="force the matvec kernel (1 dp4a, 2 tc-f16, 3 tc-fp4)")
+    ap.add_argument("--layout", choices=["ggml", "tiled"], default="ggml", help="weight layout of --profile-case")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -1,0 +1,351 @@
+// fr_fp4tile.cuh -- the FP4 tensor-core matvec on tile-major weights.
+//
+// Tile-major NVFP4 ("tiled") layout.  A one-time repack (k_tile_nvfp4, in the
+// spirit of the reference's load-time repack_weight for its tensor-core path,
+// src/fr_repack.cu:1-13) rewrites a ggml block_nvfp4 matrix [N, K] as tiles
+// of 128 rows x 256 values, tile (rb, kq) at ((rb * n_kq) + kq) * 18432 bytes:
+//   * 16384 B of codes, 128-byte-swizzled K-major: row r at r * 128, its
+//     16-byte unit c (block c >> 1 of the tile, half c & 1 of that block's 32
+//     code bytes) at ((c ^ (r & 7)) << 4); bytes keep ggml's order (byte j of
+//     a sub-block = values j, j+8), which the activation columns share;
+//   * 2048 B of scale atoms, block j of the tile at 16384 + 512 j, row r's
+//     four sub-block scales at (r & 31) * 16 + (r >> 5) * 4, with ggml's
+//     reading applied (sign bit dropped, 0x7F -> 0).
+// Rows past N and blocks past K are zero.  The byte count equals ggml's when
+// N % 128 == 0 and K % 256 == 0.
+//
+// Because a tile is one contiguous 18 KB block and a row block's tiles follow
+// each other along K, every CTA streams one contiguous byte range per matrix
+// with 1-D bulk copies that land MMA-ready in shared memory: no per-value
+// work on the SMs at all.  Work split: stream-K -- the (row block, K stage)
+// units are divided evenly over the CTAs in row-block-major order; a CTA
+// finishes each row block it touches; when several CTAs share a row block,
+// each writes its partial sums and the last to arrive adds them in CTA order
+// (deterministic) and applies the epilogue.  Arithmetic: as k_fp4mv (exact
+// products, fp32 accumulation, activation as six E2M1 digit columns).
+#pragma once
+
+#include "fr_fp4mv.cuh"
+
+namespace frb {
+
+constexpr int FT_TILE = 18432;                 // bytes per 128 x 256 tile
+constexpr int FT_CODES = 16384;
+
+// ------------------------------------------------------------ repack
+// one thread per (row, 64-block) of the padded matrix
+__global__ void __launch_bounds__(256) k_tile_nvfp4(const uint8_t *__restrict__ src, int64_t w_ld, int N, int K,
+                                                    int n_kq, uint8_t *__restrict__ dst, int64_t total) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    const int64_t id = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (id >= total) return;
+    const int nkb_p = n_kq * 4;                          // padded blocks per row
+    const int64_t row = id / nkb_p;
+    const int kb = static_cast<int>(id % nkb_p);
+    uint32_t w[9];
+    if (row < N && kb < K / 64) {
+        const uint8_t *b = src + row * w_ld + static_cast<int64_t>(kb) * NV_BYTES;
+#pragma unroll
+        for (int i = 0; i < 9; ++i) w[i] = *reinterpret_cast<const uint32_t *>(b + 4 * i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 9; ++i) w[i] = 0u;
+    }
+    uint32_t sv = w[0] & 0x7F7F7F7Fu;
+    const uint32_t nan = (sv + 0x01010101u) & 0x80808080u;
+    sv &= ~((nan >> 7) * 0xFFu);
+    const int64_t rb = row >> 7;
+    const int r = static_cast<int>(row & 127);
+    const int kq = kb >> 2, j = kb & 3;
+    uint8_t *tile = dst + (rb * n_kq + kq) * FT_TILE;
+    uint8_t *a = tile + r * 128;
+    const int sw = r & 7;
+    *reinterpret_cast<uint4 *>(a + (((2 * j) ^ sw) << 4)) = make_uint4(w[1], w[2], w[3], w[4]);
+    *reinterpret_cast<uint4 *>(a + (((2 * j + 1) ^ sw) << 4)) = make_uint4(w[5], w[6], w[7], w[8]);
+    *reinterpret_cast<uint32_t *>(tile + FT_CODES + j * 512 + (r & 31) * 16 + (r >> 5) * 4) = sv;
+}
+
+// ------------------------------------------------------------ matvec
+struct FtArgs {
+    int N, K, T;                 // rows, row length, tokens in this launch (8T <= NCOL)
+    int t0;                      // first output token index
+    int n_kq;                    // K stages of 256 (tiles per row block)
+    int n_units;                 // row blocks x (n_kq / NT)
+    int maxp;                    // partial slots per row block
+    const uint8_t *w0, *w1;      // tiled matrices
+    const uint8_t *bimg;         // activation columns (k_act_fp4) [n_kq][NCOL x 128 B]
+    const float *gtab;           // column factors (k_act_fp4) [T][8]
+    const float *s0, *s1;        // per-tensor scales (nullable)
+    const float *resid;          // [.., ldr] (nullable)
+    int64_t ldr;
+    float *y;                    // [.., ldy]
+    int64_t ldy;
+    float *part;                 // partials [row blocks][maxp][2][TMAX][128]
+    unsigned int *counter;       // [row blocks][4 quadrants], zero on entry, reset by the last arrival
+    int n_w, n_b;                // ring depths: weight stages, activation stages
+};
+
+// A pipeline stage is two 18 KB weight tiles -- the gate and up tiles of one
+// K stage (SwiGLU, NT = 1), or two consecutive K stages of one matrix
+// (NT = 2) -- so that every step of the rings moves ~37 KB: each step costs
+// a fixed hand-off latency (barrier wake-up, MMA issue) of about half a
+// microsecond, and 18 KB steps would halve the stream rate.  Each tile has
+// its own MMA issuer and TMEM accumulator.
+template <int NCOL, int EPI, int NT>
+struct FtShape {
+    static constexpr int NM = EPI == FM_SWIGLU ? 2 : 1;
+    static_assert(NM * NT <= 2, "at most two tiles per stage");
+    static constexpr int NI = NM * NT;                             // tiles (issuers, accumulators) per stage
+    static constexpr int WST = NI * FT_TILE;                       // weight stage
+    static constexpr int B_BYTES = NCOL * 128;                     // activation tile (columns only)
+    static constexpr int BST = NT * B_BYTES;                       // activation stage
+    static constexpr int TMAX = NCOL / FM_DIGITS;
+    // weight producer, two MMA issuers, four epilogue warps, activation producer
+    static constexpr int THREADS = 8 * 32;
+};
+
+// first unit of CTA c when U units go to G CTAs, and the CTA owning unit u
+__device__ __forceinline__ int ft_lo(int c, int U, int G) {
+    return static_cast<int>((static_cast<int64_t>(c) * U) / G);
+}
+__device__ __forceinline__ int ft_owner(int u, int U, int G) {
+    return static_cast<int>(((static_cast<int64_t>(u) + 1) * G - 1) / U);
+}
+
+template <int NCOL, int EPI, int NT>
+__global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(const FtArgs g) {
+    using S = FtShape<NCOL, EPI, NT>;
+    constexpr int NI = S::NI;
+    constexpr bool DUAL = S::NM == 2;
+    constexpr int TMAX = S::TMAX;
+    constexpr uint32_t TMEM_COLS = 512;
+    static_assert(NI * NCOL <= 256, "accumulators live in TMEM columns [0, 256)");
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int NW = g.n_w, NB = g.n_b;
+    uint8_t *w_ring = smem;
+    uint8_t *b_ring = w_ring + static_cast<size_t>(NW) * S::WST;
+    uint8_t *sfb_const = b_ring + static_cast<size_t>(NB) * S::BST;   // 512 B: the activation scale atom
+    float *gtab = reinterpret_cast<float *>(sfb_const + 512);             // [TMAX][8] column factors
+    uint64_t *wfull = reinterpret_cast<uint64_t *>(gtab + TMAX * FM_GSTRIDE);
+    uint64_t *wempty = wfull + NW;
+    uint64_t *bfull = wempty + NW;
+    uint64_t *bempty = bfull + NB;
+    uint64_t *accfull = bempty + NB;
+    uint64_t *accempty = accfull + 1;
+    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(accempty + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, U = g.n_units;
+    const int nsr = g.n_kq / NT;                             // stages per row block
+    const int u_lo = ft_lo(blockIdx.x, U, G), u_hi = ft_lo(blockIdx.x + 1, U, G);
+    const int n_st = u_hi - u_lo;
+    const int T = g.T;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NW; ++s) {
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], NI);
+        }
+        for (int s = 0; s < NB; ++s) {
+            mbar_init(&bfull[s], 1);
+            mbar_init(&bempty[s], NI);
+        }
+        mbar_init(accfull, NI);
+        mbar_init(accempty, 4);
+        fence_mbar_init();
+    }
+    if (warp == 3) {
+        // every activation column has scale 1.0
+        reinterpret_cast<uint4 *>(sfb_const)[lane] = make_uint4(FM_SFB * 0x01010101u, FM_SFB * 0x01010101u,
+                                                                FM_SFB * 0x01010101u, FM_SFB * 0x01010101u);
+        fence_proxy_async();
+    }
+    if (warp == 1) tmem_alloc(tmem_s, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_s;
+    const uint32_t tD = tbase;                               // tile k's accumulator: + k * NCOL
+    fr_pdl_trigger();
+
+    if (warp == 0) {
+        // ---------------- weight producer: contiguous tiles, no PDL wait
+        if (lane == 0) {
+            for (int i = 0; i < n_st; ++i) {
+                const int s = i % NW;
+                if (i >= NW && !mbar_wait(&wempty[s], ((i / NW) - 1) & 1, 50)) break;
+                uint8_t *st = w_ring + static_cast<size_t>(s) * S::WST;
+                const int u = u_lo + i;
+                // first tile of the stage: row block u / nsr, K stage (u % nsr) * NT
+                const int64_t off = (static_cast<int64_t>(u / nsr) * g.n_kq + (u % nsr) * NT) * FT_TILE;
+                mbar_expect_tx(&wfull[s], S::WST);
+                bulk_g2s(st, g.w0 + off, NT * FT_TILE, &wfull[s]);
+                if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &wfull[s]);
+            }
+        }
+    } else if (warp == 7) {
+        // ---------------- activation producer (after the PDL wait)
+        if (lane == 0) {
+            fr_pdl_wait();
+            for (int i = 0; i < n_st; ++i) {
+                const int s = i % NB;
+                if (i >= NB && !mbar_wait(&bempty[s], ((i / NB) - 1) & 1, 51)) break;
+                const int kq0 = ((u_lo + i) % nsr) * NT;
+                mbar_expect_tx(&bfull[s], S::BST);
+                bulk_g2s(b_ring + static_cast<size_t>(s) * S::BST, g.bimg + static_cast<int64_t>(kq0) * S::B_BYTES,
+                         S::BST, &bfull[s]);
+            }
+        }
+    } else if (warp == 1 || (NI == 2 && warp == 2)) {
+        // ---------------- MMA issuers: one thread per tile of the stage
+        if (lane == 0) {
+            const int k = warp - 1;
+            const uint32_t idesc = idesc_nvf4(128, NCOL);
+            // scale columns: [256, 256 + 16 NI NW) weights by ring slot and
+            // tile, then four per issuer for the constant activation atom
+            const uint32_t t_sfb = tbase + 256 + NW * 16 * NI + 4 * k;
+            tc_cp_sf(t_sfb, sdesc_plain(smem_u32(sfb_const), 128));
+            int seg = 0;
+            for (int i = 0; i < n_st; ++i) {
+                const int u = u_lo + i;
+                const bool first = i == 0 || u % nsr == 0;       // first stage of a row-block segment
+                const bool last = i == n_st - 1 || (u + 1) % nsr == 0;
+                if (first && seg > 0 && !mbar_wait(accempty, (seg - 1) & 1, 52)) break;
+                const int sw = i % NW, sb = i % NB;
+                if (!mbar_wait(&wfull[sw], (i / NW) & 1, 53)) break;
+                if (!mbar_wait(&bfull[sb], (i / NB) & 1, 54)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + k * FT_TILE;
+                const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sb) * S::BST) + (NT == 2 ? k : 0) * S::B_BYTES;
+                const uint32_t t_sfa = tbase + 256 + (sw * NI + k) * 16;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) tc_cp_sf(t_sfa + 4 * j, sdesc_plain(a_addr + FT_CODES + 512 * j, 128));
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    tc_mma_nvf4(tD + k * NCOL, sdesc_sw128(a_addr + 32 * j), sdesc_sw128(b_addr + 32 * j), idesc,
+                                t_sfa + 4 * j, t_sfb, (!first || j > 0) ? 1u : 0u);
+                tc_commit(&wempty[sw]);
+                tc_commit(&bempty[sb]);
+                if (last) {
+                    tc_commit(accfull);
+                    ++seg;
+                }
+            }
+        }
+    } else if (warp >= 3 && warp <= 6) {
+        // ---------------- epilogue warps (3..6), one TMEM lane quadrant each
+        const int q = warp & 3;
+        const int at = threadIdx.x - 96;                  // 0..127
+        const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+        const int erow = 32 * q + lane;
+        fr_pdl_wait();
+        if (at < TMAX * FM_GSTRIDE) gtab[at] = at / FM_GSTRIDE < T ? g.gtab[at] : 0.0f;
+        named_bar(1, 128);
+        const float sc0 = g.s0 ? *g.s0 : 1.0f;
+        const float sc1 = (DUAL && g.s1) ? *g.s1 : 1.0f;
+
+        auto finish = [&](int rb, int t, float a0, float a1) {
+            const int n = rb * 128 + erow;
+            if (n >= g.N || t >= T) return;
+            const int64_t tt = g.t0 + t;
+            float val;
+            if (DUAL) {
+                float result = a1;
+                result *= sc1;
+                float gate = a0;
+                gate *= sc0;
+                result *= silu_f(gate);
+                val = result;
+            } else {
+                val = a0 * sc0;
+                if (g.resid) val += g.resid[tt * g.ldr + n];
+            }
+            g.y[tt * g.ldy + n] = val;
+        };
+        // every row-block segment: drain the accumulators, then either finish
+        // the rows or publish the partial; the last of the CTAs sharing a row
+        // block adds the partials in CTA order (per quadrant, so a warp that
+        // timed out cannot hold the others)
+        int seg = 0;
+        for (int s0u = u_lo; s0u < u_hi; ++seg) {
+            const int rb = s0u / nsr;
+            const int s1u = min(u_hi, (rb + 1) * nsr);
+            if (!mbar_wait(accfull, seg & 1, 55)) break;
+            tc_fence_after();
+            float acc0[TMAX], acc1[TMAX];
+#pragma unroll
+            for (int t = 0; t < TMAX; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
+#pragma unroll
+            for (int c = 0; c < NCOL; c += 16) {
+                uint32_t d0[16], d1[16];
+                tmem_ld16(tD + lane_off + c, d0);
+                if (NI == 2) tmem_ld16(tD + NCOL + lane_off + c, d1);
+#pragma unroll
+                for (int v = 0; v < 16; ++v) {
+                    const int col = c + v, t = col / FM_DIGITS;
+                    if (t < TMAX) {
+                        const float gf = gtab[col];
+                        acc0[t] = fmaf(gf, __uint_as_float(d0[v]), acc0[t]);
+                        if (NI == 2) acc1[t] = fmaf(gf, __uint_as_float(d1[v]), acc1[t]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(accempty);        // the accumulators may be overwritten now
+            if (!DUAL && NI == 2) {
+                // two K stages per step: the two accumulators are two halves of the sum
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) {
+                    acc0[t] += acc1[t];
+                    acc1[t] = 0.0f;
+                }
+            }
+            if (s0u == rb * nsr && s1u == (rb + 1) * nsr) {
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) finish(rb, t, acc0[t], acc1[t]);
+            } else {
+                const int c_first = ft_owner(rb * nsr, U, G);
+                const int nparts = ft_owner((rb + 1) * nsr - 1, U, G) - c_first + 1;
+                const int slot = static_cast<int>(blockIdx.x) - c_first;
+                float *pp = g.part + ((static_cast<int64_t>(rb) * g.maxp + slot) * 2) * TMAX * 128;
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) {
+                    pp[t * 128 + erow] = acc0[t];
+                    if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
+                }
+                __threadfence();
+                __syncwarp();
+                unsigned prev = 0;
+                if (lane == 0) prev = atomicAdd(&g.counter[rb * 4 + q], 1u);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == static_cast<unsigned>(nparts - 1)) {
+                    __threadfence();
+                    const float *pb = g.part + (static_cast<int64_t>(rb) * g.maxp * 2) * TMAX * 128;
+#pragma unroll 1
+                    for (int t = 0; t < TMAX && t < T; ++t) {
+                        float a0 = 0.0f, a1 = 0.0f;
+                        for (int k2 = 0; k2 < nparts; ++k2) {
+                            a0 += __ldcg(pb + (k2 * 2) * TMAX * 128 + t * 128 + erow);
+                            if (DUAL) a1 += __ldcg(pb + (k2 * 2 + 1) * TMAX * 128 + t * 128 + erow);
+                        }
+                        finish(rb, t, a0, a1);
+                    }
+                    if (lane == 0) g.counter[rb * 4 + q] = 0;
+                }
+            }
+            s0u = s1u;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, TMEM_COLS);
+    }
+}
+
+} // namespace frb

@@ -12,6 +12,8 @@
 #include "fr_moe.cuh"
 #include "fr_w4a4.cuh"
 #include "fr_tcgemv.cuh"
+#include "fr_fp4mv.cuh"
+#include "fr_fp4tile.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -23,14 +25,36 @@ static bool tc_shape_ok(const void *w0, const void *w1, int64_t w_ld, int K);
 static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, int K, const float *x, int64_t ldx,
                      const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
                      int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream);
-// Tensor-core kernel for batches (T >= 3: it costs the same for T = 1..64),
-// dp4a kernel for T <= 2 and for shapes the TMA path cannot take; the path
-// can be forced either way.
-static bool use_tc(const void *w0, const void *w1, int64_t w_ld, int K, int T) {
+static int fp4_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, int K, const float *x, int64_t ldx,
+                      const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
+                      int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream);
+static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const float *x, int64_t ldx,
+                       const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
+                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream);
+constexpr int FP4_MAX_T = 16;                      // tokens per launch of the FP4 tensor-core matvecs
+// Which matvec runs on weights in ggml's layout: the dp4a kernel for up to two
+// tokens and for shapes the TMA paths cannot take, the f16 tensor-core kernel
+// for batches; the FP4 tensor-core kernel on ggml's layout (TMA boxes of row
+// segments, slower than the tiled layout's contiguous stream) when forced.
+// The path can be forced (FR_MATVEC / fr_set_matvec_path).
+enum MvKind : int { MV_DP4A = 0, MV_TC16 = 1, MV_FP4 = 2 };
+static MvKind mv_kind(const void *w0, const void *w1, int64_t w_ld, int K, int T) {
     const int path = matvec_path();
-    if (path == 1) return false;
-    if (path == 0 && T <= 2) return false;
-    return tc_shape_ok(w0, w1, w_ld, K);
+    if (path == 1 || !tc_shape_ok(w0, w1, w_ld, K)) return MV_DP4A;
+    if (path == 2) return MV_TC16;
+    if (path == 3) return MV_FP4;
+    return T <= 2 ? MV_DP4A : MV_TC16;
+}
+static bool use_tc(const void *w0, const void *w1, int64_t w_ld, int K, int T) {
+    return mv_kind(w0, w1, w_ld, K, T) != MV_DP4A;
+}
+// tensor-core matvec of either kind (the caller checked use_tc)
+static int tcx_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, int K, const float *x, int64_t ldx,
+                      const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
+                      int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream) {
+    if (mv_kind(w0, w1, w_ld, K, T) == MV_FP4)
+        return fp4_matvec(w0, w1, w_ld, N, K, x, ldx, q8, ldq, T, s0, s1, resid, ldr, y, ldy, dual, stream);
+    return tc_matvec(w0, w1, w_ld, N, K, x, ldx, q8, ldq, T, s0, s1, resid, ldr, y, ldy, dual, stream);
 }
 
 // ------------------------------------------------------------- device info
@@ -137,6 +161,7 @@ int matvec_path() {
         v = 0;
         if (e && std::string(e) == "dp4a") v = 1;
         if (e && std::string(e) == "tc") v = 2;
+        if (e && std::string(e) == "fp4") v = 3;
         g_matvec_path.store(v);
     }
     return v;
@@ -326,7 +351,7 @@ int fr_fault_inject(const char *site) {
 uint64_t fr_kernel_launches(void) { return g_launches.load(); }
 
 int fr_set_matvec_path(int path) {
-    if (path < 0 || path > 2) return FR_EINVAL;
+    if (path < 0 || path > 3) return FR_EINVAL;
     const int prev = matvec_path();
     g_matvec_path.store(path);
     return prev;
@@ -349,7 +374,7 @@ int fr_gemv_nvfp4_q8_1(const void *w, int64_t w_ld, const void *q8, int64_t ldq,
     if (rc != FR_OK) return rc;
     if (!q8 || !y || ldq < K / 32 || ldy < N || (resid && ldr < N)) return FR_EINVAL;
     if (use_tc(w, nullptr, w_ld, K, T))
-        return tc_matvec(static_cast<const uint8_t *>(w), nullptr, w_ld, N, K, nullptr, 0,
+        return tcx_matvec(static_cast<const uint8_t *>(w), nullptr, w_ld, N, K, nullptr, 0,
                          static_cast<const uint8_t *>(q8), ldq, T, scale, nullptr, resid, ldr, y, ldy, false, stream);
     GvParams p{};
     p.w0 = static_cast<const uint8_t *>(w);
@@ -374,7 +399,7 @@ int fr_gemv_nvfp4_f32(const void *w, int64_t w_ld, const float *x, int64_t ldx, 
     if (rc != FR_OK) return rc;
     if (!x || !y || ldx < K || ldy < N || (resid && ldr < N)) return FR_EINVAL;
     if (use_tc(w, nullptr, w_ld, K, T))
-        return tc_matvec(static_cast<const uint8_t *>(w), nullptr, w_ld, N, K, x, ldx, nullptr, 0, T, scale, nullptr,
+        return tcx_matvec(static_cast<const uint8_t *>(w), nullptr, w_ld, N, K, x, ldx, nullptr, 0, T, scale, nullptr,
                          resid, ldr, y, ldy, false, stream);
     GvParams p{};
     p.w0 = static_cast<const uint8_t *>(w);
@@ -399,7 +424,7 @@ int fr_gemv_nvfp4_q8_1_swiglu(const void *wg, const void *wu, int64_t w_ld, cons
     if (rc != FR_OK) return rc;
     if (!wu || (reinterpret_cast<uintptr_t>(wu) & 3) || !q8 || !y || ldq < K / 32 || ldy < N) return FR_EINVAL;
     if (use_tc(wg, wu, w_ld, K, T))
-        return tc_matvec(static_cast<const uint8_t *>(wg), static_cast<const uint8_t *>(wu), w_ld, N, K, nullptr, 0,
+        return tcx_matvec(static_cast<const uint8_t *>(wg), static_cast<const uint8_t *>(wu), w_ld, N, K, nullptr, 0,
                          static_cast<const uint8_t *>(q8), ldq, T, sg, su, nullptr, 0, y, ldy, true, stream);
     GvParams p{};
     p.w0 = static_cast<const uint8_t *>(wg);
@@ -423,7 +448,7 @@ int fr_mul_mat_nvfp4(const void *src0, int64_t nb01, const float *src1, int64_t 
     if (rc != FR_OK) return rc;
     if (!src1 || !dst || ld1 < K || ldd < N) return FR_EINVAL;
     if (use_tc(src0, nullptr, nb01, K, T))
-        return tc_matvec(static_cast<const uint8_t *>(src0), nullptr, nb01, N, K, src1, ld1, nullptr, 0, T, nullptr,
+        return tcx_matvec(static_cast<const uint8_t *>(src0), nullptr, nb01, N, K, src1, ld1, nullptr, 0, T, nullptr,
                          nullptr, nullptr, 0, dst, ldd, false, stream);
     if (T <= 2) return fr_gemv_nvfp4_f32(src0, nb01, src1, ld1, nullptr, nullptr, 0, dst, ldd, N, K, T, stream);
     void *q8 = nullptr;
@@ -453,14 +478,14 @@ int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
     if (use_tc(wg, wu, ld_gu, n_embd, T) && use_tc(wd, nullptr, ld_d, n_ff, T)) {
         // tensor-core path: the hi/lo activation kernels quantize x and the GLU
         // to q8_1 on the way (no q8_1 blocks needed)
-        rc = tc_matvec(static_cast<const uint8_t *>(wg), static_cast<const uint8_t *>(wu), ld_gu, n_ff, n_embd, x,
+        rc = tcx_matvec(static_cast<const uint8_t *>(wg), static_cast<const uint8_t *>(wu), ld_gu, n_ff, n_embd, x,
                        n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, n_ff, true, stream);
         if (rc != FR_OK) return rc;
         if (chk_glu_q8) {
             rc = quantize_launch(glu, n_ff, chk_glu_q8, n_ff / 32, T, n_ff, stream);
             if (rc != FR_OK) return rc;
         }
-        return tc_matvec(static_cast<const uint8_t *>(wd), nullptr, ld_d, n_embd, n_ff, glu, n_ff, nullptr, 0, T, sd,
+        return tcx_matvec(static_cast<const uint8_t *>(wd), nullptr, ld_d, n_embd, n_ff, glu, n_ff, nullptr, 0, T, sd,
                          nullptr, resid, n_embd, out, n_embd, false, stream);
     }
     // q8_1(x) in its own small kernel: under PDL it overlaps the start of the
@@ -1075,6 +1100,244 @@ static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, 
     return FR_OK;
 }
 
+template <int NCOL, int EPI>
+static int fp4_launch(const CUtensorMap &m0, const CUtensorMap &m1, FmArgs a, int grid, cudaStream_t stream) {
+    using S = FmShape<NCOL, EPI>;
+    auto kern = k_fp4mv<NCOL, EPI>;
+    static bool attr_done[64] = {};
+    int rc = allow_max_smem(kern, attr_done);
+    if (rc != FR_OK) return rc;
+    // ring depths: two or three MMA-ready stages, up to four activation
+    // stages, the rest of shared memory for raw weight stages (the HBM
+    // prefetch depth)
+    const int bar_bytes = 512;
+    const int cap = dev_info().smem_optin - 1024 - bar_bytes;
+    int nc = 3, nb = 4;
+    if (nb * S::BST > 40 * 1024) nb = 2;
+    int nr = (cap - nc * S::CAN - nb * S::BST) / S::RAW;
+    if (nr < 4) {
+        nc = 2;
+        nr = (cap - nc * S::CAN - nb * S::BST) / S::RAW;
+    }
+    // tuning overrides (FR_FP4_RINGS="raw,mma,act"), clamped to shared memory
+    static const char *ov = getenv("FR_FP4_RINGS");
+    if (ov && *ov) {
+        int r = 0, c = 0, b = 0;
+        if (sscanf(ov, "%d,%d,%d", &r, &c, &b) == 3 && r >= 2 && c >= 1 && b >= 1 &&
+            r * S::RAW + c * S::CAN + b * S::BST <= cap) {
+            nr = r;
+            nc = c;
+            nb = b;
+        }
+    }
+    if (nr < 2) return FR_EINVAL;
+    a.n_can = nc;
+    a.n_b = nb;
+    a.n_raw = std::min(nr, 8);
+    const size_t smem = 1024 + static_cast<size_t>(a.n_can) * S::CAN + static_cast<size_t>(a.n_b) * S::BST +
+                        static_cast<size_t>(a.n_raw) * S::RAW + bar_bytes;
+    return launch_pdl(kern, dim3(grid), dim3(S::THREADS), smem, stream, m0, m1, a);
+}
+
+template <int NCOL, int EPI, int NT>
+static int fp4t_launch(FtArgs a, int grid, cudaStream_t stream) {
+    using S = FtShape<NCOL, EPI, NT>;
+    auto kern = k_fp4t<NCOL, EPI, NT>;
+    static bool attr_done[64] = {};
+    int rc = allow_max_smem(kern, attr_done);
+    if (rc != FR_OK) return rc;
+    // about 110 KB of weights in flight per SM (measured best for one pass
+    // over a matrix: more only lengthens the memory queues), four activation
+    // stages; TMEM's 256 scale columns bound the weight ring
+    const int extra = 2048;                                  // scale atom, factors, barriers
+    const int cap = dev_info().smem_optin - 1024 - extra;
+    int nb = 4;
+    int nw = std::max(2, std::min((110 * 1024 + S::WST - 1) / S::WST, 8));
+    nw = std::min(nw, (256 - 4 * S::NI) / (16 * S::NI));
+    // tuning override (FR_FP4T_RINGS="weights,activations"), within the limits
+    static const char *ov = getenv("FR_FP4T_RINGS");
+    if (ov && *ov) {
+        int w = 0, b = 0;
+        if (sscanf(ov, "%d,%d", &w, &b) == 2 && w >= 2 && b >= 1 && w * 16 * S::NI <= 256 - 4 * S::NI &&
+            w * S::WST + b * S::BST <= cap) {
+            nw = w;
+            nb = b;
+        }
+    }
+    while (nw > 2 && nw * S::WST + nb * S::BST > cap) --nw;
+    if (nw * S::WST + nb * S::BST > cap) return FR_EINVAL;
+    a.n_w = nw;
+    a.n_b = nb;
+    const size_t smem = 1024 + static_cast<size_t>(nw) * S::WST + static_cast<size_t>(nb) * S::BST + extra;
+    return launch_pdl(kern, dim3(grid), dim3(S::THREADS), smem, stream, a);
+}
+
+template <int NCOL>
+static int fp4t_launch2(const FtArgs &a, int grid, bool dual, int nt, cudaStream_t stream) {
+    if (dual) return fp4t_launch<NCOL, FM_SWIGLU, 1>(a, grid, stream);
+    return nt == 2 ? fp4t_launch<NCOL, FM_PLAIN, 2>(a, grid, stream) : fp4t_launch<NCOL, FM_PLAIN, 1>(a, grid, stream);
+}
+
+// FP4 tensor-core matvec on tile-major weights (k_tile_nvfp4's layout):
+// k_act_fp4 builds the activation columns of a window of FP4_MAX_T tokens,
+// k_fp4t streams the weights once per window.
+static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const float *x, int64_t ldx,
+                       const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
+                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream) {
+    if (!w0 || (dual && !w1) || N <= 0 || K <= 0 || K % 256 != 0 || T <= 0 || !y) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(w0) & 15) || (w1 && (reinterpret_cast<uintptr_t>(w1) & 15))) return FR_EINVAL;
+    const DevInfo &di = dev_info();
+    if (di.cc_major != 10) return FR_ENODEVICE;
+    const int n_kq = K / 256, n_rb = (N + 127) / 128;
+    const int nt = (!dual && n_kq % 2 == 0) ? 2 : 1;         // K stages per pipeline step
+    const int nsr = n_kq / nt;
+    const int U = n_rb * nsr;
+    const int G = std::max(1, std::min(di.sms, U));
+    const int per_min = std::max(1, U / G);
+    const int maxp = std::min(G, (nsr + per_min - 1) / per_min + 1);
+    const int TW = std::min(T, FP4_MAX_T);
+    const int NCOL = FM_DIGITS * TW <= 16 ? 16 : FM_DIGITS * TW <= 32 ? 32 : FM_DIGITS * TW <= 64 ? 64 : 128;
+    const int TMAX = NCOL / FM_DIGITS;
+
+    constexpr size_t MAX_COUNTERS = 1 << 16;
+    if (static_cast<size_t>(n_rb) * 4 > MAX_COUNTERS) return FR_EINVAL;
+    const size_t part_floats = static_cast<size_t>(n_rb) * maxp * 2 * TMAX * 128;
+    const size_t part_off = MAX_COUNTERS * 4;
+    void *wsp = nullptr;
+    int rc = workspace_get_zeroed(WS_TGPART, part_off + part_floats * 4, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    const size_t b_bytes = static_cast<size_t>(n_kq) * NCOL * 128;
+    const size_t sf_bytes = static_cast<size_t>(n_kq) * 4 * 512;
+    void *actp = nullptr;
+    rc = workspace_get(WS_FP4, b_bytes + sf_bytes + static_cast<size_t>(TMAX) * FM_GSTRIDE * 4, stream, &actp);
+    if (rc != FR_OK) return rc;
+    uint8_t *bimg = static_cast<uint8_t *>(actp);
+    uint8_t *sfb = bimg + b_bytes;
+    float *gtab = reinterpret_cast<float *>(sfb + sf_bytes);
+
+    FtArgs a{};
+    a.N = N;
+    a.K = K;
+    a.n_kq = n_kq;
+    a.n_units = U;
+    a.maxp = maxp;
+    a.w0 = w0;
+    a.w1 = dual ? w1 : w0;
+    a.bimg = bimg;
+    a.gtab = gtab;
+    a.s0 = s0;
+    a.s1 = s1;
+    a.resid = resid;
+    a.ldr = ldr;
+    a.y = y;
+    a.ldy = ldy;
+    a.part = reinterpret_cast<float *>(static_cast<uint8_t *>(wsp) + part_off);
+    a.counter = static_cast<unsigned int *>(wsp);
+    const int nq = K / Q8_ELEMS;
+    for (int t0 = 0; t0 < T; t0 += TW) {
+        const int tw = std::min(TW, T - t0);
+        a.T = tw;
+        a.t0 = t0;
+        const int slices = std::max(1, std::min((nq + 7) / 8, std::max(1, 256 / tw)));
+        rc = launch_pdl(k_act_fp4, dim3(slices, tw), dim3(256), 0, stream,
+                        x ? x + t0 * ldx : static_cast<const float *>(nullptr), ldx,
+                        q8 ? q8 + t0 * ldq * Q8_BYTES : static_cast<const uint8_t *>(nullptr), ldq, K, NCOL, bimg, sfb,
+                        gtab);
+        if (rc != FR_OK) return rc;
+        switch (NCOL) {
+        case 16: rc = fp4t_launch2<16>(a, G, dual, nt, stream); break;
+        case 32: rc = fp4t_launch2<32>(a, G, dual, nt, stream); break;
+        case 64: rc = fp4t_launch2<64>(a, G, dual, nt, stream); break;
+        default: rc = fp4t_launch2<128>(a, G, dual, nt, stream); break;
+        }
+        if (rc != FR_OK) return rc;
+    }
+    return FR_OK;
+}
+
+// FP4 tensor-core matvec: k_act_fp4 writes the activation columns of up to
+// FP4_MAX_T tokens, k_fp4mv streams the weights once per such window.
+static int fp4_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, int K, const float *x, int64_t ldx,
+                      const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
+                      int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream) {
+    const DevInfo &di = dev_info();
+    const int G = std::max(1, di.sms);
+    const int TW = std::min(T, FP4_MAX_T);
+    const int NCOL = FM_DIGITS * TW <= 16 ? 16 : FM_DIGITS * TW <= 32 ? 32 : FM_DIGITS * TW <= 64 ? 64 : 128;
+    const int TMAX = NCOL / FM_DIGITS;
+    const int n_kt = K / FM_KS;
+    int ksplit = std::max(1, std::min(n_kt, (128 * G) / std::max(1, N)));
+    const int kt_per = (n_kt + ksplit - 1) / ksplit;
+    ksplit = (n_kt + kt_per - 1) / kt_per;
+    const int R = std::min(128, std::max(1, static_cast<int>((static_cast<int64_t>(N) * ksplit + G - 1) / G)));
+    const int n_rt = (N + R - 1) / R;
+
+    // activation columns, their scale atoms, the column factors
+    const size_t b_bytes = static_cast<size_t>(n_kt) * NCOL * 128;
+    const size_t sf_bytes = static_cast<size_t>(n_kt) * 4 * 512;
+    const size_t g_bytes = static_cast<size_t>(TMAX) * FM_GSTRIDE * 4;
+    void *actp = nullptr;
+    int rc = workspace_get(WS_FP4, b_bytes + sf_bytes + g_bytes, stream, &actp);
+    if (rc != FR_OK) return rc;
+    uint8_t *bimg = static_cast<uint8_t *>(actp);
+    uint8_t *sfb = bimg + b_bytes;
+    float *gtab = reinterpret_cast<float *>(sfb + sf_bytes);
+
+    constexpr size_t MAX_COUNTERS = 1 << 16;
+    if (static_cast<size_t>(n_rt) * 4 > MAX_COUNTERS) return FR_EINVAL;
+    const size_t part_floats = static_cast<size_t>(n_rt) * ksplit * 2 * TMAX * 128;
+    const size_t part_off = MAX_COUNTERS * 4;
+    void *wsp = nullptr;
+    rc = workspace_get_zeroed(WS_TGPART, part_off + part_floats * 4, stream, &wsp);
+    if (rc != FR_OK) return rc;
+
+    CUtensorMap m0, m1;
+    rc = make_map_wrows(&m0, w0, N, K, w_ld, R);
+    if (rc != FR_OK) return rc;
+    rc = make_map_wrows(&m1, dual ? w1 : w0, N, K, w_ld, R);
+    if (rc != FR_OK) return rc;
+
+    FmArgs a{};
+    a.N = N;
+    a.K = K;
+    a.R = R;
+    a.n_kt = n_kt;
+    a.ksplit = ksplit;
+    a.kt_per_split = kt_per;
+    a.bimg = bimg;
+    a.sfb = sfb;
+    a.gtab = gtab;
+    a.s0 = s0;
+    a.s1 = s1;
+    a.resid = resid;
+    a.ldr = ldr;
+    a.y = y;
+    a.ldy = ldy;
+    a.part = static_cast<float *>(static_cast<void *>(static_cast<uint8_t *>(wsp) + part_off));
+    a.counter = static_cast<unsigned int *>(wsp);
+    const int nq = K / Q8_ELEMS;
+    for (int t0 = 0; t0 < T; t0 += TW) {
+        const int tw = std::min(TW, T - t0);
+        const int slices = std::max(1, std::min((nq + 7) / 8, std::max(1, 256 / tw)));
+        rc = launch_pdl(k_act_fp4, dim3(slices, tw), dim3(256), 0, stream,
+                        x ? x + t0 * ldx : static_cast<const float *>(nullptr), ldx,
+                        q8 ? q8 + t0 * ldq * Q8_BYTES : static_cast<const uint8_t *>(nullptr), ldq, K, NCOL, bimg,
+                        sfb, gtab);
+        if (rc != FR_OK) return rc;
+        a.T = tw;
+        a.t0 = t0;
+        const int grid = n_rt * ksplit;
+        switch (NCOL) {
+        case 16: rc = dual ? fp4_launch<16, FM_SWIGLU>(m0, m1, a, grid, stream) : fp4_launch<16, FM_PLAIN>(m0, m1, a, grid, stream); break;
+        case 32: rc = dual ? fp4_launch<32, FM_SWIGLU>(m0, m1, a, grid, stream) : fp4_launch<32, FM_PLAIN>(m0, m1, a, grid, stream); break;
+        case 64: rc = dual ? fp4_launch<64, FM_SWIGLU>(m0, m1, a, grid, stream) : fp4_launch<64, FM_PLAIN>(m0, m1, a, grid, stream); break;
+        default: rc = dual ? fp4_launch<128, FM_SWIGLU>(m0, m1, a, grid, stream) : fp4_launch<128, FM_PLAIN>(m0, m1, a, grid, stream); break;
+        }
+        if (rc != FR_OK) return rc;
+    }
+    return FR_OK;
+}
+
 } // namespace frb
 
 // ======================================================================
@@ -1212,6 +1475,59 @@ static unsigned gemv_ctas(int N, int K, int64_t w_ld, int T, bool dual) {
 
 extern "C" {
 
+int64_t fr_nvfp4_tiled_bytes(int N, int K) {
+    if (N <= 0 || K <= 0 || K % 64 != 0) return -1;
+    return static_cast<int64_t>((N + 127) / 128) * ((K + 255) / 256) * FT_TILE;
+}
+
+int fr_nvfp4_tile(const void *w, int64_t w_ld, int N, int K, void *dst, cudaStream_t stream) {
+    if (fault_hit("fr_nvfp4_tile")) return FR_EINJECTED;
+    if (!w || !dst || N <= 0 || K <= 0 || K % 64 != 0) return FR_EINVAL;
+    if (w_ld < static_cast<int64_t>(K / 64) * NV_BYTES || w_ld % 4 != 0) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(w) & 3) || (reinterpret_cast<uintptr_t>(dst) & 15)) return FR_EINVAL;
+    const int n_kq = (K + 255) / 256;
+    const int64_t total = static_cast<int64_t>((N + 127) / 128) * 128 * n_kq * 4;
+    return launch_pdl(k_tile_nvfp4, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, stream,
+                      static_cast<const uint8_t *>(w), w_ld, N, K, n_kq, static_cast<uint8_t *>(dst), total);
+}
+
+int fr_gemv_tiled(const void *wt, int N, int K, const float *x, int64_t ldx, const void *q8, int64_t ldq,
+                  const float *scale, const float *resid, int64_t ldr, float *y, int64_t ldy, int T,
+                  cudaStream_t stream) {
+    if (fault_hit("fr_gemv_tiled")) return FR_EINJECTED;
+    if ((x == nullptr) == (q8 == nullptr)) return FR_EINVAL;
+    return fp4t_matvec(static_cast<const uint8_t *>(wt), nullptr, N, K, x, ldx, static_cast<const uint8_t *>(q8),
+                       ldq, T, scale, nullptr, resid, ldr, y, ldy, false, stream);
+}
+
+int fr_gemv_tiled_swiglu(const void *wg_t, const void *wu_t, int N, int K, const float *x, int64_t ldx,
+                         const void *q8, int64_t ldq, const float *sg, const float *su, float *y, int64_t ldy, int T,
+                         cudaStream_t stream) {
+    if (fault_hit("fr_gemv_tiled_swiglu")) return FR_EINJECTED;
+    if ((x == nullptr) == (q8 == nullptr)) return FR_EINVAL;
+    return fp4t_matvec(static_cast<const uint8_t *>(wg_t), static_cast<const uint8_t *>(wu_t), N, K, x, ldx,
+                       static_cast<const uint8_t *>(q8), ldq, T, sg, su, nullptr, 0, y, ldy, true, stream);
+}
+
+int fr_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void *wd_t, const float *sg,
+                 const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                 float *chk_glu, cudaStream_t stream) {
+    if (fault_hit("fr_ffn_tiled")) return FR_EINJECTED;
+    if (!x || !wg_t || !wu_t || !wd_t || !out || T <= 0 || n_embd % 256 != 0 || n_ff % 256 != 0) return FR_EINVAL;
+    float *glu = chk_glu;
+    if (!glu) {
+        void *p = nullptr;
+        const int rc = workspace_get(WS_GLU, static_cast<size_t>(T) * n_ff * sizeof(float), stream, &p);
+        if (rc != FR_OK) return rc;
+        glu = static_cast<float *>(p);
+    }
+    int rc = fp4t_matvec(static_cast<const uint8_t *>(wg_t), static_cast<const uint8_t *>(wu_t), n_ff, n_embd, x,
+                         n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, n_ff, true, stream);
+    if (rc != FR_OK) return rc;
+    return fp4t_matvec(static_cast<const uint8_t *>(wd_t), nullptr, n_embd, n_ff, glu, n_ff, nullptr, 0, T, sd,
+                       nullptr, resid, n_embd, out, n_embd, false, stream);
+}
+
 int fr_ipc_alloc(int64_t bytes, void **dev_ptr, void *handle64) {
     if (bytes <= 0 || !dev_ptr || !handle64) return FR_EINVAL;
     static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
@@ -1278,10 +1594,10 @@ int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, 
         // batches: tensor-core matvecs, the partial output into this rank's
         // own slot, then a push kernel stores it into every peer's slot
         constexpr int PUSH_CTAS = 64;
-        rc = tc_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), ld_gu, F_p,
+        rc = tcx_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), ld_gu, F_p,
                        n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
         if (rc != FR_OK) return rc;
-        rc = tc_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, ld_d, n_embd, F_p, glu, F_p, nullptr, 0, T,
+        rc = tcx_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, ld_d, n_embd, F_p, glu, F_p, nullptr, 0, T,
                        sd, nullptr, nullptr, 0, reinterpret_cast<float *>(base + slot_off), n_embd, false, stream);
         if (rc != FR_OK) return rc;
         rc = launch_pdl(k_tp_push, dim3(PUSH_CTAS), dim3(256), 0, stream, pb, nranks, rank, slot_off,

@@ -55,6 +55,11 @@ SIGNATURES = {
     "fr_mul_mat_nvfp4": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp]),
     "fr_ffn_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp]),
     "fr_ffn_nvfp4_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "fr_nvfp4_tiled_bytes": (_i64, [_i32, _i32]),
+    "fr_nvfp4_tile": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp]),
+    "fr_gemv_tiled": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i32, _vp]),
+    "fr_gemv_tiled_swiglu": (_i32, [_vp, _vp, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _vp]),
+    "fr_ffn_tiled": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp]),
     "fr_tp_buffer_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "fr_tp_ffn_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                _i64, _vp]),
@@ -238,6 +243,55 @@ def mul_mat_id(w, E, N, K, x, ids, broadcast: bool, out=None, stream=None):
         x_ld_slot, x_ld_tok = x.stride(1), x.stride(0)
     call("fr_mul_mat_id_nvfp4", _ptr(w), w.stride(1), w.stride(0), E, _ptr(x), x_ld_slot, x_ld_tok, _ptr(ids),
          ids.stride(0), _ptr(out), out.stride(1), out.stride(0), T, n_used, N, K, _stream(stream))
+    return out
+
+
+def tile_nvfp4(w, N, K, out=None, stream=None):
+    """Repack a ggml block_nvfp4 matrix [N, K] (uint8 CUDA tensor, rows
+    w.stride(0) bytes apart) into the tile-major layout (uint8 tensor)."""
+    import torch
+    nb = int(lib().fr_nvfp4_tiled_bytes(N, K))
+    if nb < 0:
+        raise ValueError(f"bad shape N={N} K={K}")
+    if out is None:
+        out = torch.empty(nb, dtype=torch.uint8, device=w.device)
+    call("fr_nvfp4_tile", _ptr(w), w.stride(0), N, K, _ptr(out), _stream(stream))
+    return out
+
+
+def gemv_tiled(wt, N, K, x=None, q8=None, T=None, scale=None, resid=None, out=None, stream=None):
+    """y = scale * W . x_q (+ resid) on tiled weights; x f32 [T, K] or q8 [T, K/32*36]."""
+    import torch
+    a = x if x is not None else q8
+    T = a.shape[0] if T is None else T
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.float32, device=a.device)
+    call("fr_gemv_tiled", _ptr(wt), N, K, _ptr(x), x.stride(0) if x is not None else 0, _ptr(q8),
+         q8.stride(0) // 36 if q8 is not None else 0, _ptr(scale), _ptr(resid),
+         resid.stride(0) if resid is not None else 0, _ptr(out), out.stride(0), T, _stream(stream))
+    return out
+
+
+def gemv_tiled_swiglu(wg_t, wu_t, N, K, x=None, q8=None, T=None, sg=None, su=None, out=None, stream=None):
+    import torch
+    a = x if x is not None else q8
+    T = a.shape[0] if T is None else T
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.float32, device=a.device)
+    call("fr_gemv_tiled_swiglu", _ptr(wg_t), _ptr(wu_t), N, K, _ptr(x), x.stride(0) if x is not None else 0,
+         _ptr(q8), q8.stride(0) // 36 if q8 is not None else 0, _ptr(sg), _ptr(su), _ptr(out), out.stride(0), T,
+         _stream(stream))
+    return out
+
+
+def ffn_tiled(x, wg_t, wu_t, wd_t, n_embd, n_ff, sg=None, su=None, sd=None, resid=None, out=None, chk_glu=None,
+              stream=None):
+    import torch
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T, n_embd), dtype=torch.float32, device=x.device)
+    call("fr_ffn_tiled", _ptr(x), _ptr(wg_t), _ptr(wu_t), _ptr(wd_t), _ptr(sg), _ptr(su), _ptr(sd), _ptr(resid),
+         _ptr(out), T, n_embd, n_ff, _ptr(chk_glu), _stream(stream))
     return out
 
 

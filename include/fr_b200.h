@@ -206,6 +206,37 @@ int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S,
 int fr_moe_combine(const float *part, const float *wts, const float *resid, float *out,
                    int T, int n_used, int n_embd, cudaStream_t stream);
 
+/* ------------------------------------------------ (a2-a4) tile-major weights
+ * A one-time repack of a ggml block_nvfp4 matrix [N, K] (rows w_ld bytes
+ * apart) into tiles of 128 rows x 256 values, each one contiguous 18 KB block
+ * (16 KB of E2M1 codes in the 128-byte-swizzled K-major order the tcgen05
+ * block-scaled MMA reads, 2 KB of UE4M3 sub-block scale atoms), tiles of a
+ * row block consecutive along K.  Same bytes as the ggml tensor when
+ * N % 128 == 0 and K % 256 == 0 (rows / blocks past the end are zero).  The
+ * reference repacks NVFP4 weights once at load for its tensor-core GEMM in
+ * the same way (include/fr_kernels.h:45-51, src/fr_repack.cu:1-13); here the
+ * tiled layout feeds the decode matvec on the FP4 tensor cores, which streams
+ * each CTA's tiles as one contiguous byte range.
+ *   fr_nvfp4_tiled_bytes : size of the tiled copy (-1 on bad shape)
+ *   fr_nvfp4_tile        : repack (K % 64 == 0)
+ *   fr_gemv_tiled        : y[t] = scale * W . x_q[t] (+ resid[t]); exactly one
+ *                          of x (f32 rows, quantized to q8_1 on the fly) or q8
+ *                          (q8_1 rows, ldq blocks apart) is non-null
+ *   fr_gemv_tiled_swiglu : y[t] = silu(sg * Wg . x_q[t]) * (su * Wu . x_q[t])
+ *   fr_ffn_tiled         : fr_ffn_nvfp4 on tiled weights
+ * K % 256 == 0 for the matvecs. */
+int64_t fr_nvfp4_tiled_bytes(int N, int K);
+int fr_nvfp4_tile(const void *w, int64_t w_ld, int N, int K, void *dst, cudaStream_t stream);
+int fr_gemv_tiled(const void *wt, int N, int K, const float *x, int64_t ldx, const void *q8, int64_t ldq,
+                  const float *scale, const float *resid, int64_t ldr, float *y, int64_t ldy, int T,
+                  cudaStream_t stream);
+int fr_gemv_tiled_swiglu(const void *wg_t, const void *wu_t, int N, int K, const float *x, int64_t ldx,
+                         const void *q8, int64_t ldq, const float *sg, const float *su, float *y, int64_t ldy, int T,
+                         cudaStream_t stream);
+int fr_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void *wd_t, const float *sg,
+                 const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                 float *chk_glu, cudaStream_t stream);
+
 /* ------------------------------------------------------ (e) tensor parallel
  * One rank's step of the dense FFN sharded over n_ff (P = nranks ranks, shard
  * F_p = n_ff / P): rank r holds gate/up rows [r*F_p, (r+1)*F_p) and, of every

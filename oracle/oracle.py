@@ -204,6 +204,35 @@ def gemm_f32out(A, SFA, B, SFB, M, N, K, alpha=1.0, nthreads=0):
 
 # ------------------------------------------------------------ comparisons
 
+def tile_nvfp4(blocks: np.ndarray, N: int, K: int) -> np.ndarray:
+    """Tile-major NVFP4 layout (the library's fr_nvfp4_tile, test
+    restatement): tiles of 128 rows x 256 values, tile (rb, kq) at
+    (rb * n_kq + kq) * 18432; 16 KB of code bytes with row r's 16-byte unit c
+    (block c >> 1, half c & 1 of its 32 code bytes, ggml byte order) at
+    r * 128 + ((c ^ (r & 7)) << 4); then per block j a 512-byte scale atom with
+    row r's sub-block scales at (r & 31) * 16 + (r >> 5) * 4, sign bit
+    dropped and 0x7F read as 0 (ggml's ue4m3 reading, ggml-common.h).
+    Padding rows / blocks are zero."""
+    n_kq, n_rb = (K + 255) // 256, (N + 127) // 128
+    b = np.zeros((n_rb * 128, n_kq * 4, 36), np.uint8)
+    b[:N, :K // 64] = np.asarray(blocks, np.uint8).reshape(N, K // 64, 36)
+    sc = b[:, :, :4] & 0x7F
+    sc[sc == 0x7F] = 0
+    codes = b[:, :, 4:].reshape(n_rb, 128, n_kq, 8, 16)           # rb, r, kq, c, 16
+    out = np.zeros((n_rb, n_kq, 18432), np.uint8)
+    r = np.arange(128)
+    tiles_codes = np.zeros((n_rb, n_kq, 128, 8, 16), np.uint8)
+    for c in range(8):
+        phys = c ^ (r & 7)
+        tiles_codes[:, :, r, phys, :] = codes[:, :, :, c, :].transpose(0, 2, 1, 3)[:, :, r, :]
+    out[:, :, :16384] = tiles_codes.reshape(n_rb, n_kq, 16384)
+    scs = sc.reshape(n_rb, 128, n_kq, 4, 4)                         # rb, r, kq, j, sb
+    atoms = np.zeros((n_rb, n_kq, 4, 32, 4, 4), np.uint8)            # rb, kq, j, r & 31, r >> 5, sb
+    atoms[:, :, :, r & 31, r >> 5, :] = scs.transpose(0, 2, 3, 1, 4)[:, :, :, r, :]
+    out[:, :, 16384:] = atoms.reshape(n_rb, n_kq, 2048)
+    return out.reshape(-1)
+
+
 def rel_err(mine: np.ndarray, ref: np.ndarray, floor_frac: float = 1e-2) -> float:
     """max |mine - ref| / max(|ref|, floor_frac * rms(ref)): the relative error,
     with outputs smaller than 1% of the rms judged against 1% of the rms (a

@@ -19,9 +19,11 @@ RTOL = 1e-3      # max |d| / max(|ref|, 1% rms(ref))
 NTOL = 1e-5      # ||d|| / ||ref||
 
 
-@pytest.fixture(params=[1, 2], ids=["dp4a", "tcgen05"], autouse=True)
+@pytest.fixture(params=[1, 2, 3], ids=["dp4a", "tc-f16", "tc-fp4"], autouse=True)
 def matvec_path(request, fr):
-    """Run every dense parity test on both matvec kernels."""
+    """Run every dense parity test on all three matvec kernels: dp4a, the
+    tensor-core kernel on decoded f16 weights, the FP4 tensor-core kernel on
+    the stored codes."""
     prev = fr.set_matvec_path(request.param)
     yield request.param
     fr.set_matvec_path(prev)
@@ -194,6 +196,32 @@ def test_ffn_stagewise(fr, O, dev, T):
     np.testing.assert_array_equal(gq8.cpu().numpy(), O.quantize_q8_1(dglu))
     ref = O.gemv_q8_1(wd, gq8.cpu().numpy(), n_embd, n_ff, nthreads=8) + r
     _check(out.cpu().numpy(), ref, O, "ffn out")
+
+
+def test_gemv_special_scales_and_blocks(fr, O, dev):
+    """Scale bytes ggml treats specially (sign bit set: ignored; 0x7F / 0xFF:
+    zero) and activation blocks of very different size (zero, 1e-6, 1e3)."""
+    import torch
+    N, K, T = 300, 1024, 3
+    w = fr.synth_nvfp4(91, N, K)
+    blocks = w.reshape(N, K // 64, 36)
+    blocks[0:7, 0, 0] = 0x7F
+    blocks[7:15, 1, 2] = 0xFF
+    blocks[15:40, 2, 1] |= 0x80
+    blocks[40:60, 3, :4] = 0x7F
+    x = fr.synth_normal(92, T * K).reshape(T, K)
+    x[0, 0:32] = 0.0
+    x[1, 64:96] *= 1e-6
+    x[2, 128:160] *= 1e3
+    x[2, 512:1024] = 0.0
+    q = O.quantize_q8_1(x)
+    y = fr.gemv_q8_1(_t(w, dev), _t(q, dev), N, K, T)
+    y2 = fr.gemv_f32(_t(w, dev), _t(x, dev), N, K)
+    torch.cuda.synchronize()
+    ref = O.gemv_q8_1(w, q, N, K)
+    _check(y.cpu().numpy(), ref, O, "special scales / blocks (q8 input)")
+    _check(y2.cpu().numpy(), ref, O, "special scales / blocks (f32 input)")
+    assert fr.device_status() == 0
 
 
 def test_invalid_arguments_return_minus_one(fr, dev):
