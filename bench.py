@@ -34,8 +34,9 @@ N_EMBD, N_FF = 4096, 14336
 N_SETS = 4
 HBM_FALLBACK = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the gate/up SwiGLU
-# matvec (T=1), from the ncu capture summarised in profiles/; None until taken.
-TRAFFIC_GATEUP = None
+# FP4 tensor-core matvec on tile-major weights (T=1), from the ncu capture
+# summarised in profiles/k_fp4t_gateup_T1.md
+TRAFFIC_GATEUP = 66.17e6
 
 
 def _peaks():
@@ -233,28 +234,40 @@ def run_ours(args):
         barrier()
         return max_over_ranks(e0.elapsed_time(e1)) / K
 
-    # ---------------- dense FFN (config 2): single GPU, or row-sharded over the ranks
+    # ---------------- dense FFN (config 2): single GPU, or sharded over n_ff.
+    # Weights are repacked once (as at model load) into the tile-major layout
+    # the FP4 tensor-core matvec streams; ggml's in-place layout is measured
+    # beside it (dp4a matvec) on one GPU.
     f0, f1 = P.shard_range(N_FF, rank, world)
-    sets = []
+    sets, gsets = [], []
     for s in range(N_SETS):
         base = 0x5EED0000 + 100 * s
-        wg = frb200.synth_nvfp4(base + 1, N_FF, N_EMBD)[f0:f1]
-        wu = frb200.synth_nvfp4(base + 2, N_FF, N_EMBD)[f0:f1]
-        wd = P.down_shard(frb200.synth_nvfp4(base + 3, N_EMBD, N_FF), N_EMBD, N_FF, rank, world)
-        sets.append(tuple(torch.from_numpy(w.copy()).to(dev) for w in (wg, wu, wd)))
+        wg = torch.from_numpy(frb200.synth_nvfp4(base + 1, N_FF, N_EMBD)[f0:f1].copy()).to(dev)
+        wu = torch.from_numpy(frb200.synth_nvfp4(base + 2, N_FF, N_EMBD)[f0:f1].copy()).to(dev)
+        wd = torch.from_numpy(P.down_shard(frb200.synth_nvfp4(base + 3, N_EMBD, N_FF), N_EMBD, N_FF, rank,
+                                           world)).to(dev)
+        F_p = f1 - f0
+        sets.append((frb200.tile_nvfp4(wg, F_p, N_EMBD), frb200.tile_nvfp4(wu, F_p, N_EMBD),
+                     frb200.tile_nvfp4(wd, N_EMBD, F_p)))
+        if world == 1:
+            gsets.append((wg, wu, wd))
+        else:
+            del wg, wu, wd
+    torch.cuda.synchronize()
     Tmax = 64
     x_all = torch.from_numpy(frb200.synth_normal(0x5EED0000 + 10, Tmax * N_EMBD).reshape(Tmax, N_EMBD)).to(dev)
     outs = [torch.empty((Tmax, N_EMBD), dtype=torch.float32, device=dev) for _ in range(N_SETS)]
-
     tp = P.TpFfn(Tmax, N_EMBD, N_FF) if world > 1 else None
 
-    def ffn_step(i, T, x=None, out=None):
-        wg, wu, wd = sets[i % N_SETS]
+    def ffn_step(i, T, x=None, out=None, layout="tiled"):
         xx = x_all[:T] if x is None else x
-        if world == 1:
-            frb200.ffn(xx, wg, wu, wd, N_EMBD, N_FF, out=(outs[i % N_SETS][:T] if out is None else out), stream=stream)
+        oo = outs[i % N_SETS][:T] if out is None else out
+        if world > 1:
+            tp(xx, *sets[i % N_SETS], out=oo, stream=stream, tiled=True)
+        elif layout == "tiled":
+            frb200.ffn_tiled(xx, *sets[i % N_SETS], N_EMBD, N_FF, out=oo, stream=stream)
         else:
-            tp(xx, wg, wu, wd, out=(outs[i % N_SETS][:T] if out is None else out), stream=stream)
+            frb200.ffn(xx, *gsets[i % N_SETS], N_EMBD, N_FF, out=oo, stream=stream)
 
     def graphs_for(fn):
         with torch.cuda.stream(stream):
@@ -293,19 +306,27 @@ def run_ours(args):
         extra[f"ffn_T{T}_gbs"] = round(ffn_bytes(T) / (msT * 1e-3) / 1e9, 1)
         extra[f"ffn_T{T}_ms_per_step"] = round(msT, 5)
         del gT
+    if world == 1:
+        # ggml's in-place block_nvfp4 layout (no repack): the dp4a matvec
+        gg = graphs_for(lambda i: ffn_step(i, 1, layout="ggml"))
+        msg = time_fn(lambda i: gg[i % N_SETS].replay(), max(20, args.steps // 4), max(args.warmup, 3))
+        extra["ffn_ggml_layout_T1_gbs"] = round(ffn_bytes(1) / (msg * 1e-3) / 1e9, 1)
+        extra["ffn_ggml_layout_T1_ms_per_step"] = round(msg, 5)
+        del gg
 
-    # dominant kernel (single GPU): gate/up SwiGLU matvec, timed alone on its stream
+    # dominant kernel (single GPU): the gate/up SwiGLU matvec with its
+    # activation-column kernel, timed alone on its stream
     roof = None
     if world == 1:
-        q8x = frb200.quantize_q8_1(x_all[:1], stream=stream)
         glu = torch.empty((1, N_FF), dtype=torch.float32, device=dev)
-        kgs = graphs_for(lambda i: frb200.gemv_swiglu(sets[i][0], sets[i][1], q8x, N_FF, N_EMBD, 1, out=glu,
-                                                       stream=stream))
+        kgs = graphs_for(lambda i: frb200.gemv_tiled_swiglu(sets[i][0], sets[i][1], N_FF, N_EMBD, x=x_all[:1],
+                                                             out=glu, stream=stream))
         k_ms = time_fn(lambda i: kgs[i % N_SETS].replay(), max(args.steps, 20), 5)
         k_gbs = gateup_bytes(1) / (k_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "k_gemv<32,1,SWIGLU,1,16> (gate/up, T=1)", "achieved": round(k_gbs, 1),
-                "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(k_gbs / hbm, 4),
-                "traffic": TRAFFIC_GATEUP, "algorithmic_bytes": gateup_bytes(1), "ms_per_launch": round(k_ms, 5)}
+        roof = {"bound": "hbm", "kernel": "k_fp4t<16,SWIGLU,1> + k_act_fp4 (gate/up on tile-major weights, T=1)",
+                "achieved": round(k_gbs, 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": round(k_gbs / hbm, 4), "traffic": TRAFFIC_GATEUP, "algorithmic_bytes": gateup_bytes(1),
+                "ms_per_launch": round(k_ms, 5)}
         del kgs
 
     # e2e through the public entry point: pinned H2D of x, the FFN, D2H of out
@@ -348,9 +369,11 @@ def run_ours(args):
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms1, 5), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-        "dtype": "int8xe2m1 (q8_1 x NVFP4, exact sub-block sums, fp32 scale)",
+        "dtype": "e2m1 (NVFP4 weights x q8_1 activation held exactly as E2M1 digit columns; tcgen05 kind::mxf4nvf4, "
+                 "fp32 accumulation)",
         "data": "synthetic (seeded splitmix64 / Box-Muller; BASELINE configs)",
-        "config": {"workload": "dense FFN gate/up 14336x4096 + down 4096x14336 NVFP4 x q8_1, T=1 (configs[1])",
+        "config": {"workload": "dense FFN gate/up 14336x4096 + down 4096x14336 NVFP4 x q8_1, T=1 (configs[1]); "
+                               "weights repacked once into the tile-major NVFP4 layout (same bytes)",
                    "global_batch": 1, "seq_len": 1,
                    "parallelism": f"tp{world} (sharded over n_ff; the down matvec's epilogue stores its partial rows "
                                   f"into every rank over NVLink, one bounded wait + rank-order sum)" if world > 1

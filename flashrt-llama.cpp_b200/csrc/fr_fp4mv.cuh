@@ -90,15 +90,34 @@ __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, in
     // 1. the token's largest block-scale exponent (each CTA scans the row)
     int emax = -1000;
     if (x != nullptr) {
-        // eight independent loads in flight per thread, not one at a time
+        // many independent loads in flight per thread, 16-byte loads when the
+        // row allows them
         float am[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
         const float *row = x + static_cast<int64_t>(t) * ldx;
-        int k = threadIdx.x;
-        for (; k + 7 * 256 < K; k += 8 * 256) {
+        if ((reinterpret_cast<uintptr_t>(row) & 15) == 0 && (K & 3) == 0) {
+            const float4 *r4 = reinterpret_cast<const float4 *>(row);
+            const int K4 = K >> 2;
+            int k = threadIdx.x;
+            for (; k + 7 * 256 < K4; k += 8 * 256) {
+                float4 v[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) am[u] = fmaxf(am[u], fabsf(row[k + u * 256]));
+                for (int u = 0; u < 8; ++u) v[u] = r4[k + u * 256];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    am[u] = fmaxf(fmaxf(am[u], fmaxf(fabsf(v[u].x), fabsf(v[u].y))), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+            }
+            for (; k < K4; k += 256) {
+                const float4 v = r4[k];
+                am[0] = fmaxf(fmaxf(am[0], fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+            }
+        } else {
+            int k = threadIdx.x;
+            for (; k + 7 * 256 < K; k += 8 * 256) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) am[u] = fmaxf(am[u], fabsf(row[k + u * 256]));
+            }
+            for (; k < K; k += 256) am[0] = fmaxf(am[0], fabsf(row[k]));
         }
-        for (; k < K; k += 256) am[0] = fmaxf(am[0], fabsf(row[k]));
         float amax = am[0];
 #pragma unroll
         for (int u = 1; u < 8; ++u) amax = fmaxf(amax, am[u]);

@@ -1562,11 +1562,15 @@ int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks) {
     return tp_layout(T, n_embd, nranks).total;
 }
 
-int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard, const float *sg,
-                    const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
-                    int nranks, int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes,
-                    cudaStream_t stream) {
-    if (fault_hit("fr_tp_ffn_nvfp4")) return FR_EINJECTED;
+} // extern "C"
+
+namespace frb {
+// One rank's tensor-parallel FFN step; `tiled`: the shards are in the
+// tile-major layout (FP4 tensor-core matvecs), else ggml's layout.
+static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard,
+                       const float *sg, const float *su, const float *sd, const float *resid, float *out, int T,
+                       int n_embd, int n_ff, int nranks, int rank, void *const *peer_base, void *local_base,
+                       int64_t buffer_bytes, bool tiled, cudaStream_t stream) {
     if (!x || !wg_shard || !wu_shard || !wd_shard || !out || !peer_base || !local_base) return FR_EINVAL;
     if (T <= 0 || nranks <= 0 || nranks > 32 || rank < 0 || rank >= nranks) return FR_EINVAL;
     // the n_ff shard boundary falls on NVFP4 block (64) boundaries, so the
@@ -1590,15 +1594,24 @@ int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, 
     float *glu = static_cast<float *>(glu_p);
 
     unsigned expect;
-    if (use_tc(wg_shard, wu_shard, ld_gu, n_embd, T) && use_tc(wd_shard, nullptr, ld_d, F_p, T)) {
-        // batches: tensor-core matvecs, the partial output into this rank's
-        // own slot, then a push kernel stores it into every peer's slot
+    if (tiled || (use_tc(wg_shard, wu_shard, ld_gu, n_embd, T) && use_tc(wd_shard, nullptr, ld_d, F_p, T))) {
+        // tensor-core matvecs, the partial output into this rank's own slot,
+        // then a push kernel stores it into every peer's slot
         constexpr int PUSH_CTAS = 64;
-        rc = tcx_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), ld_gu, F_p,
-                       n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
-        if (rc != FR_OK) return rc;
-        rc = tcx_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, ld_d, n_embd, F_p, glu, F_p, nullptr, 0, T,
-                       sd, nullptr, nullptr, 0, reinterpret_cast<float *>(base + slot_off), n_embd, false, stream);
+        float *slot = reinterpret_cast<float *>(base + slot_off);
+        if (tiled) {
+            rc = fp4t_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), F_p,
+                             n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
+            if (rc != FR_OK) return rc;
+            rc = fp4t_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, n_embd, F_p, glu, F_p, nullptr, 0, T,
+                             sd, nullptr, nullptr, 0, slot, n_embd, false, stream);
+        } else {
+            rc = tcx_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), ld_gu,
+                            F_p, n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
+            if (rc != FR_OK) return rc;
+            rc = tcx_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, ld_d, n_embd, F_p, glu, F_p, nullptr, 0,
+                            T, sd, nullptr, nullptr, 0, slot, n_embd, false, stream);
+        }
         if (rc != FR_OK) return rc;
         rc = launch_pdl(k_tp_push, dim3(PUSH_CTAS), dim3(256), 0, stream, pb, nranks, rank, slot_off,
                         static_cast<int64_t>(n_embd), static_cast<int64_t>(0), T, n_embd, L.flags);
@@ -1656,6 +1669,29 @@ int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, 
     return launch_pdl(k_tp_reduce, dim3(TP_WAIT_CTAS), dim3(256), 0, stream, flags, seen, nranks, expect, parts,
                       n_out, resid, static_cast<int64_t>(n_embd), static_cast<int64_t>(n_embd), out,
                       static_cast<int64_t>(n_embd));
+}
+
+} // namespace frb
+
+extern "C" {
+
+int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard, const float *sg,
+                    const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                    int nranks, int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes,
+                    cudaStream_t stream) {
+    if (fault_hit("fr_tp_ffn_nvfp4")) return FR_EINJECTED;
+    return tp_ffn_impl(x, wg_shard, wu_shard, wd_shard, sg, su, sd, resid, out, T, n_embd, n_ff, nranks, rank,
+                       peer_base, local_base, buffer_bytes, false, stream);
+}
+
+int fr_tp_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void *wd_t, const float *sg,
+                    const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                    int nranks, int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes,
+                    cudaStream_t stream) {
+    if (fault_hit("fr_tp_ffn_tiled")) return FR_EINJECTED;
+    if (nranks <= 0 || n_embd % 256 != 0 || n_ff % (256 * nranks) != 0) return FR_EINVAL;
+    return tp_ffn_impl(x, wg_t, wu_t, wd_t, sg, su, sd, resid, out, T, n_embd, n_ff, nranks, rank, peer_base,
+                       local_base, buffer_bytes, true, stream);
 }
 
 } // extern "C"

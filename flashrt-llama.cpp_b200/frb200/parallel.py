@@ -143,14 +143,17 @@ class TpFfn:
         dist.barrier(group=group)
 
     def __call__(self, x, wg_shard, wu_shard, wd_kshard, sg=None, su=None, sd=None, resid=None, out=None,
-                 stream=None):
+                 stream=None, tiled=False):
+        """One step.  tiled: the shards are tile-major (frb200.tile_nvfp4 of
+        the gate/up row shards and of the down K-shard)."""
         import torch
         T = x.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
         if out is None:
             out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
-        call("fr_tp_ffn_nvfp4", _ptr(x), _ptr(wg_shard), _ptr(wu_shard), _ptr(wd_kshard), _ptr(sg), _ptr(su),
+        call("fr_tp_ffn_tiled" if tiled else "fr_tp_ffn_nvfp4", _ptr(x), _ptr(wg_shard), _ptr(wu_shard),
+             _ptr(wd_kshard), _ptr(sg), _ptr(su),
              _ptr(sd), _ptr(resid), _ptr(out), T, self.n_embd, self.n_ff, self.world, self.rank,
              _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes, _stream(stream))
         return out

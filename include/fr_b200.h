@@ -253,6 +253,13 @@ int fr_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void 
  * first use; local_base is this rank's own base.  All ranks call with the
  * same T.  The reference is single-device; no counterpart. */
 int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks);
+/* fr_tp_ffn_nvfp4 on tile-major shards (fr_nvfp4_tile of the gate/up row
+ * shards [F_p, n_embd] and of the down K-shard [n_embd, F_p]);
+ * n_ff % (256 * nranks) == 0 and n_embd % 256 == 0. */
+int fr_tp_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void *wd_t, const float *sg,
+                    const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                    int nranks, int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes,
+                    cudaStream_t stream);
 int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard,
                     const float *sg, const float *su, const float *sd, const float *resid, float *out,
                     int T, int n_embd, int n_ff, int nranks, int rank,

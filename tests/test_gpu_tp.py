@@ -76,8 +76,18 @@ def _worker(rank, world, port, q):
                 kw = dict(sg=sc[0:1], su=sc[1:2], sd=sc[2:3]) if i == 2 else {}
                 y = tp(x, *shards, resid=r, **kw)
                 check(y, frb200.ffn(x, wg, wu, wd, ne, nf, resid=r, **kw), f"path {path} T={T}", path == 2)
-        # the step captured in a CUDA graph and replayed with new inputs
+        # tile-major shards (FP4 tensor-core matvecs)
         frb200.set_matvec_path(0)
+        tshards = (frb200.tile_nvfp4(shards[0], nf // world, ne), frb200.tile_nvfp4(shards[1], nf // world, ne),
+                   frb200.tile_nvfp4(shards[2], ne, nf // world))
+        tpt = P.TpFfn(8, ne, nf)
+        tps.append(tpt)
+        for i, T in enumerate((1, 2, 8)):
+            x = t(frb200.synth_normal(110 + i, T * ne).reshape(T, ne))
+            r = t(frb200.synth_normal(115 + i, T * ne).reshape(T, ne))
+            y = tpt(x, *tshards, resid=r, tiled=True)
+            check(y, frb200.ffn(x, wg, wu, wd, ne, nf, resid=r), f"tiled T={T}", True)
+        # the step captured in a CUDA graph and replayed with new inputs
         tp = tps[0]
         xg = torch.empty((2, ne), dtype=torch.float32, device=dev)
         yg = torch.empty((2, ne), dtype=torch.float32, device=dev)
