@@ -86,6 +86,14 @@ __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, in
     const int nq = K / Q8_ELEMS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ int s_e[8];
+    // this CTA's q8_1 blocks, one warp each; the first block's value is
+    // loaded before the row scan so both loads are in flight together
+    const int per = (nq + gridDim.x - 1) / gridDim.x;
+    const int b_lo = blockIdx.x * per, b_hi = min(nq, b_lo + per);
+    const int b_first = b_lo + warp;
+    float x_first = 0.0f;
+    if (x != nullptr && b_first < b_hi)
+        x_first = x[static_cast<int64_t>(t) * ldx + static_cast<int64_t>(b_first) * Q8_ELEMS + lane];
 
     // 1. the token's largest block-scale exponent (each CTA scans the row)
     int emax = -1000;
@@ -149,13 +157,12 @@ __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, in
     }
 
     // 2. this CTA's q8_1 blocks, one warp each
-    const int per = (nq + gridDim.x - 1) / gridDim.x;
-    const int b_lo = blockIdx.x * per, b_hi = min(nq, b_lo + per);
-    for (int b = b_lo + warp; b < b_hi; b += 8) {
+    for (int b = b_first; b < b_hi; b += 8) {
         int q;
         __half hd;
         if (x != nullptr) {
-            const q8_lane r = q8_1_chunk(x[static_cast<int64_t>(t) * ldx + static_cast<int64_t>(b) * Q8_ELEMS + lane]);
+            const q8_lane r = q8_1_chunk(
+                b == b_first ? x_first : x[static_cast<int64_t>(t) * ldx + static_cast<int64_t>(b) * Q8_ELEMS + lane]);
             q = r.q;
             hd = __float2half_rn(r.d);
         } else {

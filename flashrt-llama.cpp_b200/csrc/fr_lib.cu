@@ -1151,8 +1151,10 @@ static int fp4t_launch(FtArgs a, int grid, cudaStream_t stream) {
     // stages; TMEM's 256 scale columns bound the weight ring
     const int extra = 2048;                                  // scale atom, factors, barriers
     const int cap = dev_info().smem_optin - 1024 - extra;
+    // the down projection (one matrix) follows the activation kernel of the
+    // GLU: a deeper ring prefetches more of its weights meanwhile
     int nb = 4;
-    int nw = std::max(2, std::min((110 * 1024 + S::WST - 1) / S::WST, 8));
+    int nw = std::max(2, std::min(((EPI == FM_PLAIN ? 184 : 110) * 1024 + S::WST - 1) / S::WST, 8));
     nw = std::min(nw, (256 - 4 * S::NI) / (16 * S::NI));
     // tuning override (FR_FP4T_RINGS="weights,activations"), within the limits
     static const char *ov = getenv("FR_FP4T_RINGS");
