@@ -288,23 +288,35 @@ def run_ours(args):
 
     sampler = ClockSampler(local)
     sampler.start()
-    t_end = time.time() + 1.5
+    # ~1.5 s of steps before timing (clocks settle).  Ranks run the same
+    # number of steps: the tensor-parallel step advances in lock step, so the
+    # count comes from the slowest rank's first chunk, agreed by all-reduce.
     with torch.cuda.stream(stream):
-        i = 0
-        while time.time() < t_end:
-            for _ in range(200):
+        t0 = time.time()
+        for i in range(200):
+            g1[i % N_SETS].replay()
+        stream.synchronize()
+        chunks = int(1.5 / max(time.time() - t0, 1e-4))
+        chunks = int(max_over_ranks(float(min(chunks, 1000))))
+        for c in range(chunks):
+            for i in range(200):
                 g1[i % N_SETS].replay()
-                i += 1
             stream.synchronize()
     ms1 = time_fn(lambda i: g1[i % N_SETS].replay(), args.steps, max(args.warmup, 3))
     clocks = sampler.stop()
 
     extra = {}
     for T in (8, 64):
-        gT = graphs_for(lambda i, T=T: ffn_step(i, T))
+        # T > 16 runs the tile-major FP4 kernel in windows of 16 tokens (each
+        # re-streaming the weights); on one GPU the ggml layout's f16
+        # tensor-core kernel reads them once for all 64 and is faster there
+        layout = "ggml" if (T > 16 and world == 1) else "tiled"
+        gT = graphs_for(lambda i, T=T, layout=layout: ffn_step(i, T, layout=layout))
         msT = time_fn(lambda i: gT[i % N_SETS].replay(), max(10, args.steps // 8), max(args.warmup, 3))
         extra[f"ffn_T{T}_gbs"] = round(ffn_bytes(T) / (msT * 1e-3) / 1e9, 1)
         extra[f"ffn_T{T}_ms_per_step"] = round(msT, 5)
+        extra[f"ffn_T{T}_path"] = ("ggml layout, f16 tensor-core matvec" if layout == "ggml"
+                                   else "tile-major layout, FP4 tensor-core matvec")
         del gT
     if world == 1:
         # ggml's in-place block_nvfp4 layout (no repack): the dp4a matvec
@@ -344,18 +356,17 @@ def run_ours(args):
 
     # ---------------- MoE layer (config 3): fused on one GPU, expert-parallel over ranks
     msets = _moe_sets(frb200, torch, dev, rank, world, 2)
+    ep = P.EpMoe(64, 2048, 768, 128, 8) if world > 1 else None
     for T in (1, 64):
         xm = torch.from_numpy(frb200.synth_normal(0x5EED3000 + rank * 131 + T, T * 2048).reshape(T, 2048)).to(dev)
         om = torch.empty((T, 2048), dtype=torch.float32, device=dev)
         if world == 1:
             mg = graphs_for(lambda i, xm=xm, om=om: frb200.moe_ffn(xm, *msets[i % 2], 2048, 768, 128, 8, out=om,
                                                                   stream=stream))
-            mms = time_fn(lambda i: mg[i % N_SETS].replay(), max(20, args.steps // 4), max(args.warmup, 3))
-            del mg
         else:
-            with torch.cuda.stream(stream):
-                mms = time_fn(lambda i, xm=xm: P.ep_moe(xm, *msets[i % 2], 2048, 768, 128, 8),
-                              max(10, args.steps // 10), max(args.warmup, 3))
+            mg = graphs_for(lambda i, xm=xm, om=om: ep(xm, *msets[i % 2], out=om, stream=stream))
+        mms = time_fn(lambda i: mg[i % N_SETS].replay(), max(20, args.steps // 4), max(args.warmup, 3))
+        del mg
         extra[f"moe_T{T}_tok_s"] = round(world * T / (mms * 1e-3), 1)
         extra[f"moe_T{T}_ms_per_layer"] = round(mms, 5)
 
@@ -380,8 +391,9 @@ def run_ours(args):
                    else "single GPU",
                    "l2": f"rotating {N_SETS} weight sets ({N_SETS * ffn_bytes(0) / 1e6:.0f} MB > L2)",
                    "graph": "one CUDA graph per step (PDL edges between kernels; no NCCL call on the tp step)",
-                   "moe": "config 3 layer (E=128, top-8, hidden 2048, FFN 768): fused on 1 GPU, expert-parallel "
-                          "(E/N experts per rank, all-to-all of routed rows, per-rank tokens) for N > 1"},
+                   "moe": "config 3 layer (E=128, top-8, hidden 2048, FFN 768): fused on 1 GPU; for N > 1 expert-parallel "
+                          "(E/N experts per rank, per-rank tokens, routed rows and outputs exchanged by NVLink peer "
+                          "stores, bounded waits, one CUDA graph per layer)"},
         "clocks": clocks,
         "e2e": {"value": round(ffn_bytes(1) / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": N_EMBD * 4, "d2h_bytes_per_step": N_EMBD * 4,
@@ -394,6 +406,8 @@ def run_ours(args):
     del g1, egs
     if tp is not None:
         tp.close()
+    if ep is not None:
+        ep.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -402,17 +416,28 @@ def run_ours(args):
 
 
 def run_profile_case(args):
-    """A short, fixed sequence of the hot kernels for profiler captures: four
-    rotating weight sets (> L2) of config 2, `--steps` dense FFN steps at
-    T = --tokens (the q8_1 / activation-column kernel, the gate/up SwiGLU
-    matvec, the down matvec), synchronised after each step.  Prints nothing
-    but a done line; never a benchmark number."""
+    """A short, fixed sequence of the hot kernels for profiler captures:
+    `--case ffn`: four rotating weight sets (> L2) of config 2, `--steps` dense
+    FFN steps at T = --tokens (the q8_1 / activation-column kernel, the gate/up
+    SwiGLU matvec, the down matvec); `--case moe`: two config-3 layers
+    alternating.  Synchronised after each step.  Prints nothing but a done
+    line; never a benchmark number."""
     import torch
     import frb200
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     if args.matvec is not None:
         frb200.set_matvec_path(args.matvec)
+    if args.case == "moe":
+        msets = _moe_sets(frb200, torch, dev, 0, 1, 2)
+        T = args.tokens
+        xm = torch.from_numpy(frb200.synth_normal(0x5EED3000 + T, T * 2048).reshape(T, 2048)).to(dev)
+        om = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+        for i in range(args.steps):
+            frb200.moe_ffn(xm, *msets[i % 2], 2048, 768, 128, 8, out=om)
+            torch.cuda.synchronize()
+        print(f"profile case done: {args.steps} MoE layers, T={T}, status {frb200.device_status()}")
+        return
     sets = []
     for s in range(N_SETS):
         base = 0x5EED0000 + 100 * s
@@ -448,6 +473,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step of --profile-case")
     ap.add_argument("--matvec", type=int, default=None, help="force the matvec kernel (1 dp4a, 2 tc-f16, 3 tc-fp4)")
     ap.add_argument("--layout", choices=["ggml", "tiled"], default="ggml", help="weight layout of --profile-case")
+    ap.add_argument("--case", choices=["ffn", "moe"], default="ffn", help="workload of --profile-case")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)

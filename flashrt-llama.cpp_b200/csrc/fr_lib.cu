@@ -758,7 +758,7 @@ int fr_mul_mat_id_nvfp4(const void *w, int64_t nb01, int64_t nb02, int E, const 
     rc = allow_max_smem(k_group_ids, attr_done);
     if (rc != FR_OK) return rc;
     rc = launch_pdl(k_group_ids, dim3(1), dim3(1024), group_smem(T, n_used), stream, ids, ids_ld, T, n_used, E, eoff,
-                    slots, act);
+                    slots, act, 0);
     if (rc != FR_OK) return rc;
     rc = bcast ? quantize_launch2(x, x_ld_tok, 1, 0, q8, K / 32, T, K, stream)
                : quantize_launch2(x, x_ld_tok, n_used, x_ld_slot, q8, K / 32, T * n_used, K, stream);
@@ -1347,10 +1347,15 @@ static int fp4_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N,
 // ======================================================================
 extern "C" {
 
-int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S, const void *wg, const void *wu,
-                         const void *wd, const float *sg, const float *su, const float *sd, float *out, int64_t ldo,
-                         int n_embd, int n_ff, int E, cudaStream_t stream) {
-    if (fault_hit("fr_moe_experts_nvfp4")) return FR_EINJECTED;
+} // extern "C"
+
+namespace frb {
+// Expert FFN over pre-routed rows; skip_neg: rows with expert id -1 are empty
+// slots of a fixed-capacity exchange and are left out (their output rows are
+// not written).
+static int moe_experts_impl(const float *x, int64_t ldx, const int32_t *eid, int S, const void *wg, const void *wu,
+                            const void *wd, const float *sg, const float *su, const float *sd, float *out, int64_t ldo,
+                            int n_embd, int n_ff, int E, int skip_neg, cudaStream_t stream) {
     if (S < 0 || E <= 0 || E > MOE_MAX_E || n_embd <= 0 || n_ff <= 0) return FR_EINVAL;
     if (S == 0) return FR_OK;
     if (!x || !eid || !wg || !wu || !wd || !out || n_embd % 64 != 0 || n_ff % 64 != 0) return FR_EINVAL;
@@ -1383,7 +1388,7 @@ int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S,
     if (rc != FR_OK) return rc;
     // each row is one "token" with one slot
     rc = launch_pdl(k_group_ids, dim3(1), dim3(1024), group_smem(S, 1), stream, eid, static_cast<int64_t>(1), S, 1, E,
-                    eoff, slots, act);
+                    eoff, slots, act, skip_neg);
     if (rc != FR_OK) return rc;
     rc = quantize_launch(x, ldx, q8x, n_embd / 32, S, n_embd, stream);
     if (rc != FR_OK) return rc;
@@ -1431,6 +1436,16 @@ int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S,
     q.ld_tok = ldo;
     q.ld_slot = 0;
     return moe_launch<false>(q, max_active, S, stream);
+}
+} // namespace frb
+
+extern "C" {
+
+int fr_moe_experts_nvfp4(const float *x, int64_t ldx, const int32_t *eid, int S, const void *wg, const void *wu,
+                         const void *wd, const float *sg, const float *su, const float *sd, float *out, int64_t ldo,
+                         int n_embd, int n_ff, int E, cudaStream_t stream) {
+    if (fault_hit("fr_moe_experts_nvfp4")) return FR_EINJECTED;
+    return moe_experts_impl(x, ldx, eid, S, wg, wu, wd, sg, su, sd, out, ldo, n_embd, n_ff, E, 0, stream);
 }
 
 int fr_moe_combine(const float *part, const float *wts, const float *resid, float *out, int T, int n_used, int n_embd,
@@ -1528,6 +1543,107 @@ int fr_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void 
     if (rc != FR_OK) return rc;
     return fp4t_matvec(static_cast<const uint8_t *>(wd_t), nullptr, n_embd, n_ff, glu, n_ff, nullptr, 0, T, sd,
                        nullptr, resid, n_embd, out, n_embd, false, stream);
+}
+
+} // extern "C"
+
+namespace frb {
+// expert-parallel exchange buffer (see k_ep_dispatch)
+struct EpLayout {
+    int64_t flags_d, flags_r, seen_d, seen_r, recv_x, recv_eid, back, total;
+};
+static EpLayout ep_layout(int T, int n_embd, int n_used, int P) {
+    const int64_t cap = static_cast<int64_t>(T) * n_used;
+    EpLayout l{};
+    l.flags_d = 0;
+    l.flags_r = 128;
+    l.seen_d = 256;
+    l.seen_r = 384;
+    l.recv_x = 512;
+    l.recv_eid = l.recv_x + (P * cap * n_embd * 4 + 255) / 256 * 256;
+    l.back = l.recv_eid + (P * cap * 4 + 255) / 256 * 256;
+    l.total = l.back + (cap * n_embd * 4 + 255) / 256 * 256;
+    return l;
+}
+} // namespace frb
+
+extern "C" {
+
+int64_t fr_ep_buffer_bytes(int T_max, int n_embd, int n_used, int nranks) {
+    if (T_max <= 0 || n_embd <= 0 || n_used <= 0 || nranks <= 0) return -1;
+    return ep_layout(T_max, n_embd, n_used, nranks).total;
+}
+
+int fr_ep_moe_nvfp4(const float *x, const float *w_r, const void *wg_local, const void *wu_local,
+                    const void *wd_local, const float *sg, const float *su, const float *sd, const float *resid,
+                    float *out, int T, int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val, int nranks,
+                    int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream) {
+    if (fault_hit("fr_ep_moe_nvfp4")) return FR_EINJECTED;
+    int rc = check_route_shape(T, n_embd, E, n_used);
+    if (rc != FR_OK) return rc;
+    if (!x || !w_r || !wg_local || !wu_local || !wd_local || !out || !peer_base || !local_base) return FR_EINVAL;
+    if (nranks <= 0 || nranks > 32 || rank < 0 || rank >= nranks || E % nranks != 0 || T > T_max) return FR_EINVAL;
+    if (n_embd % 64 != 0 || n_ff % 64 != 0 || !aligned16(x) || !aligned16(w_r)) return FR_EINVAL;
+    const int cap = T_max * n_used;
+    if (static_cast<int64_t>(nranks) * cap > MOE_MAX_SLOTS) return FR_EINVAL;
+    const EpLayout L = ep_layout(T_max, n_embd, n_used, nranks);
+    if (buffer_bytes < L.total) return FR_EINVAL;
+    uint8_t *base = static_cast<uint8_t *>(local_base);
+    uint8_t *const *pb = reinterpret_cast<uint8_t *const *>(peer_base);
+    const int E_p = E / nranks;
+    const int S = T * n_used;
+    // routing (replicated router) and this rank's expert outputs live in a
+    // workspace of their own: the expert FFN uses the MoE workspace
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_logits = take(static_cast<size_t>(T) * E * 4);
+    const size_t o_ids = take(static_cast<size_t>(S) * 4);
+    const size_t o_wts = take(static_cast<size_t>(S) * 4);
+    const size_t o_eoff = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_act = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_slots = take(static_cast<size_t>(S) * 4);
+    const size_t o_y = take(static_cast<size_t>(nranks) * cap * n_embd * 4);
+    void *wsp = nullptr;
+    rc = workspace_get(WS_ACT2, off, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    uint8_t *w = static_cast<uint8_t *>(wsp);
+    int32_t *ids = reinterpret_cast<int32_t *>(w + o_ids);
+    float *wts = reinterpret_cast<float *>(w + o_wts);
+    float *y = reinterpret_cast<float *>(w + o_y);
+    rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, reinterpret_cast<float *>(w + o_logits), ids,
+                      wts, reinterpret_cast<int32_t *>(w + o_eoff), reinterpret_cast<int32_t *>(w + o_slots),
+                      reinterpret_cast<int32_t *>(w + o_act), stream);
+    if (rc != FR_OK) return rc;
+    // rows to the expert owners
+    rc = launch_pdl(k_ep_dispatch, dim3(EP_CTAS), dim3(256), 0, stream, x, static_cast<int64_t>(n_embd),
+                    static_cast<const int32_t *>(ids), S, cap, n_used, E_p, n_embd, pb, nranks, rank, L.recv_x,
+                    L.recv_eid, L.flags_d);
+    if (rc != FR_OK) return rc;
+    rc = launch_pdl(k_tp_reduce, dim3(1), dim3(256), 0, stream, reinterpret_cast<const unsigned int *>(base + L.flags_d),
+                    reinterpret_cast<unsigned int *>(base + L.seen_d), nranks, static_cast<unsigned>(EP_CTAS),
+                    static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<const float *>(nullptr),
+                    static_cast<int64_t>(0), static_cast<int64_t>(1), static_cast<float *>(nullptr),
+                    static_cast<int64_t>(0));
+    if (rc != FR_OK) return rc;
+    // this rank's experts over everything it received (empty slots skipped)
+    rc = moe_experts_impl(reinterpret_cast<const float *>(base + L.recv_x), n_embd,
+                          reinterpret_cast<const int32_t *>(base + L.recv_eid), nranks * cap, wg_local, wu_local,
+                          wd_local, sg, su, sd, y, n_embd, n_embd, n_ff, E_p, 1, stream);
+    if (rc != FR_OK) return rc;
+    // outputs back to the slots they came from
+    rc = launch_pdl(k_ep_return, dim3(EP_CTAS), dim3(256), 0, stream, static_cast<const float *>(y),
+                    reinterpret_cast<const int32_t *>(base + L.recv_eid), cap, n_embd, pb, nranks, rank, L.back,
+                    L.flags_r);
+    if (rc != FR_OK) return rc;
+    rc = launch_pdl(k_tp_reduce, dim3(1), dim3(256), 0, stream, reinterpret_cast<const unsigned int *>(base + L.flags_r),
+                    reinterpret_cast<unsigned int *>(base + L.seen_r), nranks, static_cast<unsigned>(EP_CTAS),
+                    static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<const float *>(nullptr),
+                    static_cast<int64_t>(0), static_cast<int64_t>(1), static_cast<float *>(nullptr),
+                    static_cast<int64_t>(0));
+    if (rc != FR_OK) return rc;
+    return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream,
+                      reinterpret_cast<const float *>(base + L.back), static_cast<const float *>(wts), resid, out,
+                      n_used, n_embd);
 }
 
 int fr_ipc_alloc(int64_t bytes, void **dev_ptr, void *handle64) {

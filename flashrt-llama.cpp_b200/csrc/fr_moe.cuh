@@ -190,10 +190,12 @@ __global__ void __launch_bounds__(1024) k_topk_group(const float *__restrict__ l
 }
 
 // permute for caller-given ids [T, n_used] (row stride ids_ld); out-of-range
-// ids are flagged in the status word and routed to no expert.
+// ids are flagged in the status word and routed to no expert, except -1 when
+// `skip_neg` is set (an empty slot of a fixed-capacity exchange).
 __global__ void __launch_bounds__(1024) k_group_ids(const int32_t *__restrict__ ids, int64_t ids_ld, int T,
                                                     int n_used, int E, int32_t *__restrict__ eoff,
-                                                    int32_t *__restrict__ slots, int32_t *__restrict__ act) {
+                                                    int32_t *__restrict__ slots, int32_t *__restrict__ act,
+                                                    int skip_neg) {
     fr_pdl_wait();
     fr_pdl_trigger();
     extern __shared__ int32_t sm_i[];
@@ -203,7 +205,7 @@ __global__ void __launch_bounds__(1024) k_group_ids(const int32_t *__restrict__ 
     for (int s = threadIdx.x; s < T * n_used; s += blockDim.x) {
         int e = ids[static_cast<int64_t>(s / n_used) * ids_ld + s % n_used];
         if (e < 0 || e >= E) {
-            fr_flag(FR_ST_BADINPUT);
+            if (!(skip_neg && e == -1)) fr_flag(FR_ST_BADINPUT);
             e = -1;
         }
         ids_s[s] = e;
@@ -387,6 +389,75 @@ __global__ void __launch_bounds__(256) k_moe_combine(const float *__restrict__ p
     for (int k = 1; k < n_used; ++k) sum += pt[static_cast<int64_t>(k) * n_embd] * ws[k];
     if (resid) sum = sum + resid[static_cast<int64_t>(t) * n_embd + r];
     out[static_cast<int64_t>(t) * n_embd + r] = sum;
+}
+
+// ------------------------------------------------------------ expert parallel
+// Fixed-capacity exchange buffers, one per rank, mapped by every peer (CUDA
+// IPC): [flags 64 u32 (32 dispatch, 32 return)][consumed counts of the two
+// waits][recv_x P x cap x K f32][recv_eid P x cap i32][back cap x K f32],
+// cap = T_max * n_used slots.  Slot s of token t is t * n_used + k.
+constexpr int EP_CTAS = 64;
+
+// Dispatch: every slot's activation row goes to the expert owner's recv_x at
+// [this rank][slot], with the owner-local expert id; every other rank gets -1
+// for that slot, and slots past S (this call's T * n_used) get -1 everywhere,
+// so each call rewrites the whole [this rank] band of every peer.  Each CTA
+// then counts itself into every rank's dispatch flag[rank].
+__global__ void __launch_bounds__(256) k_ep_dispatch(const float *__restrict__ x, int64_t ldx,
+                                                     const int32_t *__restrict__ ids, int S, int cap, int n_used,
+                                                     int E_p, int K, uint8_t *const *peer_base, int npeers, int rank,
+                                                     int64_t off_x, int64_t off_eid, int64_t flag_off) {
+    fr_pdl_wait();
+    const int per = (cap + gridDim.x - 1) / gridDim.x;
+    const int s_lo = blockIdx.x * per, s_hi = min(cap, s_lo + per);
+    for (int s = s_lo; s < s_hi; ++s) {
+        const int e = s < S ? ids[s] : -1;
+        const int dest = e >= 0 ? e / E_p : -1;
+        if (threadIdx.x < npeers) {
+            int32_t *eid = reinterpret_cast<int32_t *>(peer_base[threadIdx.x] + off_eid) +
+                           static_cast<int64_t>(rank) * cap + s;
+            *eid = static_cast<int>(threadIdx.x) == dest ? e - dest * E_p : -1;
+        }
+        if (dest >= 0) {
+            const float4 *src = reinterpret_cast<const float4 *>(x + static_cast<int64_t>(s / n_used) * ldx);
+            float4 *dst = reinterpret_cast<float4 *>(peer_base[dest] + off_x) +
+                          (static_cast<int64_t>(rank) * cap + s) * (K / 4);
+            for (int i = threadIdx.x; i < K / 4; i += blockDim.x) dst[i] = src[i];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < npeers; ++q)
+            atomicAdd_system(reinterpret_cast<unsigned int *>(peer_base[q] + flag_off) + rank, 1u);
+    }
+    fr_pdl_trigger();
+}
+
+// Return: the expert outputs of the rows this rank received (y [P x cap, K])
+// go back to the source rank's `back` at the slot they came from; then each
+// CTA counts itself into every rank's return flag[rank].
+__global__ void __launch_bounds__(256) k_ep_return(const float *__restrict__ y, const int32_t *__restrict__ recv_eid,
+                                                   int cap, int K, uint8_t *const *peer_base, int npeers, int rank,
+                                                   int64_t off_back, int64_t flag_off) {
+    fr_pdl_wait();
+    const int rows = npeers * cap;
+    const int per = (rows + gridDim.x - 1) / gridDim.x;
+    const int r_lo = blockIdx.x * per, r_hi = min(rows, r_lo + per);
+    for (int r = r_lo; r < r_hi; ++r) {
+        if (recv_eid[r] < 0) continue;
+        const int src = r / cap, s = r % cap;
+        const float4 *from = reinterpret_cast<const float4 *>(y + static_cast<int64_t>(r) * K);
+        float4 *to = reinterpret_cast<float4 *>(peer_base[src] + off_back) + static_cast<int64_t>(s) * (K / 4);
+        for (int i = threadIdx.x; i < K / 4; i += blockDim.x) to[i] = from[i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < npeers; ++q)
+            atomicAdd_system(reinterpret_cast<unsigned int *>(peer_base[q] + flag_off) + rank, 1u);
+    }
+    fr_pdl_trigger();
 }
 
 } // namespace frb

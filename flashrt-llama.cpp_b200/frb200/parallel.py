@@ -101,27 +101,19 @@ def tp_ffn(x, wg_shard, wu_shard, wd_kshard, n_embd, n_ff, resid=None, group=Non
     return y if resid is None else y + resid
 
 
-class TpFfn:
-    """Tensor-parallel dense FFN with the reduction fused into the down
-    matvec's epilogue: each rank's down matvec stores its partial output rows
-    straight into its slot on every rank over NVLink (CUDA IPC peer mappings,
-    no multicast object) and counts finished CTAs into per-rank flags; a
-    bounded wait kernel sums the slots in rank order.  No NCCL call on the
-    step; the step is one stream of kernels and is CUDA-graph capturable.
+class _PeerBuffer:
+    """One device buffer per rank, mapped into every other rank's process by
+    CUDA IPC (no multicast object); `peer_ptrs` is the device array of the
+    ranks' base addresses the library's multi-GPU entries take."""
 
-    `max_tokens` sizes the shared buffer; every call must use the same token
-    count on all ranks (ranks advance in lock step)."""
-
-    def __init__(self, max_tokens, n_embd, n_ff, group=None):
+    def __init__(self, nbytes, group=None):
         import torch
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.n_embd, self.n_ff, self.max_tokens = n_embd, n_ff, max_tokens
-        L = lib()
-        self.nbytes = int(L.fr_tp_buffer_bytes(max_tokens, n_embd, n_ff, self.world))
+        self.nbytes = int(nbytes)
         if self.nbytes <= 0:
-            raise ValueError("bad tensor-parallel FFN shape")
+            raise ValueError("bad exchange buffer size")
         local = C.c_void_p()
         handle = (C.c_ubyte * 64)()
         call("fr_ipc_alloc", self.nbytes, C.byref(local), handle)
@@ -142,22 +134,6 @@ class TpFfn:
         self.peer_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=torch.cuda.current_device())
         dist.barrier(group=group)
 
-    def __call__(self, x, wg_shard, wu_shard, wd_kshard, sg=None, su=None, sd=None, resid=None, out=None,
-                 stream=None, tiled=False):
-        """One step.  tiled: the shards are tile-major (frb200.tile_nvfp4 of
-        the gate/up row shards and of the down K-shard)."""
-        import torch
-        T = x.shape[0]
-        if T > self.max_tokens:
-            raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
-        if out is None:
-            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
-        call("fr_tp_ffn_tiled" if tiled else "fr_tp_ffn_nvfp4", _ptr(x), _ptr(wg_shard), _ptr(wu_shard),
-             _ptr(wd_kshard), _ptr(sg), _ptr(su),
-             _ptr(sd), _ptr(resid), _ptr(out), T, self.n_embd, self.n_ff, self.world, self.rank,
-             _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes, _stream(stream))
-        return out
-
     def close(self):
         """Release the mappings (all ranks, after their last step has finished)."""
         import torch
@@ -171,6 +147,68 @@ class TpFfn:
         dist.barrier(group=self.group)
         call("fr_ipc_free", C.c_void_p(self.local))
         self.local = None
+
+
+class TpFfn(_PeerBuffer):
+    """Tensor-parallel dense FFN with the reduction fused into the down
+    matvec's epilogue: each rank's down matvec stores its partial output rows
+    straight into its slot on every rank over NVLink (CUDA IPC peer mappings,
+    no multicast object) and counts finished CTAs into per-rank flags; a
+    bounded wait kernel sums the slots in rank order.  No NCCL call on the
+    step; the step is one stream of kernels and is CUDA-graph capturable.
+
+    `max_tokens` sizes the shared buffer; every call must use the same token
+    count on all ranks (ranks advance in lock step)."""
+
+    def __init__(self, max_tokens, n_embd, n_ff, group=None):
+        world = dist.get_world_size(group)
+        super().__init__(lib().fr_tp_buffer_bytes(max_tokens, n_embd, n_ff, world), group)
+        self.n_embd, self.n_ff, self.max_tokens = n_embd, n_ff, max_tokens
+
+    def __call__(self, x, wg_shard, wu_shard, wd_kshard, sg=None, su=None, sd=None, resid=None, out=None,
+                 stream=None, tiled=False):
+        """One step.  tiled: the shards are tile-major (frb200.tile_nvfp4 of
+        the gate/up row shards and of the down K-shard)."""
+        import torch
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
+        call("fr_tp_ffn_tiled" if tiled else "fr_tp_ffn_nvfp4", _ptr(x), _ptr(wg_shard), _ptr(wu_shard),
+             _ptr(wd_kshard), _ptr(sg), _ptr(su), _ptr(sd), _ptr(resid), _ptr(out), T, self.n_embd, self.n_ff,
+             self.world, self.rank, _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes, _stream(stream))
+        return out
+
+
+class EpMoe(_PeerBuffer):
+    """Expert-parallel MoE layer over NVLink peer stores (fr_ep_moe_nvfp4):
+    this rank's E/P experts, its own tokens; routed rows go to the expert
+    owners and outputs come back through fixed-capacity exchange buffers, with
+    bounded waits and no host synchronisation (CUDA-graph capturable).  The
+    result equals the single-GPU layer.  Every call uses the same T on all
+    ranks, T <= max_tokens."""
+
+    def __init__(self, max_tokens, n_embd, n_ff, E, n_used, group=None):
+        world = dist.get_world_size(group)
+        if E % world:
+            raise ValueError(f"{E} experts do not split over {world} ranks")
+        super().__init__(lib().fr_ep_buffer_bytes(max_tokens, n_embd, n_used, world), group)
+        self.max_tokens, self.n_embd, self.n_ff, self.E, self.n_used = max_tokens, n_embd, n_ff, E, n_used
+
+    def __call__(self, x, w_r, wg_local, wu_local, wd_local, sg=None, su=None, sd=None, resid=None, out=None,
+                 clamp=6.103515625e-5, stream=None):
+        import torch
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
+        call("fr_ep_moe_nvfp4", _ptr(x), _ptr(w_r), _ptr(wg_local), _ptr(wu_local), _ptr(wd_local), _ptr(sg), _ptr(su),
+             _ptr(sd), _ptr(resid), _ptr(out), T, self.max_tokens, self.n_embd, self.n_ff, self.E, self.n_used,
+             clamp, self.world, self.rank, _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes,
+             _stream(stream))
+        return out
 
 
 def _exchange(send: torch.Tensor, send_counts, recv_counts, group=None) -> torch.Tensor:

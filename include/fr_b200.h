@@ -265,6 +265,25 @@ int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, 
                     int T, int n_embd, int n_ff, int nranks, int rank,
                     void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream);
 
+/* ------------------------------------------------------ (e) expert parallel
+ * One rank's step of the MoE layer with E/P experts per rank (rank r owns
+ * experts [r*E/P, (r+1)*E/P); wg/wu/wd_local hold their rows) and its own T
+ * tokens.  The router runs replicated; every routed slot's activation row is
+ * stored into the expert owner's exchange buffer over NVLink (fixed capacity
+ * T_max * n_used slots per source rank, empty slots marked), a bounded wait
+ * sees every rank's rows in, the owner runs its experts, the outputs go back
+ * to the source slots the same way, and the token owner combines them in slot
+ * order -- the arithmetic and order of fr_moe_ffn_nvfp4 on one GPU, so the
+ * result is identical.  No host synchronisation; CUDA-graph capturable.
+ * peer_base / local_base: a buffer of fr_ep_buffer_bytes(T_max, n_embd,
+ * n_used, P) bytes per rank as for fr_tp_ffn_nvfp4.  All ranks call with the
+ * same T.  The reference is single-device; no counterpart. */
+int64_t fr_ep_buffer_bytes(int T_max, int n_embd, int n_used, int nranks);
+int fr_ep_moe_nvfp4(const float *x, const float *w_r, const void *wg_local, const void *wu_local,
+                    const void *wd_local, const float *sg, const float *su, const float *sd, const float *resid,
+                    float *out, int T, int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val, int nranks,
+                    int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream);
+
 /* Peer buffers for fr_tp_ffn_nvfp4 without any library-side multicast
  * object: fr_ipc_alloc returns a zeroed device buffer and its 64-byte CUDA
  * IPC handle (exchanged between the ranks by the host), fr_ipc_open maps a
