@@ -1,0 +1,364 @@
+// fr_fp4moe.cuh -- the MoE expert matvecs (the per-expert GEMV/GEMM of
+// mul_mat_id, src/fr_win_flint_batched_moe.cuh:180-340 in the reference) on
+// the FP4 tensor cores, with every expert's matrix in the tile-major NVFP4
+// layout of fr_fp4tile.cuh (the stacked [E * N, K] matrix repacked at once:
+// expert e's tiles start at e * e_stride).
+//
+// Work.  The routing's grouping (eoff / slots / act) lists each active
+// expert's slots in slot order.  They are cut into windows of at most TMAX
+// tokens (8 * TMAX = NCOL activation columns, the MMA's N); a unit is
+// (window, row block of 128, K stage of 256), and the units are divided evenly
+// over the CTAs in that order (stream-K, as k_fp4t), so every row block of
+// every used expert is streamed from HBM once per window -- once per call
+// unless more than TMAX tokens chose the expert.  The windows are counted on
+// the device from the grouping, so the launch needs no host sync and can be
+// captured in a CUDA graph.
+//
+// Activation.  k_act_fp4 writes one image per source row (a token for the
+// gate/up pair, a slot for the down projection): per K stage one 1024-byte
+// 128-byte-swizzled atom of its eight E2M1 digit columns.  The activation
+// producer gathers the window's atoms into the stage buffer (token i at rows
+// [8i, 8i+8)); rows past the window keep stale bytes, which are valid E2M1
+// codes and only reach accumulator columns that are never read.
+//
+// Epilogue.  Column factors (9^p 2^(E0+1), per source row) and output rows are
+// staged per window in each epilogue warp's own shared-memory copy (no barrier
+// between warps inside the loop, so a warp whose wait timed out holds no one).
+// SwiGLU with per-expert scales writes the GLU row of each slot; the plain
+// form writes each slot's projected row.  Row blocks shared by several CTAs
+// are finished by the last to arrive, adding the partials in CTA order.
+#pragma once
+
+#include "fr_fp4tile.cuh"
+
+namespace frb {
+
+constexpr int FE_MAX_E = 256;                  // experts (one scan entry per thread)
+
+struct FeArgs {
+    int N, K;                    // rows per expert, row length
+    int n_kq, n_rb;              // K stages of 256, row blocks of 128 per expert
+    int E, n_used, bcast;        // source row of slot s: bcast ? s / n_used : s
+    const int32_t *eoff, *slots, *act;
+    const uint8_t *w0, *w1;      // tiled expert matrices; w1 = up for the SwiGLU pair
+    int64_t e_stride;            // bytes per expert
+    const uint8_t *img;          // per source row: n_kq atoms of 1024 B (k_act_fp4, t_stride = n_kq * 1024)
+    const float *gtab;           // per source row: 8 column factors
+    const float *s0, *s1;        // per-expert scales [E] (nullable)
+    float *y;                    // output row of slot s = t * n_used + k at y + t * ld_tok + k * ld_slot
+    int64_t ld_tok, ld_slot;
+    float *part;                 // [grid][2: first / last segment][2: matrix][TMAX][128]
+    unsigned int *counter;       // [max_rbg][4 quadrants], zero on entry, reset by the last arrival
+    int max_rbg;                 // window row blocks the counters cover
+    int n_w, n_b;                // ring depths
+};
+
+// shared-memory bytes past the two rings
+__host__ __device__ constexpr int fe_extra_bytes() {
+    return 512 + 4 * (16 * FM_GSTRIDE * 4) + 4 * 16 * 8 + (FE_MAX_E + 1) * 4 + 64 + 64 * 8 + 16;
+}
+
+template <int NCOL, int EPI>
+__global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
+    using S = FtShape<NCOL, EPI, 1>;
+    constexpr int NI = S::NI;
+    constexpr bool DUAL = S::NM == 2;
+    constexpr int TMAX = S::TMAX;
+    constexpr uint32_t TMEM_COLS = 512;
+    static_assert(NI * NCOL <= 256, "accumulators live in TMEM columns [0, 256)");
+    static_assert(TMAX <= 16, "window factor tables hold 16 tokens");
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int NW = g.n_w, NB = g.n_b;
+    uint8_t *w_ring = smem;
+    uint8_t *b_ring = w_ring + static_cast<size_t>(NW) * S::WST;
+    uint8_t *sfb_const = b_ring + static_cast<size_t>(NB) * S::BST;      // 512 B
+    float *gtab_w = reinterpret_cast<float *>(sfb_const + 512);            // [4 warps][16 * 8]
+    int64_t *orow_w = reinterpret_cast<int64_t *>(gtab_w + 4 * 16 * FM_GSTRIDE); // [4 warps][16]
+    int *win_off = reinterpret_cast<int *>(orow_w + 4 * 16);                       // [FE_MAX_E + 1]
+    int *wsum = win_off + FE_MAX_E + 1;                                    // [8] warp sums of the scan
+    uint64_t *wfull = reinterpret_cast<uint64_t *>(
+        (reinterpret_cast<uintptr_t>(wsum + 16) + 7) & ~uintptr_t(7));
+    uint64_t *wempty = wfull + NW;
+    uint64_t *bfull = wempty + NW;
+    uint64_t *bempty = bfull + NB;
+    uint64_t *accfull = bempty + NB;
+    uint64_t *accempty = accfull + 1;
+    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(accempty + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NW; ++s) {
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], NI);
+        }
+        for (int s = 0; s < NB; ++s) {
+            mbar_init(&bfull[s], 1);
+            mbar_init(&bempty[s], NI);
+        }
+        mbar_init(accfull, NI);
+        mbar_init(accempty, 4);
+        fence_mbar_init();
+    }
+    if (warp == 3) {
+        reinterpret_cast<uint4 *>(sfb_const)[lane] = make_uint4(FM_SFB * 0x01010101u, FM_SFB * 0x01010101u,
+                                                                FM_SFB * 0x01010101u, FM_SFB * 0x01010101u);
+        fence_proxy_async();
+    }
+    if (warp == 1) tmem_alloc(tmem_s, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_s;
+    const uint32_t tD = tbase;
+    fr_pdl_trigger();
+    fr_pdl_wait();                                           // the grouping and the activation images
+
+    // windows per active expert -> exclusive prefix win_off (one entry per thread)
+    const int n_act = min(max(g.act[g.E], 0), g.E);
+    {
+        const int i = threadIdx.x;
+        int nw = 0;
+        if (i < n_act) {
+            const int e = g.act[i];
+            if (e >= 0 && e < g.E) nw = (g.eoff[e + 1] - g.eoff[e] + TMAX - 1) / TMAX;
+        }
+        int inc = nw;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, inc, off);
+            if (lane >= off) inc += v;
+        }
+        if (lane == 31) wsum[warp] = inc;
+        __syncthreads();
+        int base = 0;
+        for (int w = 0; w < warp; ++w) base += wsum[w];
+        win_off[i + 1] = base + inc;
+        if (i == 0) win_off[0] = 0;
+        __syncthreads();
+    }
+    const int W = win_off[n_act];
+    const int nsr = g.n_kq;
+    int U = W * g.n_rb * nsr;
+    if (W * g.n_rb > g.max_rbg) {
+        if (threadIdx.x == 0) fr_flag(FR_ST_BADINPUT);
+        U = 0;
+    }
+    const int G = min(static_cast<int>(gridDim.x), U);
+    const bool active = static_cast<int>(blockIdx.x) < G;
+    const int u_lo = active ? ft_lo(blockIdx.x, U, G) : 0;
+    const int u_hi = active ? ft_lo(blockIdx.x + 1, U, G) : 0;
+    const int n_st = u_hi - u_lo;
+
+    // window w -> expert e, first slot sb, tokens nt
+    auto window = [&](int w, int &e, int &sb, int &nt) {
+        int lo = 0, hi = n_act;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (win_off[mid] <= w) lo = mid; else hi = mid;
+        }
+        e = g.act[lo];
+        sb = g.eoff[e] + (w - win_off[lo]) * TMAX;
+        nt = min(TMAX, g.eoff[e + 1] - sb);
+    };
+    const int64_t img_row = static_cast<int64_t>(g.n_kq) * 1024;
+
+    if (warp == 0) {
+        // ---------------- weight producer
+        if (lane == 0) {
+            int cur_w = -1, e = 0, sb = 0, nt = 0;
+            for (int i = 0; i < n_st; ++i) {
+                const int s = i % NW;
+                if (i >= NW && !mbar_wait(&wempty[s], ((i / NW) - 1) & 1, 60)) break;
+                const int u = u_lo + i;
+                const int rbg = u / nsr, kq = u % nsr;
+                const int w = rbg / g.n_rb, rb = rbg % g.n_rb;
+                if (w != cur_w) {
+                    window(w, e, sb, nt);
+                    cur_w = w;
+                }
+                const int64_t off = static_cast<int64_t>(e) * g.e_stride +
+                                    (static_cast<int64_t>(rb) * g.n_kq + kq) * FT_TILE;
+                uint8_t *st = w_ring + static_cast<size_t>(s) * S::WST;
+                mbar_expect_tx(&wfull[s], S::WST);
+                bulk_g2s(st, g.w0 + off, FT_TILE, &wfull[s]);
+                if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &wfull[s]);
+            }
+        }
+    } else if (warp == 7) {
+        // ---------------- activation producer: the window's atoms of this K stage
+        if (lane == 0) {
+            int cur_w = -1, e = 0, sb = 0, nt = 0;
+            for (int i = 0; i < n_st; ++i) {
+                const int s = i % NB;
+                if (i >= NB && !mbar_wait(&bempty[s], ((i / NB) - 1) & 1, 61)) break;
+                const int u = u_lo + i;
+                const int rbg = u / nsr, kq = u % nsr;
+                const int w = rbg / g.n_rb;
+                if (w != cur_w) {
+                    window(w, e, sb, nt);
+                    cur_w = w;
+                }
+                uint8_t *st = b_ring + static_cast<size_t>(s) * S::BST;
+                mbar_expect_tx(&bfull[s], static_cast<uint32_t>(nt) * 1024u);
+                for (int t = 0; t < nt; ++t) {
+                    const int sl = g.slots[sb + t];
+                    const int row = g.bcast ? sl / g.n_used : sl;
+                    bulk_g2s(st + t * 1024, g.img + row * img_row + kq * 1024, 1024, &bfull[s]);
+                }
+            }
+        }
+    } else if (warp == 1 || (NI == 2 && warp == 2)) {
+        // ---------------- MMA issuers: one thread per matrix
+        if (lane == 0) {
+            const int k = warp - 1;
+            const uint32_t idesc = idesc_nvf4(128, NCOL);
+            const uint32_t t_sfb = tbase + 256 + NW * 16 * NI + 4 * k;
+            tc_cp_sf(t_sfb, sdesc_plain(smem_u32(sfb_const), 128));
+            int seg = 0;
+            for (int i = 0; i < n_st; ++i) {
+                const int u = u_lo + i;
+                const bool first = i == 0 || u % nsr == 0;
+                const bool last = i == n_st - 1 || (u + 1) % nsr == 0;
+                if (first && seg > 0 && !mbar_wait(accempty, (seg - 1) & 1, 62)) break;
+                const int sw = i % NW, sb = i % NB;
+                if (!mbar_wait(&wfull[sw], (i / NW) & 1, 63)) break;
+                if (!mbar_wait(&bfull[sb], (i / NB) & 1, 64)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + k * FT_TILE;
+                const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sb) * S::BST);
+                const uint32_t t_sfa = tbase + 256 + (sw * NI + k) * 16;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) tc_cp_sf(t_sfa + 4 * j, sdesc_plain(a_addr + FT_CODES + 512 * j, 128));
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    tc_mma_nvf4(tD + k * NCOL, sdesc_sw128(a_addr + 32 * j), sdesc_sw128(b_addr + 32 * j), idesc,
+                                t_sfa + 4 * j, t_sfb, (!first || j > 0) ? 1u : 0u);
+                tc_commit(&wempty[sw]);
+                tc_commit(&bempty[sb]);
+                if (last) {
+                    tc_commit(accfull);
+                    ++seg;
+                }
+            }
+        }
+    } else if (warp >= 3 && warp <= 6) {
+        // ---------------- epilogue warps (3..6), one TMEM lane quadrant each
+        const int q = warp & 3;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+        const int erow = 32 * q + lane;
+        float *gt = gtab_w + q * 16 * FM_GSTRIDE;
+        int64_t *orow = orow_w + q * 16;
+        float *part_cta = g.part + static_cast<int64_t>(blockIdx.x) * 2 * 2 * TMAX * 128;
+        int seg = 0;
+        for (int s0u = u_lo; s0u < u_hi; ++seg) {
+            const int rbg = s0u / nsr;
+            const int s1u = min(u_hi, (rbg + 1) * nsr);
+            const int w = rbg / g.n_rb, rb = rbg % g.n_rb;
+            int e, sb, nt;
+            window(w, e, sb, nt);
+            // this warp's copy of the window's factors and output rows
+            __syncwarp();
+#pragma unroll
+            for (int c = lane; c < TMAX * FM_GSTRIDE; c += 32) {
+                const int t = c / FM_GSTRIDE;
+                float v = 0.0f;
+                if (t < nt) {
+                    const int sl = g.slots[sb + t];
+                    const int row = g.bcast ? sl / g.n_used : sl;
+                    v = g.gtab[static_cast<int64_t>(row) * FM_GSTRIDE + (c % FM_GSTRIDE)];
+                }
+                gt[c] = v;
+            }
+            if (lane < TMAX) {
+                const int sl = lane < nt ? g.slots[sb + lane] : 0;
+                orow[lane] = static_cast<int64_t>(sl / g.n_used) * g.ld_tok + static_cast<int64_t>(sl % g.n_used) * g.ld_slot;
+            }
+            __syncwarp();
+            const float sc0 = g.s0 ? g.s0[e] : 1.0f;
+            const float sc1 = (DUAL && g.s1) ? g.s1[e] : 1.0f;
+            auto finish = [&](int t, float a0, float a1) {
+                const int n = rb * 128 + erow;
+                if (n >= g.N || t >= nt) return;
+                float val;
+                if (DUAL) {
+                    float result = a1;
+                    result *= sc1;
+                    float gate = a0;
+                    gate *= sc0;
+                    result *= silu_f(gate);
+                    val = result;
+                } else {
+                    val = a0 * sc0;
+                }
+                g.y[orow[t] + n] = val;
+            };
+
+            if (!mbar_wait(accfull, seg & 1, 65)) break;
+            tc_fence_after();
+            float acc0[TMAX], acc1[TMAX];
+#pragma unroll
+            for (int t = 0; t < TMAX; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
+#pragma unroll
+            for (int c = 0; c < NCOL; c += 16) {
+                uint32_t d0[16], d1[16];
+                tmem_ld16(tD + lane_off + c, d0);
+                if (NI == 2) tmem_ld16(tD + NCOL + lane_off + c, d1);
+#pragma unroll
+                for (int v = 0; v < 16; ++v) {
+                    const int col = c + v, t = col / FM_DIGITS;
+                    const float gf = gt[col];
+                    acc0[t] = fmaf(gf, __uint_as_float(d0[v]), acc0[t]);
+                    if (NI == 2) acc1[t] = fmaf(gf, __uint_as_float(d1[v]), acc1[t]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(accempty);
+            if (s0u == rbg * nsr && s1u == (rbg + 1) * nsr) {
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) finish(t, acc0[t], acc1[t]);
+            } else {
+                const int c_first = ft_owner(rbg * nsr, U, G);
+                const int c_last = ft_owner((rbg + 1) * nsr - 1, U, G);
+                const int which = s0u == u_lo ? 0 : 1;
+                float *pp = part_cta + which * 2 * TMAX * 128;
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) {
+                    pp[t * 128 + erow] = acc0[t];
+                    if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
+                }
+                __threadfence();
+                __syncwarp();
+                unsigned prev = 0;
+                if (lane == 0) prev = atomicAdd(&g.counter[rbg * 4 + q], 1u);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == static_cast<unsigned>(c_last - c_first)) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int t = 0; t < nt; ++t) {
+                        float a0 = 0.0f, a1 = 0.0f;
+                        for (int c = c_first; c <= c_last; ++c) {
+                            const int wc = (ft_lo(c, U, G) / nsr == rbg) ? 0 : 1;
+                            const float *pb = g.part + (static_cast<int64_t>(c) * 2 + wc) * 2 * TMAX * 128;
+                            a0 += __ldcg(pb + t * 128 + erow);
+                            if (DUAL) a1 += __ldcg(pb + TMAX * 128 + t * 128 + erow);
+                        }
+                        finish(t, a0, a1);
+                    }
+                    if (lane == 0) g.counter[rbg * 4 + q] = 0;
+                }
+            }
+            s0u = s1u;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, TMEM_COLS);
+    }
+}
+
+} // namespace frb

@@ -72,14 +72,17 @@ __device__ __forceinline__ void f16_split(__half h, int &m, int &E) {
 // in the 128-byte-swizzled K-major layout (row n = 8t + p); sfb: per 64-block
 // one 512-byte scale atom, every entry of rows n < 8T set to 1.0 (consumers
 // that keep one constant atom ignore it); gtab[t * 8 + p] = 9^p * 2^(E0_t+1).
-// Rows n >= 8T are left as they are (their MMA columns are never read).  x_k
-// follows quantize_q8_1 exactly (d = f16(amax / 127), q = roundf(x / d)); the
-// input is f32 rows or q8_1 blocks.  Grid (slices, T), 256 threads; warp per
-// q8_1 block.
+// Rows n >= 8T are left as they are (their MMA columns are never read).  With
+// t_stride > 0 (and NCOL = 8) every token gets its own image instead, at
+// bimg + t * t_stride: per K stage one 1024-byte swizzle atom of its eight
+// rows, so a consumer can gather any set of tokens atom by atom (the MoE
+// expert windows); sfb may then be null.  x_k follows quantize_q8_1 exactly
+// (d = f16(amax / 127), q = roundf(x / d)); the input is f32 rows or q8_1
+// blocks.  Grid (slices, T), 256 threads; warp per q8_1 block.
 __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, int64_t ldx,
                                                  const uint8_t *__restrict__ q8, int64_t ldq, int K, int NCOL,
                                                  uint8_t *__restrict__ bimg, uint8_t *__restrict__ sfb,
-                                                 float *__restrict__ gtab) {
+                                                 float *__restrict__ gtab, int64_t t_stride) {
     fr_pdl_wait();
     fr_pdl_trigger();
     const int t = blockIdx.y;
@@ -199,21 +202,22 @@ __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, in
         const int kb = b >> 1, kq = kb >> 2, kbl = kb & 3;
         const int sbk = (b & 1) * 2 + (lane >> 4);   // sub-block inside the 64-block
         const int j = lane & 15;
-        uint8_t *img = bimg + static_cast<int64_t>(kq) * NCOL * 128;
+        uint8_t *img = bimg + t * t_stride + static_cast<int64_t>(kq) * NCOL * 128;
+        const int n0 = t_stride > 0 ? 0 : FM_DIGITS * t;
 #pragma unroll
         for (int p = 0; p < FM_DIGITS; ++p) {
             const uint32_t hi = __shfl_xor_sync(0xffffffffu, nib[p], 8);
             if (j < 8) {
-                const int n = FM_DIGITS * t + p;
+                const int n = n0 + p;
                 const int idx = kbl * 32 + sbk * 8 + j;
                 const int c16 = idx >> 4;
                 img[n * 128 + ((c16 ^ (n & 7)) << 4) + (idx & 15)] = static_cast<uint8_t>(nib[p] | (hi << 4));
             }
         }
-        if (j == 0) {
+        if (j == 0 && sfb != nullptr) {
 #pragma unroll
             for (int p = 0; p < FM_DIGITS; ++p) {
-                const int n = FM_DIGITS * t + p;
+                const int n = n0 + p;
                 sfb[static_cast<int64_t>(kb) * 512 + (n & 31) * 16 + (n >> 5) * 4 + sbk] = static_cast<uint8_t>(FM_SFB);
             }
         }

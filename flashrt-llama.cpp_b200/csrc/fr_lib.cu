@@ -14,6 +14,7 @@
 #include "fr_tcgemv.cuh"
 #include "fr_fp4mv.cuh"
 #include "fr_fp4tile.cuh"
+#include "fr_fp4moe.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -1244,7 +1245,7 @@ static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const
         rc = launch_pdl(k_act_fp4, dim3(slices, tw), dim3(256), 0, stream,
                         x ? x + t0 * ldx : static_cast<const float *>(nullptr), ldx,
                         q8 ? q8 + t0 * ldq * Q8_BYTES : static_cast<const uint8_t *>(nullptr), ldq, K, NCOL, bimg, sfb,
-                        gtab);
+                        gtab, static_cast<int64_t>(0));
         if (rc != FR_OK) return rc;
         switch (NCOL) {
         case 16: rc = fp4t_launch2<16>(a, G, dual, nt, stream); break;
@@ -1324,7 +1325,7 @@ static int fp4_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N,
         rc = launch_pdl(k_act_fp4, dim3(slices, tw), dim3(256), 0, stream,
                         x ? x + t0 * ldx : static_cast<const float *>(nullptr), ldx,
                         q8 ? q8 + t0 * ldq * Q8_BYTES : static_cast<const uint8_t *>(nullptr), ldq, K, NCOL, bimg,
-                        sfb, gtab);
+                        sfb, gtab, static_cast<int64_t>(0));
         if (rc != FR_OK) return rc;
         a.T = tw;
         a.t0 = t0;
@@ -1543,6 +1544,241 @@ int fr_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void 
     if (rc != FR_OK) return rc;
     return fp4t_matvec(static_cast<const uint8_t *>(wd_t), nullptr, n_embd, n_ff, glu, n_ff, nullptr, 0, T, sd,
                        nullptr, resid, n_embd, out, n_embd, false, stream);
+}
+
+} // extern "C"
+
+// ======================================================================
+// MoE experts on the FP4 tensor cores (tile-major expert weights)
+// ======================================================================
+namespace frb {
+
+template <int NCOL, int EPI>
+static int fp4e_launch(FeArgs a, int grid, cudaStream_t stream) {
+    using S = FtShape<NCOL, EPI, 1>;
+    auto kern = k_fp4e<NCOL, EPI>;
+    static bool attr_done[64] = {};
+    int rc = allow_max_smem(kern, attr_done);
+    if (rc != FR_OK) return rc;
+    const int extra = fe_extra_bytes() + 64;
+    const int cap = dev_info().smem_optin - 1024 - extra;
+    int nb = 4;
+    int nw = std::max(2, std::min(((EPI == FM_PLAIN ? 184 : 110) * 1024 + S::WST - 1) / S::WST, 8));
+    nw = std::min(nw, (256 - 4 * S::NI) / (16 * S::NI));
+    static const char *ov = getenv("FR_FP4E_RINGS");
+    if (ov && *ov) {
+        int w = 0, b = 0;
+        if (sscanf(ov, "%d,%d", &w, &b) == 2 && w >= 2 && b >= 1 && w * 16 * S::NI <= 256 - 4 * S::NI &&
+            w * S::WST + b * S::BST <= cap) {
+            nw = w;
+            nb = b;
+        }
+    }
+    while (nw > 2 && nw * S::WST + nb * S::BST > cap) --nw;
+    if (nw * S::WST + nb * S::BST > cap) return FR_EINVAL;
+    a.n_w = nw;
+    a.n_b = nb;
+    const size_t smem = 1024 + static_cast<size_t>(nw) * S::WST + static_cast<size_t>(nb) * S::BST + extra;
+    return launch_pdl(kern, dim3(grid), dim3(256), smem, stream, a);
+}
+
+static int fe_ncol(int max_tok) {
+    const int tw = std::min(std::max(1, max_tok), FP4_MAX_T);
+    return FM_DIGITS * tw <= 16 ? 16 : FM_DIGITS * tw <= 32 ? 32 : FM_DIGITS * tw <= 64 ? 64 : 128;
+}
+
+// Per-source-row activation images of `rows` f32 rows (k_act_fp4), then the
+// expert matvec of one projection.  `a` carries the routing, weights and
+// output; max_tok bounds the tokens any expert receives (picks the window).
+static int fp4e_run(FeArgs a, bool dual, const float *x, int64_t ldx, int rows, int max_tok, int max_active,
+                    uint8_t *img, float *gtab, cudaStream_t stream) {
+    const DevInfo &di = dev_info();
+    if (di.cc_major != 10) return FR_ENODEVICE;
+    const int n_kq = a.K / 256;
+    const int nq = a.K / Q8_ELEMS;
+    const int slices = std::max(1, std::min((nq + 7) / 8, std::max(1, 256 / std::max(1, rows))));
+    int rc = launch_pdl(k_act_fp4, dim3(slices, rows), dim3(256), 0, stream, x, ldx,
+                        static_cast<const uint8_t *>(nullptr), static_cast<int64_t>(0), a.K, FM_DIGITS, img,
+                        static_cast<uint8_t *>(nullptr), gtab, static_cast<int64_t>(n_kq) * 1024);
+    if (rc != FR_OK) return rc;
+    const int NCOL = fe_ncol(max_tok);
+    const int TMAX = NCOL / FM_DIGITS;
+    const int G = std::max(1, di.sms);
+    const long max_windows = std::min<long>(a.E, max_active) + (static_cast<long>(rows) * (a.bcast ? a.n_used : 1)) / TMAX + 1;
+    const size_t cnt_bytes = align256(static_cast<size_t>(max_windows) * a.n_rb * 4 * sizeof(unsigned));
+    const size_t part_bytes = static_cast<size_t>(G) * 2 * 2 * TMAX * 128 * sizeof(float);
+    // counters (kept at zero between calls; grow-only, cleared when they
+    // grow) and partials live in separate buffers, so a call that needs more
+    // counters never finds another call's partials over them
+    void *cnt = nullptr, *prt = nullptr;
+    rc = workspace_get_zeroed(WS_FE, cnt_bytes, stream, &cnt);
+    if (rc != FR_OK) return rc;
+    rc = workspace_get(WS_FE, part_bytes, stream, &prt);
+    if (rc != FR_OK) return rc;
+    a.counter = static_cast<unsigned int *>(cnt);
+    a.part = static_cast<float *>(prt);
+    a.max_rbg = static_cast<int>(max_windows * a.n_rb);
+    a.img = img;
+    a.gtab = gtab;
+    a.n_kq = n_kq;
+    if (dual) {
+        switch (NCOL) {
+        case 16: return fp4e_launch<16, FM_SWIGLU>(a, G, stream);
+        case 32: return fp4e_launch<32, FM_SWIGLU>(a, G, stream);
+        case 64: return fp4e_launch<64, FM_SWIGLU>(a, G, stream);
+        default: return fp4e_launch<128, FM_SWIGLU>(a, G, stream);
+        }
+    }
+    switch (NCOL) {
+    case 16: return fp4e_launch<16, FM_PLAIN>(a, G, stream);
+    case 32: return fp4e_launch<32, FM_PLAIN>(a, G, stream);
+    case 64: return fp4e_launch<64, FM_PLAIN>(a, G, stream);
+    default: return fp4e_launch<128, FM_PLAIN>(a, G, stream);
+    }
+}
+
+static bool fe_shape_ok(int N, int K) { return N > 0 && K > 0 && N % 128 == 0 && K % 256 == 0; }
+
+} // namespace frb
+
+extern "C" {
+
+int fr_moe_ffn_tiled(const float *x, const float *w_r, const void *wg_t, const void *wu_t, const void *wd_t,
+                     const float *sg, const float *su, const float *sd, const float *resid, float *out, int T,
+                     int n_embd, int n_ff, int E, int n_used, float clamp_val, int32_t *chk_ids, float *chk_wts,
+                     float *chk_glu, float *chk_part, cudaStream_t stream) {
+    if (fault_hit("fr_moe_ffn_tiled")) return FR_EINJECTED;
+    int rc = check_route_shape(T, n_embd, E, n_used);
+    if (rc != FR_OK) return rc;
+    if (!x || !w_r || !wg_t || !wu_t || !wd_t || !out) return FR_EINVAL;
+    if (!fe_shape_ok(n_ff, n_embd) || !fe_shape_ok(n_embd, n_ff) || E > FE_MAX_E) return FR_EINVAL;
+    if (!aligned16(x) || !aligned16(w_r) || !aligned16(wg_t) || !aligned16(wu_t) || !aligned16(wd_t)) return FR_EINVAL;
+    const int S = T * n_used;
+    const int kq_gu = n_embd / 256, kq_d = n_ff / 256;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_logits = take(static_cast<size_t>(T) * E * 4);
+    const size_t o_ids = take(static_cast<size_t>(S) * 4);
+    const size_t o_wts = take(static_cast<size_t>(S) * 4);
+    const size_t o_eoff = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_act = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_slots = take(static_cast<size_t>(S) * 4);
+    const size_t o_gx = take(static_cast<size_t>(T) * FM_GSTRIDE * 4);
+    const size_t o_ix = take(static_cast<size_t>(T) * kq_gu * 1024);
+    const size_t o_glu = take(static_cast<size_t>(S) * n_ff * 4);
+    const size_t o_gg = take(static_cast<size_t>(S) * FM_GSTRIDE * 4);
+    const size_t o_ig = take(static_cast<size_t>(S) * kq_d * 1024);
+    const size_t o_part = take(static_cast<size_t>(S) * n_embd * 4);
+    void *wsp = nullptr;
+    rc = workspace_get(WS_MOE, off, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    uint8_t *base = static_cast<uint8_t *>(wsp);
+    float *logits = reinterpret_cast<float *>(base + o_logits);
+    int32_t *ids = chk_ids ? chk_ids : reinterpret_cast<int32_t *>(base + o_ids);
+    float *wts = chk_wts ? chk_wts : reinterpret_cast<float *>(base + o_wts);
+    int32_t *eoff = reinterpret_cast<int32_t *>(base + o_eoff);
+    int32_t *act = reinterpret_cast<int32_t *>(base + o_act);
+    int32_t *slots = reinterpret_cast<int32_t *>(base + o_slots);
+    float *glu = chk_glu ? chk_glu : reinterpret_cast<float *>(base + o_glu);
+    float *part = chk_part ? chk_part : reinterpret_cast<float *>(base + o_part);
+
+    rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream);
+    if (rc != FR_OK) return rc;
+    const int max_active = std::min(E, S);
+    FeArgs a{};
+    a.N = n_ff;
+    a.K = n_embd;
+    a.n_rb = n_ff / 128;
+    a.E = E;
+    a.n_used = n_used;
+    a.bcast = 1;
+    a.eoff = eoff;
+    a.slots = slots;
+    a.act = act;
+    a.w0 = static_cast<const uint8_t *>(wg_t);
+    a.w1 = static_cast<const uint8_t *>(wu_t);
+    a.e_stride = static_cast<int64_t>(n_ff / 128) * kq_gu * FT_TILE;
+    a.s0 = sg;
+    a.s1 = su;
+    a.y = glu;
+    a.ld_tok = static_cast<int64_t>(n_used) * n_ff;
+    a.ld_slot = n_ff;
+    rc = fp4e_run(a, true, x, n_embd, T, T, max_active, base + o_ix, reinterpret_cast<float *>(base + o_gx), stream);
+    if (rc != FR_OK) return rc;
+    FeArgs d{};
+    d.N = n_embd;
+    d.K = n_ff;
+    d.n_rb = n_embd / 128;
+    d.E = E;
+    d.n_used = n_used;
+    d.bcast = 0;
+    d.eoff = eoff;
+    d.slots = slots;
+    d.act = act;
+    d.w0 = static_cast<const uint8_t *>(wd_t);
+    d.w1 = d.w0;
+    d.e_stride = static_cast<int64_t>(n_embd / 128) * kq_d * FT_TILE;
+    d.s0 = sd;
+    d.y = part;
+    d.ld_tok = static_cast<int64_t>(n_used) * n_embd;
+    d.ld_slot = n_embd;
+    rc = fp4e_run(d, false, glu, n_ff, S, T, max_active, base + o_ig, reinterpret_cast<float *>(base + o_gg), stream);
+    if (rc != FR_OK) return rc;
+    return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream,
+                      static_cast<const float *>(part), static_cast<const float *>(wts), resid, out, n_used, n_embd);
+}
+
+int fr_mul_mat_id_tiled(const void *w_t, int E, int N, int K, const float *x, int64_t x_ld_slot, int64_t x_ld_tok,
+                        const int32_t *ids, int64_t ids_ld, float *dst, int64_t dst_ld_slot, int64_t dst_ld_tok,
+                        int T, int n_used, cudaStream_t stream) {
+    if (fault_hit("fr_mul_mat_id_tiled")) return FR_EINJECTED;
+    if (!w_t || !x || !ids || !dst || T <= 0 || n_used <= 0 || n_used > MOE_MAX_USED) return FR_EINVAL;
+    if (!fe_shape_ok(N, K) || E <= 0 || E > FE_MAX_E || static_cast<long>(T) * n_used > MOE_MAX_SLOTS) return FR_EINVAL;
+    if (!aligned16(w_t) || ids_ld < n_used || x_ld_tok < K) return FR_EINVAL;
+    const bool bcast = x_ld_slot == 0;
+    // the slot rows of a per-slot input must be evenly spaced (one row stride)
+    if (!bcast && (x_ld_slot < K || x_ld_tok != static_cast<int64_t>(n_used) * x_ld_slot)) return FR_EINVAL;
+    const int rows = bcast ? T : T * n_used;
+    const int64_t ldx = bcast ? x_ld_tok : x_ld_slot;
+    const int S = T * n_used;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_eoff = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_act = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_slots = take(static_cast<size_t>(S) * 4);
+    const size_t o_g = take(static_cast<size_t>(rows) * FM_GSTRIDE * 4);
+    const size_t o_img = take(static_cast<size_t>(rows) * (K / 256) * 1024);
+    void *wsp = nullptr;
+    int rc = workspace_get(WS_MOE, off, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    uint8_t *base = static_cast<uint8_t *>(wsp);
+    int32_t *eoff = reinterpret_cast<int32_t *>(base + o_eoff);
+    int32_t *act = reinterpret_cast<int32_t *>(base + o_act);
+    int32_t *slots = reinterpret_cast<int32_t *>(base + o_slots);
+    static bool attr_done[64] = {};
+    rc = allow_max_smem(k_group_ids, attr_done);
+    if (rc != FR_OK) return rc;
+    rc = launch_pdl(k_group_ids, dim3(1), dim3(1024), group_smem(T, n_used), stream, ids, ids_ld, T, n_used, E, eoff,
+                    slots, act, 0);
+    if (rc != FR_OK) return rc;
+    FeArgs a{};
+    a.N = N;
+    a.K = K;
+    a.n_rb = N / 128;
+    a.E = E;
+    a.n_used = n_used;
+    a.bcast = bcast ? 1 : 0;
+    a.eoff = eoff;
+    a.slots = slots;
+    a.act = act;
+    a.w0 = static_cast<const uint8_t *>(w_t);
+    a.w1 = a.w0;
+    a.e_stride = static_cast<int64_t>(N / 128) * (K / 256) * FT_TILE;
+    a.y = dst;
+    a.ld_tok = dst_ld_tok;
+    a.ld_slot = dst_ld_slot;
+    return fp4e_run(a, false, x, ldx, rows, T, std::min(E, S), base + o_img, reinterpret_cast<float *>(base + o_g),
+                    stream);
 }
 
 } // extern "C"

@@ -60,6 +60,10 @@ SIGNATURES = {
     "fr_gemv_tiled": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i32, _vp]),
     "fr_gemv_tiled_swiglu": (_i32, [_vp, _vp, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _vp]),
     "fr_ffn_tiled": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp]),
+    "fr_mul_mat_id_tiled": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i32, _i32,
+                                   _vp]),
+    "fr_moe_ffn_tiled": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
+                                C.c_float, _vp, _vp, _vp, _vp, _vp]),
     "fr_tp_buffer_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "fr_tp_ffn_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                _i64, _vp]),
@@ -314,6 +318,48 @@ def moe_ffn(x, w_r, wg, wu, wd, n_embd, n_ff, E, n_used, sg=None, su=None, sd=No
         chk["glu"] = torch.empty((T, n_used, n_ff), dtype=torch.float32, device=dev)
         chk["part"] = torch.empty((T, n_used, n_embd), dtype=torch.float32, device=dev)
     call("fr_moe_ffn_nvfp4", _ptr(x), _ptr(w_r), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg), _ptr(su), _ptr(sd),
+         _ptr(resid), _ptr(out), T, n_embd, n_ff, E, n_used, clamp, _ptr(chk.get("ids")), _ptr(chk.get("wts")),
+         _ptr(chk.get("glu")), _ptr(chk.get("part")), _stream(stream))
+    return (out, chk) if check else out
+
+
+def tile_experts(w, E, N, K, out=None, stream=None):
+    """Repack E stacked ggml block_nvfp4 experts [E, N, K] (uint8, experts
+    N * w.stride(1) bytes apart, N % 128 == 0) into the tile-major layout."""
+    rows = w.reshape(E * N, -1) if w.dim() == 3 else w
+    return tile_nvfp4(rows, E * N, K, out=out, stream=stream)
+
+
+def mul_mat_id_tiled(w_t, E, N, K, x, ids, broadcast: bool, out=None, stream=None):
+    """mul_mat_id on tile_experts weights; x: [T, K] (broadcast) or [T, n_used, K]."""
+    import torch
+    T, n_used = ids.shape
+    if out is None:
+        out = torch.empty((T, n_used, N), dtype=torch.float32, device=x.device)
+    if broadcast:
+        x_ld_slot, x_ld_tok = 0, x.stride(0)
+    else:
+        x_ld_slot, x_ld_tok = x.stride(1), x.stride(0)
+    call("fr_mul_mat_id_tiled", _ptr(w_t), E, N, K, _ptr(x), x_ld_slot, x_ld_tok, _ptr(ids), ids.stride(0),
+         _ptr(out), out.stride(1), out.stride(0), T, n_used, _stream(stream))
+    return out
+
+
+def moe_ffn_tiled(x, w_r, wg_t, wu_t, wd_t, n_embd, n_ff, E, n_used, sg=None, su=None, sd=None, resid=None,
+                  out=None, clamp=6.103515625e-5, check=False, stream=None):
+    """moe_ffn on tile_experts weights (FP4 tensor-core expert matvecs)."""
+    import torch
+    T = x.shape[0]
+    dev = x.device
+    if out is None:
+        out = torch.empty((T, n_embd), dtype=torch.float32, device=dev)
+    chk = {}
+    if check:
+        chk["ids"] = torch.empty((T, n_used), dtype=torch.int32, device=dev)
+        chk["wts"] = torch.empty((T, n_used), dtype=torch.float32, device=dev)
+        chk["glu"] = torch.empty((T, n_used, n_ff), dtype=torch.float32, device=dev)
+        chk["part"] = torch.empty((T, n_used, n_embd), dtype=torch.float32, device=dev)
+    call("fr_moe_ffn_tiled", _ptr(x), _ptr(w_r), _ptr(wg_t), _ptr(wu_t), _ptr(wd_t), _ptr(sg), _ptr(su), _ptr(sd),
          _ptr(resid), _ptr(out), T, n_embd, n_ff, E, n_used, clamp, _ptr(chk.get("ids")), _ptr(chk.get("wts")),
          _ptr(chk.get("glu")), _ptr(chk.get("part")), _stream(stream))
     return (out, chk) if check else out

@@ -237,6 +237,32 @@ int fr_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void 
                  const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
                  float *chk_glu, cudaStream_t stream);
 
+/* ------------------------------------ (a7-a10) MoE on tiled expert weights
+ * The expert matrices repacked by fr_nvfp4_tile as one stacked [E * N, K]
+ * matrix (N % 128 == 0, so expert e's tiles start at e * N/128 * K/256 *
+ * 18432 bytes -- the ggml tensor's own expert stride).  The per-expert
+ * matvecs then run on the FP4 tensor cores: each active expert's slots are
+ * cut into windows of up to 16 tokens, and every row block of every used
+ * expert is streamed once per window (once per call unless more than 16
+ * tokens chose the expert), with the window count taken on the device from
+ * the routing (no host sync, graph-capturable).
+ *   fr_mul_mat_id_tiled : fr_mul_mat_id_nvfp4 on tiled experts [E][N, K]
+ *                         (N % 128 == 0, K % 256 == 0; a per-slot input must
+ *                         have x_ld_tok == n_used * x_ld_slot).  Replaces the
+ *                         hook ggml_cuda_frt_moe_mul_mat_id
+ *                         (src/fr_win_qwen36_sm120.cu:2502-2618) for
+ *                         repacked expert tensors.
+ *   fr_moe_ffn_tiled    : fr_moe_ffn_nvfp4 on tiled experts (n_embd and n_ff
+ *                         multiples of 256); same routing, grouping, check
+ *                         buffers and slot-order combine. */
+int fr_mul_mat_id_tiled(const void *w_t, int E, int N, int K, const float *x, int64_t x_ld_slot,
+                        int64_t x_ld_tok, const int32_t *ids, int64_t ids_ld, float *dst, int64_t dst_ld_slot,
+                        int64_t dst_ld_tok, int T, int n_used, cudaStream_t stream);
+int fr_moe_ffn_tiled(const float *x, const float *w_r, const void *wg_t, const void *wu_t, const void *wd_t,
+                     const float *sg, const float *su, const float *sd, const float *resid, float *out, int T,
+                     int n_embd, int n_ff, int E, int n_used, float clamp_val, int32_t *chk_ids, float *chk_wts,
+                     float *chk_glu, float *chk_part, cudaStream_t stream);
+
 /* ------------------------------------------------------ (e) tensor parallel
  * One rank's step of the dense FFN sharded over n_ff (P = nranks ranks, shard
  * F_p = n_ff / P): rank r holds gate/up rows [r*F_p, (r+1)*F_p) and, of every
