@@ -34,6 +34,7 @@
 namespace frb {
 
 constexpr int FE_MAX_E = 256;                  // experts (one scan entry per thread)
+constexpr int FE_TAB = 32;                     // windows of one CTA kept in its shared-memory table
 
 struct FeArgs {
     int N, K;                    // rows per expert, row length
@@ -50,55 +51,80 @@ struct FeArgs {
     float *part;                 // [grid][2: first / last segment][2: matrix][TMAX][128]
     unsigned int *counter;       // [max_rbg][4 quadrants], zero on entry, reset by the last arrival
     int max_rbg;                 // window row blocks the counters cover
-    int n_w, n_b;                // ring depths
+    int n_w, n_b;                // ring depth (stages of weights + activation atoms); n_b = n_w
+};
+
+// Issue groups.  Each tcgen05 step of an issuing thread (barrier wait, scale
+// copy, MMA, commit) costs it ~0.1-0.2 us, so one thread issuing a whole
+// 18 KB tile (two waits, four scale copies, four MMAs, two commits) moves
+// only ~15 GB/s.  Stages therefore alternate between P issue groups (one
+// thread per matrix in each; group p takes the stages i with i % P == p), each
+// with its own TMEM accumulators, which the epilogue adds.  The ring depth is
+// a multiple of P, so a group owns its ring slots and waits on every phase of
+// them in order (a parity wait that skipped a phase could pass on a later
+// one).  Where TMEM allows, the accumulators are double-buffered across
+// row-block segments (D = 2), so the MMAs of a segment need not wait for the
+// epilogue to drain the previous one.  Weights and activation atoms of a stage
+// share one full / empty barrier pair (one wait and one commit per stage).
+template <int NCOL, int EPI>
+struct FeShape {
+    static constexpr int NM = EPI == FM_SWIGLU ? 2 : 1;           // matrices per stage
+    static constexpr int P = 2 * NM * NCOL <= 256 ? 2 : 1;        // issue groups
+    static constexpr int D = 2 * P * NM * NCOL <= 256 ? 2 : 1;    // accumulator sets (segments in flight)
+    static constexpr int NISS = P * NM;                           // issuer threads
+    // weight producer, issuers (warps 1, 2, then 8, 9), epilogue 3..6, activation producer 7
+    static constexpr int THREADS = 32 * (8 + (NISS > 2 ? NISS - 2 : 0));
 };
 
 // shared-memory bytes past the two rings
 __host__ __device__ constexpr int fe_extra_bytes() {
-    return 512 + 4 * (16 * FM_GSTRIDE * 4) + 4 * 16 * 8 + (FE_MAX_E + 1) * 4 + 64 + 64 * 8 + 16;
+    return 512 + 4 * (16 * FM_GSTRIDE * 4) + 4 * 16 * 8 + (FE_MAX_E + 1) * 4 + 64 +
+           FE_TAB * (3 + 16) * 4 + 32 * 4 + 64 * 8 + 16;
 }
 
 template <int NCOL, int EPI>
-__global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
+__global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const FeArgs g) {
     using S = FtShape<NCOL, EPI, 1>;
-    constexpr int NI = S::NI;
-    constexpr bool DUAL = S::NM == 2;
+    using H = FeShape<NCOL, EPI>;
+    constexpr int NM = H::NM, P = H::P, D = H::D, NISS = H::NISS;
+    constexpr bool DUAL = NM == 2;
     constexpr int TMAX = S::TMAX;
     constexpr uint32_t TMEM_COLS = 512;
-    static_assert(NI * NCOL <= 256, "accumulators live in TMEM columns [0, 256)");
+    static_assert(D * NISS * NCOL <= 256, "accumulators live in TMEM columns [0, 256)");
     static_assert(TMAX <= 16, "window factor tables hold 16 tokens");
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int NW = g.n_w, NB = g.n_b;
+    const int NW = g.n_w;                                   // stages in the ring (weights + activations)
     uint8_t *w_ring = smem;
     uint8_t *b_ring = w_ring + static_cast<size_t>(NW) * S::WST;
-    uint8_t *sfb_const = b_ring + static_cast<size_t>(NB) * S::BST;      // 512 B
+    uint8_t *sfb_const = b_ring + static_cast<size_t>(NW) * S::BST;      // 512 B
     float *gtab_w = reinterpret_cast<float *>(sfb_const + 512);            // [4 warps][16 * 8]
     int64_t *orow_w = reinterpret_cast<int64_t *>(gtab_w + 4 * 16 * FM_GSTRIDE); // [4 warps][16]
     int *win_off = reinterpret_cast<int *>(orow_w + 4 * 16);                       // [FE_MAX_E + 1]
     int *wsum = win_off + FE_MAX_E + 1;                                    // [8] warp sums of the scan
-    uint64_t *wfull = reinterpret_cast<uint64_t *>(
-        (reinterpret_cast<uintptr_t>(wsum + 16) + 7) & ~uintptr_t(7));
-    uint64_t *wempty = wfull + NW;
-    uint64_t *bfull = wempty + NW;
-    uint64_t *bempty = bfull + NB;
-    uint64_t *accfull = bempty + NB;
-    uint64_t *accempty = accfull + 1;
-    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(accempty + 1);
+    int *tab_e = wsum + 16;                                                // this CTA's windows: expert,
+    int *tab_sb = tab_e + FE_TAB;                                          //   first slot,
+    int *tab_nt = tab_sb + FE_TAB;                                         //   tokens,
+    int *tab_row = tab_nt + FE_TAB;                                        //   source rows [FE_TAB][16]
+    int *stage_n = tab_row + FE_TAB * 16;                                  // MMA N of each activation stage
+    uint64_t *full = reinterpret_cast<uint64_t *>(
+        (reinterpret_cast<uintptr_t>(stage_n + 32) + 7) & ~uintptr_t(7));
+    uint64_t *empty = full + NW;
+    uint64_t *accfull = empty + NW;                          // [D]
+    uint64_t *accempty = accfull + D;                        // [D]
+    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(accempty + D);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < NW; ++s) {
-            mbar_init(&wfull[s], 1);
-            mbar_init(&wempty[s], NI);
+            mbar_init(&full[s], 2);                          // weight and activation producers
+            mbar_init(&empty[s], NM);                        // the owning group's issuers
         }
-        for (int s = 0; s < NB; ++s) {
-            mbar_init(&bfull[s], 1);
-            mbar_init(&bempty[s], NI);
+        for (int d = 0; d < D; ++d) {
+            mbar_init(&accfull[d], NISS);                    // every issuer, once per segment
+            mbar_init(&accempty[d], 4);                      // the four epilogue warps
         }
-        mbar_init(accfull, NI);
-        mbar_init(accempty, 4);
         fence_mbar_init();
     }
     if (warp == 3) {
@@ -115,7 +141,8 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
     fr_pdl_trigger();
     fr_pdl_wait();                                           // the grouping and the activation images
 
-    // windows per active expert -> exclusive prefix win_off (one entry per thread)
+    // windows per active expert -> exclusive prefix win_off, one entry per
+    // thread of the first FE_MAX_E (the block may have more threads)
     const int n_act = min(max(g.act[g.E], 0), g.E);
     {
         const int i = threadIdx.x;
@@ -130,12 +157,14 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
             const int v = __shfl_up_sync(0xffffffffu, inc, off);
             if (lane >= off) inc += v;
         }
-        if (lane == 31) wsum[warp] = inc;
+        if (i < FE_MAX_E && lane == 31) wsum[warp] = inc;
         __syncthreads();
-        int base = 0;
-        for (int w = 0; w < warp; ++w) base += wsum[w];
-        win_off[i + 1] = base + inc;
-        if (i == 0) win_off[0] = 0;
+        if (i < FE_MAX_E) {
+            int base = 0;
+            for (int w = 0; w < warp; ++w) base += wsum[w];
+            win_off[i + 1] = base + inc;
+            if (i == 0) win_off[0] = 0;
+        }
         __syncthreads();
     }
     const int W = win_off[n_act];
@@ -151,7 +180,7 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
     const int u_hi = active ? ft_lo(blockIdx.x + 1, U, G) : 0;
     const int n_st = u_hi - u_lo;
 
-    // window w -> expert e, first slot sb, tokens nt
+    // window w -> expert e, first slot sb, tokens nt (from the grouping)
     auto window = [&](int w, int &e, int &sb, int &nt) {
         int lo = 0, hi = n_act;
         while (hi - lo > 1) {
@@ -159,8 +188,54 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
             if (win_off[mid] <= w) lo = mid; else hi = mid;
         }
         e = g.act[lo];
+        if (e < 0 || e >= g.E) {                             // never from a valid grouping
+            fr_flag(FR_ST_BADINPUT);
+            e = 0;
+            sb = 0;
+            nt = 0;
+            return;
+        }
         sb = g.eoff[e] + (w - win_off[lo]) * TMAX;
-        nt = min(TMAX, g.eoff[e + 1] - sb);
+        nt = max(0, min(TMAX, g.eoff[e + 1] - sb));
+    };
+    // The windows this CTA touches, with their source rows, looked up once
+    // here (two rounds of loads for the whole CTA) so that no role waits on a
+    // global load inside its loop.  A CTA spanning more than FE_TAB windows
+    // looks the rest up as it reaches them.
+    const int wpu = g.n_rb * nsr;                            // units per window
+    const int w_first = n_st > 0 ? u_lo / wpu : 0;
+    const int n_tab = n_st > 0 ? min(FE_TAB, (u_hi - 1) / wpu - w_first + 1) : 0;
+    if (static_cast<int>(threadIdx.x) < n_tab) {
+        int e, sb, nt;
+        window(w_first + threadIdx.x, e, sb, nt);
+        tab_e[threadIdx.x] = e;
+        tab_sb[threadIdx.x] = sb;
+        tab_nt[threadIdx.x] = nt;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < n_tab * 16; idx += blockDim.x) {
+        const int j = idx >> 4, t = idx & 15;
+        if (t < tab_nt[j]) {
+            const int sl = g.slots[tab_sb[j] + t];
+            tab_row[idx] = g.bcast ? sl / g.n_used : sl;
+        }
+    }
+    __syncthreads();
+    auto win_at = [&](int w, int &e, int &sb, int &nt) {
+        const int j = w - w_first;
+        if (j < n_tab) {
+            e = tab_e[j];
+            sb = tab_sb[j];
+            nt = tab_nt[j];
+        } else {
+            window(w, e, sb, nt);
+        }
+    };
+    auto row_at = [&](int w, int sb, int t) -> int {
+        const int j = w - w_first;
+        if (j < n_tab) return tab_row[j * 16 + t];
+        const int sl = g.slots[sb + t];
+        return g.bcast ? sl / g.n_used : sl;
     };
     const int64_t img_row = static_cast<int64_t>(g.n_kq) * 1024;
 
@@ -170,75 +245,90 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
             int cur_w = -1, e = 0, sb = 0, nt = 0;
             for (int i = 0; i < n_st; ++i) {
                 const int s = i % NW;
-                if (i >= NW && !mbar_wait(&wempty[s], ((i / NW) - 1) & 1, 60)) break;
+                if (i >= NW && !mbar_wait(&empty[s], ((i / NW) - 1) & 1, 60)) break;
                 const int u = u_lo + i;
-                const int rbg = u / nsr, kq = u % nsr;
-                const int w = rbg / g.n_rb, rb = rbg % g.n_rb;
+                const int w = u / wpu, rb = (u % wpu) / nsr, kq = u % nsr;
                 if (w != cur_w) {
-                    window(w, e, sb, nt);
+                    win_at(w, e, sb, nt);
                     cur_w = w;
                 }
                 const int64_t off = static_cast<int64_t>(e) * g.e_stride +
                                     (static_cast<int64_t>(rb) * g.n_kq + kq) * FT_TILE;
                 uint8_t *st = w_ring + static_cast<size_t>(s) * S::WST;
-                mbar_expect_tx(&wfull[s], S::WST);
-                bulk_g2s(st, g.w0 + off, FT_TILE, &wfull[s]);
-                if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &wfull[s]);
+                mbar_expect_tx(&full[s], S::WST);
+                bulk_g2s(st, g.w0 + off, FT_TILE, &full[s]);
+                if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &full[s]);
             }
         }
     } else if (warp == 7) {
-        // ---------------- activation producer: the window's atoms of this K stage
-        if (lane == 0) {
-            int cur_w = -1, e = 0, sb = 0, nt = 0;
-            for (int i = 0; i < n_st; ++i) {
-                const int s = i % NB;
-                if (i >= NB && !mbar_wait(&bempty[s], ((i / NB) - 1) & 1, 61)) break;
-                const int u = u_lo + i;
-                const int rbg = u / nsr, kq = u % nsr;
-                const int w = rbg / g.n_rb;
-                if (w != cur_w) {
-                    window(w, e, sb, nt);
-                    cur_w = w;
-                }
-                uint8_t *st = b_ring + static_cast<size_t>(s) * S::BST;
-                mbar_expect_tx(&bfull[s], static_cast<uint32_t>(nt) * 1024u);
-                for (int t = 0; t < nt; ++t) {
-                    const int sl = g.slots[sb + t];
-                    const int row = g.bcast ? sl / g.n_used : sl;
-                    bulk_g2s(st + t * 1024, g.img + row * img_row + kq * 1024, 1024, &bfull[s]);
-                }
+        // ---------------- activation producer: lane t copies token t's atom
+        // of the stage; the stage records the MMA width its tokens need
+        int cur_w = -1, nt = 0, ncol = 16;
+        const uint8_t *src = g.img;
+        for (int i = 0; i < n_st; ++i) {
+            const int s = i % NW;
+            const int u = u_lo + i;
+            const int w = u / wpu, kq = u % nsr;
+            if (w != cur_w) {
+                int e, sb;
+                win_at(w, e, sb, nt);
+                if (lane < nt) src = g.img + static_cast<int64_t>(row_at(w, sb, lane)) * img_row;
+                const int need = nt * FM_DIGITS;
+                ncol = need <= 16 ? 16 : need <= 32 ? 32 : need <= 64 ? 64 : 128;
+                cur_w = w;
             }
+            bool ok = true;
+            if (lane == 0 && i >= NW) ok = mbar_wait(&empty[s], ((i / NW) - 1) & 1, 61);
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+            uint8_t *st = b_ring + static_cast<size_t>(s) * S::BST;
+            if (lane == 0) {
+                stage_n[s] = min(ncol, NCOL);
+                mbar_expect_tx(&full[s], static_cast<uint32_t>(nt) * 1024u);
+            }
+            __syncwarp();
+            if (lane < nt) bulk_g2s(st + lane * 1024, src + kq * 1024, 1024, &full[s]);
         }
-    } else if (warp == 1 || (NI == 2 && warp == 2)) {
-        // ---------------- MMA issuers: one thread per matrix
-        if (lane == 0) {
-            const int k = warp - 1;
-            const uint32_t idesc = idesc_nvf4(128, NCOL);
-            const uint32_t t_sfb = tbase + 256 + NW * 16 * NI + 4 * k;
+    } else if (warp == 1 || warp == 2 || warp >= 8) {
+        // ---------------- MMA issuers: thread (group p, matrix m) issues the
+        // stages i with i % P == p into accumulator (set seg % D, p, m)
+        const int ii = warp <= 2 ? warp - 1 : warp - 6;
+        if (lane == 0 && ii < NISS) {
+            const int p = ii / NM, m = ii % NM;
+            const uint32_t t_sfb = tbase + 256 + NW * 16 * NM + 4 * ii;
             tc_cp_sf(t_sfb, sdesc_plain(smem_u32(sfb_const), 128));
             int seg = 0;
+            bool started = false;
             for (int i = 0; i < n_st; ++i) {
                 const int u = u_lo + i;
                 const bool first = i == 0 || u % nsr == 0;
                 const bool last = i == n_st - 1 || (u + 1) % nsr == 0;
-                if (first && seg > 0 && !mbar_wait(accempty, (seg - 1) & 1, 62)) break;
-                const int sw = i % NW, sb = i % NB;
-                if (!mbar_wait(&wfull[sw], (i / NW) & 1, 63)) break;
-                if (!mbar_wait(&bfull[sb], (i / NB) & 1, 64)) break;
-                tc_fence_after();
-                const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + k * FT_TILE;
-                const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sb) * S::BST);
-                const uint32_t t_sfa = tbase + 256 + (sw * NI + k) * 16;
+                const int d = seg % D;
+                if (first) {
+                    started = false;
+                    // every issuer waits for each drain of its set, in order
+                    if (seg >= D && !mbar_wait(&accempty[d], ((seg / D) - 1) & 1, 62)) break;
+                }
+                if (i % P == p) {
+                    const int sw = i % NW;
+                    if (!mbar_wait(&full[sw], (i / NW) & 1, 63)) break;
+                    tc_fence_after();
+                    const uint32_t idesc = idesc_nvf4(128, stage_n[sw]);
+                    const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + m * FT_TILE;
+                    const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sw) * S::BST);
+                    const uint32_t t_sfa = tbase + 256 + (sw * NM + m) * 16;
+                    const uint32_t t_acc = tD + ((d * P + p) * NM + m) * NCOL;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) tc_cp_sf(t_sfa + 4 * j, sdesc_plain(a_addr + FT_CODES + 512 * j, 128));
+                    for (int j = 0; j < 4; ++j)
+                        tc_cp_sf(t_sfa + 4 * j, sdesc_plain(a_addr + FT_CODES + 512 * j, 128));
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    tc_mma_nvf4(tD + k * NCOL, sdesc_sw128(a_addr + 32 * j), sdesc_sw128(b_addr + 32 * j), idesc,
-                                t_sfa + 4 * j, t_sfb, (!first || j > 0) ? 1u : 0u);
-                tc_commit(&wempty[sw]);
-                tc_commit(&bempty[sb]);
+                    for (int j = 0; j < 4; ++j)
+                        tc_mma_nvf4(t_acc, sdesc_sw128(a_addr + 32 * j), sdesc_sw128(b_addr + 32 * j), idesc,
+                                    t_sfa + 4 * j, t_sfb, (started || j > 0) ? 1u : 0u);
+                    tc_commit(&empty[sw]);
+                    started = true;
+                }
                 if (last) {
-                    tc_commit(accfull);
+                    tc_commit(&accfull[d]);
                     ++seg;
                 }
             }
@@ -257,23 +347,20 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
             const int s1u = min(u_hi, (rbg + 1) * nsr);
             const int w = rbg / g.n_rb, rb = rbg % g.n_rb;
             int e, sb, nt;
-            window(w, e, sb, nt);
+            win_at(w, e, sb, nt);
             // this warp's copy of the window's factors and output rows
             __syncwarp();
 #pragma unroll
             for (int c = lane; c < TMAX * FM_GSTRIDE; c += 32) {
                 const int t = c / FM_GSTRIDE;
                 float v = 0.0f;
-                if (t < nt) {
-                    const int sl = g.slots[sb + t];
-                    const int row = g.bcast ? sl / g.n_used : sl;
-                    v = g.gtab[static_cast<int64_t>(row) * FM_GSTRIDE + (c % FM_GSTRIDE)];
-                }
+                if (t < nt) v = g.gtab[static_cast<int64_t>(row_at(w, sb, t)) * FM_GSTRIDE + (c % FM_GSTRIDE)];
                 gt[c] = v;
             }
             if (lane < TMAX) {
-                const int sl = lane < nt ? g.slots[sb + lane] : 0;
-                orow[lane] = static_cast<int64_t>(sl / g.n_used) * g.ld_tok + static_cast<int64_t>(sl % g.n_used) * g.ld_slot;
+                const int slot = lane < nt ? g.slots[sb + lane] : 0;
+                orow[lane] = static_cast<int64_t>(slot / g.n_used) * g.ld_tok +
+                             static_cast<int64_t>(slot % g.n_used) * g.ld_slot;
             }
             __syncwarp();
             const float sc0 = g.s0 ? g.s0[e] : 1.0f;
@@ -295,27 +382,37 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
                 g.y[orow[t] + n] = val;
             };
 
-            if (!mbar_wait(accfull, seg & 1, 65)) break;
+            const int d = seg % D;                           // this segment's accumulator set
+            if (!mbar_wait(&accfull[d], (seg / D) & 1, 65)) break;
             tc_fence_after();
             float acc0[TMAX], acc1[TMAX];
 #pragma unroll
             for (int t = 0; t < TMAX; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
+            const int ncol_used = nt * FM_DIGITS;
+            // groups that issued a stage of this segment
+            const int i0 = s0u - u_lo, n_seg = s1u - s0u;
 #pragma unroll
-            for (int c = 0; c < NCOL; c += 16) {
-                uint32_t d0[16], d1[16];
-                tmem_ld16(tD + lane_off + c, d0);
-                if (NI == 2) tmem_ld16(tD + NCOL + lane_off + c, d1);
+            for (int p = 0; p < P; ++p) {
+                if (n_seg < P && (i0 + n_seg - 1) % P != p && i0 % P != p) continue;
+                const uint32_t t_acc = tD + ((d * P + p) * NM) * NCOL + lane_off;
 #pragma unroll
-                for (int v = 0; v < 16; ++v) {
-                    const int col = c + v, t = col / FM_DIGITS;
-                    const float gf = gt[col];
-                    acc0[t] = fmaf(gf, __uint_as_float(d0[v]), acc0[t]);
-                    if (NI == 2) acc1[t] = fmaf(gf, __uint_as_float(d1[v]), acc1[t]);
+                for (int c = 0; c < NCOL; c += 16) {
+                    if (c >= ncol_used) break;
+                    uint32_t d0[16], d1[16];
+                    tmem_ld16(t_acc + c, d0);
+                    if (DUAL) tmem_ld16(t_acc + NCOL + c, d1);
+#pragma unroll
+                    for (int v = 0; v < 16; ++v) {
+                        const int col = c + v, t = col / FM_DIGITS;
+                        const float gf = gt[col];
+                        acc0[t] = fmaf(gf, __uint_as_float(d0[v]), acc0[t]);
+                        if (DUAL) acc1[t] = fmaf(gf, __uint_as_float(d1[v]), acc1[t]);
+                    }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(accempty);
+            if (lane == 0) mbar_arrive(&accempty[d]);
             if (s0u == rbg * nsr && s1u == (rbg + 1) * nsr) {
 #pragma unroll
                 for (int t = 0; t < TMAX; ++t) finish(t, acc0[t], acc1[t]);
@@ -326,8 +423,10 @@ __global__ void __launch_bounds__(256, 1) k_fp4e(const FeArgs g) {
                 float *pp = part_cta + which * 2 * TMAX * 128;
 #pragma unroll
                 for (int t = 0; t < TMAX; ++t) {
-                    pp[t * 128 + erow] = acc0[t];
-                    if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
+                    if (t < nt) {
+                        pp[t * 128 + erow] = acc0[t];
+                        if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
+                    }
                 }
                 __threadfence();
                 __syncwarp();

@@ -79,20 +79,20 @@ __device__ __forceinline__ void f16_split(__half h, int &m, int &E) {
 // expert windows); sfb may then be null.  x_k follows quantize_q8_1 exactly
 // (d = f16(amax / 127), q = roundf(x / d)); the input is f32 rows or q8_1
 // blocks.  Grid (slices, T), 256 threads; warp per q8_1 block.
-__global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, int64_t ldx,
-                                                 const uint8_t *__restrict__ q8, int64_t ldq, int K, int NCOL,
-                                                 uint8_t *__restrict__ bimg, uint8_t *__restrict__ sfb,
-                                                 float *__restrict__ gtab, int64_t t_stride) {
-    fr_pdl_wait();
-    fr_pdl_trigger();
-    const int t = blockIdx.y;
+// One CTA's share (slice `slice` of `nslices`) of token t's columns; every
+// thread of the 256-thread CTA calls it.
+__device__ __forceinline__ void act_fp4_row(const float *__restrict__ x, int64_t ldx,
+                                            const uint8_t *__restrict__ q8, int64_t ldq, int K, int NCOL,
+                                            uint8_t *__restrict__ bimg, uint8_t *__restrict__ sfb,
+                                            float *__restrict__ gtab, int64_t t_stride, int t, int slice,
+                                            int nslices) {
     const int nq = K / Q8_ELEMS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ int s_e[8];
     // this CTA's q8_1 blocks, one warp each; the first block's value is
     // loaded before the row scan so both loads are in flight together
-    const int per = (nq + gridDim.x - 1) / gridDim.x;
-    const int b_lo = blockIdx.x * per, b_hi = min(nq, b_lo + per);
+    const int per = (nq + nslices - 1) / nslices;
+    const int b_lo = slice * per, b_hi = min(nq, b_lo + per);
     const int b_first = b_lo + warp;
     float x_first = 0.0f;
     if (x != nullptr && b_first < b_hi)
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, in
 #pragma unroll
     for (int w = 1; w < 8; ++w) emax = max(emax, s_e[w]);
     const int e0 = emax > -1000 ? emax - FM_SPAN : 0;
-    if (blockIdx.x == 0 && threadIdx.x < FM_GSTRIDE) {
+    if (slice == 0 && threadIdx.x < FM_GSTRIDE) {
         float v = 1.0f;
         for (int p = 0; p < static_cast<int>(threadIdx.x); ++p) v *= 9.0f;
         gtab[t * FM_GSTRIDE + threadIdx.x] = ldexpf(v, e0 + 1);
@@ -222,6 +222,15 @@ __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, in
             }
         }
     }
+}
+
+__global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, int64_t ldx,
+                                                 const uint8_t *__restrict__ q8, int64_t ldq, int K, int NCOL,
+                                                 uint8_t *__restrict__ bimg, uint8_t *__restrict__ sfb,
+                                                 float *__restrict__ gtab, int64_t t_stride) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    act_fp4_row(x, ldx, q8, ldq, K, NCOL, bimg, sfb, gtab, t_stride, blockIdx.y, blockIdx.x, gridDim.x);
 }
 
 // ------------------------------------------------------------ matvec

@@ -697,21 +697,53 @@ static int moe_launch(MoeParams p, int max_active, int max_tok, cudaStream_t str
 
 static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
-static int group_smem(int T, int n_used) {
-    return static_cast<int>((static_cast<size_t>(T) * n_used + 2 * MOE_MAX_E) * sizeof(int32_t));
-}
+// k_group_ids: per-warp expert counts of its 32 warps plus the scan scratch
+static int group_smem(int, int) { return static_cast<int>((32 * MOE_MAX_E + 33) * sizeof(int32_t)); }
 
+// Routing (k_route).  aux: 0 = nothing else; 1 = q8_1 rows of x into q8
+// (ldq blocks per row); 2 = per-token FP4 digit images of x into img/gtab
+// (t_stride bytes per token) -- both computed by extra CTAs of the launch.
 static int route_launch(const float *x, int64_t ldx, const float *w_r, int T, int K, int E, int n_used,
                         float clamp_val, float *logits, int32_t *ids, float *wts, int32_t *eoff, int32_t *slots,
-                        int32_t *act, cudaStream_t stream) {
-    int rc = launch_pdl(k_router_logits, dim3((E + 3) / 4, (T + 3) / 4), dim3(256), 0, stream, x, ldx, w_r, logits,
-                        T, K, E);
+                        int32_t *act, cudaStream_t stream, int aux = 0, uint8_t *q8 = nullptr, int64_t ldq = 0,
+                        uint8_t *img = nullptr, float *gtab = nullptr, int64_t t_stride = 0) {
+    const int n_tc = (T + 3) / 4;
+    void *cnt = nullptr;
+    int rc = workspace_get_zeroed(WS_ROUTE, static_cast<size_t>(n_tc + 1) * sizeof(unsigned), stream, &cnt);
     if (rc != FR_OK) return rc;
-    static bool attr_done[64] = {};
-    rc = allow_max_smem(k_topk_group, attr_done);
-    if (rc != FR_OK) return rc;
-    return launch_pdl(k_topk_group, dim3(1), dim3(1024), group_smem(T, n_used), stream,
-                      static_cast<const float *>(logits), T, E, n_used, clamp_val, ids, wts, eoff, slots, act);
+    RouteArgs a{};
+    a.x = x;
+    a.ldx = ldx;
+    a.wr = w_r;
+    a.T = T;
+    a.K = K;
+    a.E = E;
+    a.n_used = n_used;
+    a.clamp_val = clamp_val;
+    a.logits = logits;
+    a.ids = ids;
+    a.wts = wts;
+    a.eoff = eoff;
+    a.slots = slots;
+    a.act = act;
+    a.cnt = static_cast<unsigned int *>(cnt);
+    a.n_rt = (E / 4) * n_tc;
+    a.aux = aux;
+    int n_aux = 0;
+    if (aux == 1) {
+        a.q8 = q8;
+        a.ldq = ldq;
+        n_aux = static_cast<int>((static_cast<int64_t>(T) * (K / Q8_ELEMS) + 7) / 8);
+    } else if (aux == 2) {
+        const int nq = K / Q8_ELEMS;
+        a.img = img;
+        a.gtab = gtab;
+        a.t_stride = t_stride;
+        a.img_slices = std::max(1, std::min((nq + 7) / 8, std::max(1, 256 / T)));
+        n_aux = T * a.img_slices;
+    }
+    const size_t smem = (8 * MOE_MAX_E + 33) * sizeof(int);
+    return launch_pdl(k_route, dim3(a.n_rt + n_aux), dim3(256), smem, stream, a);
 }
 
 static int check_route_shape(int T, int K, int E, int n_used) {
@@ -826,9 +858,8 @@ int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const voi
     uint8_t *q8g = base + o_q8g;
     float *part = chk_part ? chk_part : reinterpret_cast<float *>(base + o_part);
 
-    rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream);
-    if (rc != FR_OK) return rc;
-    rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
+    rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream,
+                      1, q8x, n_embd / 32);
     if (rc != FR_OK) return rc;
     MoeParams p{};
     p.w0 = static_cast<const uint8_t *>(wg);
@@ -1556,34 +1587,41 @@ namespace frb {
 template <int NCOL, int EPI>
 static int fp4e_launch(FeArgs a, int grid, cudaStream_t stream) {
     using S = FtShape<NCOL, EPI, 1>;
+    using H = FeShape<NCOL, EPI>;
     auto kern = k_fp4e<NCOL, EPI>;
     static bool attr_done[64] = {};
     int rc = allow_max_smem(kern, attr_done);
     if (rc != FR_OK) return rc;
     const int extra = fe_extra_bytes() + 64;
     const int cap = dev_info().smem_optin - 1024 - extra;
-    int nb = 4;
-    int nw = std::max(2, std::min(((EPI == FM_PLAIN ? 184 : 110) * 1024 + S::WST - 1) / S::WST, 8));
-    nw = std::min(nw, (256 - 4 * S::NI) / (16 * S::NI));
+    // TMEM: accumulators in columns [0, 256), then 16 scale columns per
+    // weight tile of the ring and 4 per issuer for the activation atom; each
+    // ring stage holds a weight stage and its activation atoms
+    const int nw_tmem = (256 - 4 * H::NISS) / (16 * H::NM);
+    const int per = S::WST + S::BST;
+    int nw = std::max(2, std::min(((EPI == FM_PLAIN ? 184 : 146) * 1024 + S::WST - 1) / S::WST, 8));
+    nw = std::min(nw, nw_tmem);
     static const char *ov = getenv("FR_FP4E_RINGS");
     if (ov && *ov) {
-        int w = 0, b = 0;
-        if (sscanf(ov, "%d,%d", &w, &b) == 2 && w >= 2 && b >= 1 && w * 16 * S::NI <= 256 - 4 * S::NI &&
-            w * S::WST + b * S::BST <= cap) {
-            nw = w;
-            nb = b;
-        }
+        const int w = atoi(ov);
+        if (w >= 2 && w <= nw_tmem && w * per <= cap) nw = w;
     }
-    while (nw > 2 && nw * S::WST + nb * S::BST > cap) --nw;
-    if (nw * S::WST + nb * S::BST > cap) return FR_EINVAL;
+    while (nw > 2 && nw * per > cap) --nw;
+    // each issue group owns the ring slots s with s % P == its index
+    nw -= nw % H::P;
+    if (nw < 2 || nw * per > cap) return FR_EINVAL;
     a.n_w = nw;
-    a.n_b = nb;
-    const size_t smem = 1024 + static_cast<size_t>(nw) * S::WST + static_cast<size_t>(nb) * S::BST + extra;
-    return launch_pdl(kern, dim3(grid), dim3(256), smem, stream, a);
+    a.n_b = nw;
+    const size_t smem = 1024 + static_cast<size_t>(nw) * per + extra;
+    return launch_pdl(kern, dim3(grid), dim3(H::THREADS), smem, stream, a);
 }
 
-static int fe_ncol(int max_tok) {
-    const int tw = std::min(std::max(1, max_tok), FP4_MAX_T);
+// MMA columns of the window: 8 per token.  Windows of 8 tokens let two issue
+// groups (and, for one matrix, two accumulator sets) fit in TMEM; the plain
+// projection takes 16-token windows when more than 64 tokens make re-reads
+// of an expert's rows likely.
+static int fe_ncol(int max_tok, bool dual) {
+    const int tw = std::min(std::max(1, max_tok), (dual || max_tok <= 64) ? 8 : FP4_MAX_T);
     return FM_DIGITS * tw <= 16 ? 16 : FM_DIGITS * tw <= 32 ? 32 : FM_DIGITS * tw <= 64 ? 64 : 128;
 }
 
@@ -1597,11 +1635,14 @@ static int fp4e_run(FeArgs a, bool dual, const float *x, int64_t ldx, int rows, 
     const int n_kq = a.K / 256;
     const int nq = a.K / Q8_ELEMS;
     const int slices = std::max(1, std::min((nq + 7) / 8, std::max(1, 256 / std::max(1, rows))));
-    int rc = launch_pdl(k_act_fp4, dim3(slices, rows), dim3(256), 0, stream, x, ldx,
+    int rc = FR_OK;
+    if (x != nullptr) {                                      // else the images are already built
+        rc = launch_pdl(k_act_fp4, dim3(slices, rows), dim3(256), 0, stream, x, ldx,
                         static_cast<const uint8_t *>(nullptr), static_cast<int64_t>(0), a.K, FM_DIGITS, img,
                         static_cast<uint8_t *>(nullptr), gtab, static_cast<int64_t>(n_kq) * 1024);
-    if (rc != FR_OK) return rc;
-    const int NCOL = fe_ncol(max_tok);
+        if (rc != FR_OK) return rc;
+    }
+    const int NCOL = fe_ncol(max_tok, dual);
     const int TMAX = NCOL / FM_DIGITS;
     const int G = std::max(1, di.sms);
     const long max_windows = std::min<long>(a.E, max_active) + (static_cast<long>(rows) * (a.bcast ? a.n_used : 1)) / TMAX + 1;
@@ -1626,7 +1667,7 @@ static int fp4e_run(FeArgs a, bool dual, const float *x, int64_t ldx, int rows, 
         case 16: return fp4e_launch<16, FM_SWIGLU>(a, G, stream);
         case 32: return fp4e_launch<32, FM_SWIGLU>(a, G, stream);
         case 64: return fp4e_launch<64, FM_SWIGLU>(a, G, stream);
-        default: return fp4e_launch<128, FM_SWIGLU>(a, G, stream);
+        default: return fp4e_launch<64, FM_SWIGLU>(a, G, stream);
         }
     }
     switch (NCOL) {
@@ -1682,7 +1723,9 @@ int fr_moe_ffn_tiled(const float *x, const float *w_r, const void *wg_t, const v
     float *glu = chk_glu ? chk_glu : reinterpret_cast<float *>(base + o_glu);
     float *part = chk_part ? chk_part : reinterpret_cast<float *>(base + o_part);
 
-    rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream);
+    rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream,
+                      2, nullptr, 0, base + o_ix, reinterpret_cast<float *>(base + o_gx),
+                      static_cast<int64_t>(kq_gu) * 1024);
     if (rc != FR_OK) return rc;
     const int max_active = std::min(E, S);
     FeArgs a{};
@@ -1703,7 +1746,8 @@ int fr_moe_ffn_tiled(const float *x, const float *w_r, const void *wg_t, const v
     a.y = glu;
     a.ld_tok = static_cast<int64_t>(n_used) * n_ff;
     a.ld_slot = n_ff;
-    rc = fp4e_run(a, true, x, n_embd, T, T, max_active, base + o_ix, reinterpret_cast<float *>(base + o_gx), stream);
+    rc = fp4e_run(a, true, nullptr, 0, T, T, max_active, base + o_ix, reinterpret_cast<float *>(base + o_gx),
+                  stream);
     if (rc != FR_OK) return rc;
     FeArgs d{};
     d.N = n_embd;

@@ -1,13 +1,14 @@
 // fr_moe.cuh -- MoE routing, token permute, expert-grouped matvec, combine.
 //
-//   k_router_logits : logits[t, e] = x[t] . W_r[e]           (f32)
-//   k_topk_group    : softmax top-k per token (one warp per token, the
-//                     reference's algorithm, src/fr_win_qwen36_sm120.cu:
-//                     1826-1870) and, in the same single-CTA launch, the token
-//                     permute: eoff/slots/act (src/fr_win_flint_batched_moe.cuh:
-//                     76-166).  Slots inside an expert are in slot order, so the
-//                     grouping is deterministic (the reference's atomics leave
-//                     it unspecified).
+//   k_route         : one launch for the router logits (f32), the softmax
+//                     top-k per token (one warp per token, the reference's
+//                     algorithm, src/fr_win_qwen36_sm120.cu:1826-1870) and the
+//                     token permute eoff/slots/act (src/fr_win_flint_batched_
+//                     moe.cuh:76-166), chained by last-arriver counters, plus
+//                     the experts' activation input in extra CTAs.  Slots inside
+//                     an expert are in slot order, so the grouping is
+//                     deterministic (the reference's atomics leave it
+//                     unspecified).
 //   k_group_ids     : the same permute for ids given by the caller (mul_mat_id)
 //   k_moe_gemv      : CTA = (active expert, row chunk).  The chunk's weight rows
 //                     are bulk-copied into shared memory once and stay resident
@@ -19,6 +20,7 @@
 #pragma once
 
 #include "fr_gemv.cuh"
+#include "fr_fp4mv.cuh"
 
 namespace frb {
 
@@ -26,16 +28,12 @@ constexpr int MOE_MAX_E = 256;
 constexpr int MOE_MAX_USED = 32;
 constexpr int MOE_MAX_SLOTS = 8192;   // T * n_used handled by the single-CTA permute
 
-// ------------------------------------------------------------ router logits
-// grid (E / 4, ceil(T / 4)), 256 threads: 4 expert rows x 4 tokens per CTA.
-__global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, int64_t ldx,
-                                                       const float *__restrict__ wr, float *__restrict__ logits,
-                                                       int T, int K, int E) {
-    fr_pdl_wait();
-    fr_pdl_trigger();
+// ------------------------------------------------------------ router tile
+// logits[t, e] for 4 experts x 4 tokens (e0, t0), fp32, by 256 threads
+__device__ __forceinline__ void router_tile(const float *__restrict__ x, int64_t ldx, const float *__restrict__ wr,
+                                            float *__restrict__ logits, int T, int K, int E, int e0, int t0) {
     __shared__ float red[8][16];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int e0 = blockIdx.x * 4, t0 = blockIdx.y * 4;
     float acc[4][4];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
@@ -76,117 +74,246 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     }
 }
 
-// ------------------------------------------------------------ permute helper
-// Single-CTA stable grouping of n_slots slot ids held in shared memory
-// (ids_s[s] = expert of slot s): eoff[E+1], slots[], act[E+1].  1024 threads.
-__device__ __forceinline__ void group_slots(const int32_t *ids_s, int n_slots, int E, int32_t *eoff,
-                                            int32_t *slots, int32_t *act, int32_t *cnt_s, int32_t *off_s) {
-    const int tid = threadIdx.x;
-    if (tid < E) {
-        int c = 0;
-        for (int s = 0; s < n_slots; ++s) c += ids_s[s] == tid;
-        cnt_s[tid] = c;
+// ------------------------------------------------------------ top-k
+// Softmax top-k of one token by one warp, the reference's algorithm
+// (src/fr_win_qwen36_sm120.cu:1826-1870): softmax in fp32, n_used rounds of
+// warp argmax (ties -> lower id), weights renormalised by max(sum, clamp).
+// Logits are read through L2 (other CTAs wrote them).
+__device__ __forceinline__ void topk_token(const float *__restrict__ l, int E, int n_used, float clamp_val,
+                                           int32_t *__restrict__ ids_row, float *__restrict__ w_row) {
+    const int lane = threadIdx.x & 31;
+    const int per = E / 32;
+    float wt[MOE_MAX_E / 32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+        wt[i] = (i < per) ? __ldcg(l + lane + 32 * i) : -INFINITY;
+        mx = fmaxf(mx, wt[i]);
     }
-    __syncthreads();
-    if (tid == 0) {
-        int run = 0, na = 0;
-        for (int e = 0; e < E; ++e) {
-            off_s[e] = run;
-            eoff[e] = run;
-            run += cnt_s[e];
-            if (cnt_s[e] > 0) act[na++] = e;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+        if (i < per) {
+            wt[i] = expf(wt[i] - mx);
+            sum += wt[i];
         }
-        eoff[E] = run;
-        for (int e = na; e < E; ++e) act[e] = -1;
-        act[E] = na;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+        if (i < per) {
+            wt[i] *= inv;
+            if (isnan(wt[i])) wt[i] = -FLT_MAX;
+        } else {
+            wt[i] = -INFINITY;
+        }
+    }
+    float wsum = 0.0f, outw = 0.0f;
+    for (int k = 0; k < n_used; ++k) {
+        float bv = wt[0];
+        int be = lane;
+#pragma unroll
+        for (int i = 1; i < MOE_MAX_E / 32; ++i) {
+            if (wt[i] > bv) { bv = wt[i]; be = lane + 32 * i; }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float v = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int e = __shfl_xor_sync(0xffffffffu, be, off);
+            if (v > bv || (v == bv && e < be)) { bv = v; be = e; }
+        }
+        if ((be & 31) == lane) {
+#pragma unroll
+            for (int i = 0; i < MOE_MAX_E / 32; ++i)
+                if (i == (be >> 5)) wt[i] = -INFINITY;
+            wsum += bv;
+        }
+        if (k == lane) outw = bv;
+        if (lane == 0) ids_row[k] = be;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, off);
+    wsum = fmaxf(wsum, clamp_val);
+    const float invs = 1.0f / wsum;
+    if (lane < n_used) w_row[lane] = outw * invs;
+}
+
+// ------------------------------------------------------------ permute
+// exclusive prefix sum over the block (any multiple of 32 threads); `scratch`
+// holds 33 ints; returns the block total through *total
+__device__ __forceinline__ int block_excl_scan(int v, int *scratch, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += o;
+    }
+    if (lane == 31) scratch[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? scratch[lane] : 0;
+        int wi = w;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, wi, off);
+            if (lane >= off) wi += o;
+        }
+        if (lane < nw) scratch[lane] = wi - w;
+        if (lane == 31) scratch[32] = wi;
     }
     __syncthreads();
-    if (tid < E && cnt_s[tid] > 0) {
-        int pos = off_s[tid];
-        for (int s = 0; s < n_slots; ++s)
-            if (ids_s[s] == tid) slots[pos++] = s;
+    const int r = scratch[warp] + inc - v;
+    *total = scratch[32];
+    __syncthreads();
+    return r;
+}
+
+// Stable grouping of S slots by expert (get(s) = expert of slot s, or -1 for
+// no expert) into eoff[E+1], slots[] (each expert's slots in slot order) and
+// act[E+1] (active experts ascending, -1 padded, count at act[E]): the token
+// permute of src/fr_win_flint_batched_moe.cuh:76-166, deterministic.  Each
+// warp owns a contiguous run of slots and walks it 32 at a time; lanes of
+// one expert find each other with __match_any_sync, so the cost is
+// O(S / threads) per thread.  cnt holds (blockDim / 32) * E ints; scratch 33.
+// E <= blockDim.  Every thread of the block calls it.
+template <typename F>
+__device__ __forceinline__ void group_slots_warp(F get, int S, int E, int32_t *__restrict__ eoff,
+                                                 int32_t *__restrict__ slots, int32_t *__restrict__ act, int *cnt,
+                                                 int *scratch) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int per = ((S + nw - 1) / nw + 31) & ~31;
+    const int lo = warp * per, hi = min(S, lo + per);
+    for (int i = tid; i < nw * E; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    for (int base = lo; base < hi; base += 32) {
+        const int sl = base + lane;
+        const int e = sl < hi ? get(sl) : -1;
+        const unsigned m = __match_any_sync(0xffffffffu, e);
+        if (e >= 0 && lane == __ffs(m) - 1) cnt[warp * E + e] += __popc(m);
+    }
+    __syncthreads();
+    // per expert: running offsets over the warps, then the block scan
+    int tot = 0;
+    if (tid < E) {
+        for (int w = 0; w < nw; ++w) {
+            const int c = cnt[w * E + tid];
+            cnt[w * E + tid] = tot;
+            tot += c;
+        }
+    }
+    int n_slot = 0, n_act = 0;
+    const int off = block_excl_scan(tot, scratch, &n_slot);
+    const int rank = block_excl_scan(tot > 0 ? 1 : 0, scratch, &n_act);
+    if (tid < E) {
+        eoff[tid] = off;
+        if (tot > 0) act[rank] = tid;
+        for (int w = 0; w < nw; ++w) cnt[w * E + tid] += off;
+    }
+    if (tid == 0) {
+        eoff[E] = n_slot;
+        act[E] = n_act;
+    }
+    for (int i = n_act + tid; i < E; i += blockDim.x) act[i] = -1;
+    __syncthreads();
+    for (int base = lo; base < hi; base += 32) {
+        const int sl = base + lane;
+        const int e = sl < hi ? get(sl) : -1;
+        const unsigned m = __match_any_sync(0xffffffffu, e);
+        int pos = 0;
+        if (e >= 0) pos = cnt[warp * E + e] + __popc(m & ((1u << lane) - 1u));
+        __syncwarp();
+        if (e >= 0) {
+            slots[pos] = sl;
+            if (lane == __ffs(m) - 1) cnt[warp * E + e] += __popc(m);
+        }
+        __syncwarp();
     }
 }
 
-// ------------------------------------------------------------ top-k + permute
-// One CTA of 1024 threads.  Warp w routes tokens w, w+32, ...
-__global__ void __launch_bounds__(1024) k_topk_group(const float *__restrict__ logits, int T, int E, int n_used,
-                                                     float clamp_val, int32_t *__restrict__ ids_out,
-                                                     float *__restrict__ w_out, int32_t *__restrict__ eoff,
-                                                     int32_t *__restrict__ slots, int32_t *__restrict__ act) {
+// ------------------------------------------------------------ fused routing
+// One launch: router logits (4 experts x 4 tokens per CTA), softmax top-k of
+// each 4-token chunk by the last of its CTAs to finish, the permute by the
+// last chunk to finish (counters zero on entry, reset by the last arrivals,
+// so graph replays need no reset), and -- in extra CTAs, independent of the
+// routing -- the expert matvecs' activation input: q8_1 rows of x (aux 1) or
+// its per-token FP4 digit images (aux 2).
+struct RouteArgs {
+    const float *x;
+    int64_t ldx;
+    const float *wr;
+    int T, K, E, n_used;
+    float clamp_val;
+    float *logits;
+    int32_t *ids;
+    float *wts;
+    int32_t *eoff, *slots, *act;
+    unsigned int *cnt;           // [n_tc + 1]
+    int n_rt;                    // router CTAs = (E / 4) * n_tc
+    int aux;                     // 0 none, 1 q8_1, 2 FP4 images
+    uint8_t *q8;                 // aux 1: [T][K / 32 blocks]
+    int64_t ldq;
+    uint8_t *img;                // aux 2: per token, t_stride bytes
+    float *gtab;
+    int64_t t_stride;
+    int img_slices;
+};
+
+__global__ void __launch_bounds__(256) k_route(const RouteArgs a) {
     fr_pdl_wait();
     fr_pdl_trigger();
-    extern __shared__ int32_t sm_i[];
-    int32_t *ids_s = sm_i;                        // [T * n_used]
-    int32_t *cnt_s = ids_s + T * n_used;          // [E]
-    int32_t *off_s = cnt_s + MOE_MAX_E;           // [E]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int per = E / 32;
-    for (int t = warp; t < T; t += 32) {
-        const float *l = logits + static_cast<int64_t>(t) * E;
-        float wt[MOE_MAX_E / 32];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < MOE_MAX_E / 32; ++i) {
-            wt[i] = (i < per) ? l[lane + 32 * i] : -INFINITY;
-            mx = fmaxf(mx, wt[i]);
+    extern __shared__ int sm_route[];
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int b = blockIdx.x;
+    if (b >= a.n_rt) {
+        const int c = b - a.n_rt;
+        if (a.aux == 1) {
+            const int lane = tid & 31, nc = a.K / Q8_ELEMS;
+            const int64_t blk_id = static_cast<int64_t>(c) * 8 + warp;
+            if (blk_id >= static_cast<int64_t>(a.T) * nc) return;
+            const int t = static_cast<int>(blk_id / nc), ch = static_cast<int>(blk_id % nc);
+            const q8_lane r = q8_1_chunk(a.x[static_cast<int64_t>(t) * a.ldx + static_cast<int64_t>(ch) * Q8_ELEMS + lane]);
+            uint8_t *blk = a.q8 + (t * a.ldq + ch) * Q8_BYTES;
+            blk[4 + lane] = static_cast<uint8_t>(r.q);
+            if (lane == 0) *reinterpret_cast<__half2 *>(blk) = __halves2half2(__float2half_rn(r.d), __float2half_rn(r.sum));
+        } else if (a.aux == 2) {
+            act_fp4_row(a.x, a.ldx, nullptr, 0, a.K, FM_DIGITS, a.img, nullptr, a.gtab, a.t_stride, c / a.img_slices,
+                        c % a.img_slices, a.img_slices);
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        float sum = 0.0f;
-#pragma unroll
-        for (int i = 0; i < MOE_MAX_E / 32; ++i) {
-            if (i < per) {
-                wt[i] = expf(wt[i] - mx);
-                sum += wt[i];
-            }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        const float inv = 1.0f / sum;
-#pragma unroll
-        for (int i = 0; i < MOE_MAX_E / 32; ++i) {
-            if (i < per) {
-                wt[i] *= inv;
-                if (isnan(wt[i])) wt[i] = -FLT_MAX;
-            } else {
-                wt[i] = -INFINITY;
-            }
-        }
-        float wsum = 0.0f, outw = 0.0f;
-        for (int k = 0; k < n_used; ++k) {
-            float bv = wt[0];
-            int be = lane;
-#pragma unroll
-            for (int i = 1; i < MOE_MAX_E / 32; ++i) {
-                if (wt[i] > bv) { bv = wt[i]; be = lane + 32 * i; }
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const float v = __shfl_xor_sync(0xffffffffu, bv, off);
-                const int e = __shfl_xor_sync(0xffffffffu, be, off);
-                if (v > bv || (v == bv && e < be)) { bv = v; be = e; }
-            }
-            if ((be & 31) == lane) {
-#pragma unroll
-                for (int i = 0; i < MOE_MAX_E / 32; ++i)
-                    if (i == (be >> 5)) wt[i] = -INFINITY;
-                wsum += bv;
-            }
-            if (k == lane) outw = bv;
-            if (lane == 0) {
-                ids_out[static_cast<int64_t>(t) * n_used + k] = be;
-                ids_s[t * n_used + k] = be;
-            }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, off);
-        wsum = fmaxf(wsum, clamp_val);
-        const float invs = 1.0f / wsum;
-        if (lane < n_used) w_out[static_cast<int64_t>(t) * n_used + lane] = outw * invs;
+        return;
+    }
+    const int n_ec = a.E / 4, n_tc = (a.T + 3) / 4;
+    const int ec = b % n_ec, tc = b / n_ec;
+    router_tile(a.x, a.ldx, a.wr, a.logits, a.T, a.K, a.E, ec * 4, tc * 4);
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&a.cnt[tc], 1u) == static_cast<unsigned>(n_ec - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // this chunk's tokens: warp u routes token 4 tc + u
+    const int t = tc * 4 + warp;
+    if (warp < 4 && t < a.T)
+        topk_token(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.n_used, a.clamp_val,
+                   a.ids + static_cast<int64_t>(t) * a.n_used, a.wts + static_cast<int64_t>(t) * a.n_used);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        a.cnt[tc] = 0;
+        s_last = atomicAdd(&a.cnt[n_tc], 1u) == static_cast<unsigned>(n_tc - 1);
     }
     __syncthreads();
-    group_slots(ids_s, T * n_used, E, eoff, slots, act, cnt_s, off_s);
+    if (!s_last) return;
+    __threadfence();
+    const int32_t *ids = a.ids;
+    group_slots_warp([&](int s) { return __ldcg(ids + s); }, a.T * a.n_used, a.E, a.eoff, a.slots, a.act, sm_route,
+                     sm_route + 8 * MOE_MAX_E);
+    if (tid == 0) a.cnt[n_tc] = 0;
 }
 
 // permute for caller-given ids [T, n_used] (row stride ids_ld); out-of-range
@@ -198,20 +325,18 @@ __global__ void __launch_bounds__(1024) k_group_ids(const int32_t *__restrict__ 
                                                     int skip_neg) {
     fr_pdl_wait();
     fr_pdl_trigger();
-    extern __shared__ int32_t sm_i[];
-    int32_t *ids_s = sm_i;
-    int32_t *cnt_s = ids_s + T * n_used;
-    int32_t *off_s = cnt_s + MOE_MAX_E;
-    for (int s = threadIdx.x; s < T * n_used; s += blockDim.x) {
+    extern __shared__ int sm_i[];
+    auto get = [&](int s) {
         int e = ids[static_cast<int64_t>(s / n_used) * ids_ld + s % n_used];
-        if (e < 0 || e >= E) {
-            if (!(skip_neg && e == -1)) fr_flag(FR_ST_BADINPUT);
-            e = -1;
-        }
-        ids_s[s] = e;
+        if (e < 0 || e >= E) e = -1;
+        return e;
+    };
+    // flag bad ids once
+    for (int s = threadIdx.x; s < T * n_used; s += blockDim.x) {
+        const int e = ids[static_cast<int64_t>(s / n_used) * ids_ld + s % n_used];
+        if ((e < 0 || e >= E) && !(skip_neg && e == -1)) fr_flag(FR_ST_BADINPUT);
     }
-    __syncthreads();
-    group_slots(ids_s, T * n_used, E, eoff, slots, act, cnt_s, off_s);
+    group_slots_warp(get, T * n_used, E, eoff, slots, act, sm_i, sm_i + (blockDim.x >> 5) * E);
 }
 
 // ------------------------------------------------------------ grouped matvec
