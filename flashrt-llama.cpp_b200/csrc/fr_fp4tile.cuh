@@ -83,7 +83,7 @@ struct FtArgs {
     int64_t ldy;
     float *part;                 // partials [row blocks][maxp][2][TMAX][128]
     unsigned int *counter;       // [row blocks][4 quadrants], zero on entry, reset by the last arrival
-    int n_w, n_b;                // ring depths: weight stages, activation stages
+    int n_w, n_b;                // ring depth (stages of weights + activation columns); n_b = n_w
 };
 
 // A pipeline stage is two 18 KB weight tiles -- the gate and up tiles of one
@@ -91,7 +91,12 @@ struct FtArgs {
 // (NT = 2) -- so that every step of the rings moves ~37 KB: each step costs
 // a fixed hand-off latency (barrier wake-up, MMA issue) of about half a
 // microsecond, and 18 KB steps would halve the stream rate.  Each tile has
-// its own MMA issuer and TMEM accumulator.
+// its own MMA issuer and TMEM accumulator.  Each tcgen05 step of an issuing
+// thread costs it ~0.1-0.2 us, so where TMEM allows the stages alternate
+// between two issue groups (P = 2; four issuer threads, each with its own
+// accumulator, added by the epilogue); the ring depth is then even, so a group
+// owns its slots and waits on every phase of them in order.  Weights and
+// activation columns of a stage share one full / empty barrier pair.
 template <int NCOL, int EPI, int NT>
 struct FtShape {
     static constexpr int NM = EPI == FM_SWIGLU ? 2 : 1;
@@ -101,8 +106,11 @@ struct FtShape {
     static constexpr int B_BYTES = NCOL * 128;                     // activation tile (columns only)
     static constexpr int BST = NT * B_BYTES;                       // activation stage
     static constexpr int TMAX = NCOL / FM_DIGITS;
-    // weight producer, two MMA issuers, four epilogue warps, activation producer
-    static constexpr int THREADS = 8 * 32;
+    static constexpr int P = 2 * NI * NCOL <= 256 ? 2 : 1;         // issue groups
+    static constexpr int NISS = P * NI;                            // issuer threads = accumulators
+    // weight producer, issuers (warps 1, 2, then 8, 9), four epilogue warps
+    // (3..6), activation producer (7)
+    static constexpr int THREADS = 32 * (8 + (NISS > 2 ? NISS - 2 : 0));
 };
 
 // first unit of CTA c when U units go to G CTAs, and the CTA owning unit u
@@ -116,24 +124,22 @@ __device__ __forceinline__ int ft_owner(int u, int U, int G) {
 template <int NCOL, int EPI, int NT>
 __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(const FtArgs g) {
     using S = FtShape<NCOL, EPI, NT>;
-    constexpr int NI = S::NI;
+    constexpr int NI = S::NI, P = S::P, NISS = S::NISS;
     constexpr bool DUAL = S::NM == 2;
     constexpr int TMAX = S::TMAX;
     constexpr uint32_t TMEM_COLS = 512;
-    static_assert(NI * NCOL <= 256, "accumulators live in TMEM columns [0, 256)");
+    static_assert(NISS * NCOL <= 256, "accumulators live in TMEM columns [0, 256)");
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int NW = g.n_w, NB = g.n_b;
+    const int NW = g.n_w;                                   // ring stages (weights + activation columns)
     uint8_t *w_ring = smem;
     uint8_t *b_ring = w_ring + static_cast<size_t>(NW) * S::WST;
-    uint8_t *sfb_const = b_ring + static_cast<size_t>(NB) * S::BST;   // 512 B: the activation scale atom
+    uint8_t *sfb_const = b_ring + static_cast<size_t>(NW) * S::BST;   // 512 B: the activation scale atom
     float *gtab = reinterpret_cast<float *>(sfb_const + 512);             // [TMAX][8] column factors
-    uint64_t *wfull = reinterpret_cast<uint64_t *>(gtab + TMAX * FM_GSTRIDE);
-    uint64_t *wempty = wfull + NW;
-    uint64_t *bfull = wempty + NW;
-    uint64_t *bempty = bfull + NB;
-    uint64_t *accfull = bempty + NB;
+    uint64_t *full = reinterpret_cast<uint64_t *>(gtab + TMAX * FM_GSTRIDE);
+    uint64_t *empty = full + NW;
+    uint64_t *accfull = empty + NW;
     uint64_t *accempty = accfull + 1;
     uint32_t *tmem_s = reinterpret_cast<uint32_t *>(accempty + 1);
 
@@ -146,14 +152,10 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NW; ++s) {
-            mbar_init(&wfull[s], 1);
-            mbar_init(&wempty[s], NI);
+            mbar_init(&full[s], 2);                          // weight and activation producers
+            mbar_init(&empty[s], NI);                        // the owning group's issuers
         }
-        for (int s = 0; s < NB; ++s) {
-            mbar_init(&bfull[s], 1);
-            mbar_init(&bempty[s], NI);
-        }
-        mbar_init(accfull, NI);
+        mbar_init(accfull, NISS);                            // every issuer, once per segment
         mbar_init(accempty, 4);
         fence_mbar_init();
     }
@@ -176,14 +178,14 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
         if (lane == 0) {
             for (int i = 0; i < n_st; ++i) {
                 const int s = i % NW;
-                if (i >= NW && !mbar_wait(&wempty[s], ((i / NW) - 1) & 1, 50)) break;
+                if (i >= NW && !mbar_wait(&empty[s], ((i / NW) - 1) & 1, 50)) break;
                 uint8_t *st = w_ring + static_cast<size_t>(s) * S::WST;
                 const int u = u_lo + i;
                 // first tile of the stage: row block u / nsr, K stage (u % nsr) * NT
                 const int64_t off = (static_cast<int64_t>(u / nsr) * g.n_kq + (u % nsr) * NT) * FT_TILE;
-                mbar_expect_tx(&wfull[s], S::WST);
-                bulk_g2s(st, g.w0 + off, NT * FT_TILE, &wfull[s]);
-                if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &wfull[s]);
+                mbar_expect_tx(&full[s], S::WST);
+                bulk_g2s(st, g.w0 + off, NT * FT_TILE, &full[s]);
+                if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &full[s]);
             }
         }
     } else if (warp == 7) {
@@ -191,44 +193,55 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
         if (lane == 0) {
             fr_pdl_wait();
             for (int i = 0; i < n_st; ++i) {
-                const int s = i % NB;
-                if (i >= NB && !mbar_wait(&bempty[s], ((i / NB) - 1) & 1, 51)) break;
+                const int s = i % NW;
+                if (i >= NW && !mbar_wait(&empty[s], ((i / NW) - 1) & 1, 51)) break;
                 const int kq0 = ((u_lo + i) % nsr) * NT;
-                mbar_expect_tx(&bfull[s], S::BST);
+                mbar_expect_tx(&full[s], S::BST);
                 bulk_g2s(b_ring + static_cast<size_t>(s) * S::BST, g.bimg + static_cast<int64_t>(kq0) * S::B_BYTES,
-                         S::BST, &bfull[s]);
+                         S::BST, &full[s]);
             }
         }
-    } else if (warp == 1 || (NI == 2 && warp == 2)) {
-        // ---------------- MMA issuers: one thread per tile of the stage
-        if (lane == 0) {
-            const int k = warp - 1;
+    } else if (warp == 1 || warp == 2 || warp >= 8) {
+        // ---------------- MMA issuers: thread (group p, tile k) issues tile k
+        // of the stages i with i % P == p into accumulator p * NI + k
+        const int ii = warp <= 2 ? warp - 1 : warp - 6;
+        if (lane == 0 && ii < NISS) {
+            const int p = ii / NI, k = ii % NI;
             const uint32_t idesc = idesc_nvf4(128, NCOL);
             // scale columns: [256, 256 + 16 NI NW) weights by ring slot and
             // tile, then four per issuer for the constant activation atom
-            const uint32_t t_sfb = tbase + 256 + NW * 16 * NI + 4 * k;
+            const uint32_t t_sfb = tbase + 256 + NW * 16 * NI + 4 * ii;
+            const uint32_t t_acc = tD + ii * NCOL;
             tc_cp_sf(t_sfb, sdesc_plain(smem_u32(sfb_const), 128));
             int seg = 0;
+            bool started = false;
             for (int i = 0; i < n_st; ++i) {
                 const int u = u_lo + i;
                 const bool first = i == 0 || u % nsr == 0;       // first stage of a row-block segment
                 const bool last = i == n_st - 1 || (u + 1) % nsr == 0;
-                if (first && seg > 0 && !mbar_wait(accempty, (seg - 1) & 1, 52)) break;
-                const int sw = i % NW, sb = i % NB;
-                if (!mbar_wait(&wfull[sw], (i / NW) & 1, 53)) break;
-                if (!mbar_wait(&bfull[sb], (i / NB) & 1, 54)) break;
-                tc_fence_after();
-                const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + k * FT_TILE;
-                const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sb) * S::BST) + (NT == 2 ? k : 0) * S::B_BYTES;
-                const uint32_t t_sfa = tbase + 256 + (sw * NI + k) * 16;
+                if (first) {
+                    started = false;
+                    // every issuer waits for each drain, in order
+                    if (seg > 0 && !mbar_wait(accempty, (seg - 1) & 1, 52)) break;
+                }
+                if (i % P == p) {
+                    const int sw = i % NW;
+                    if (!mbar_wait(&full[sw], (i / NW) & 1, 53)) break;
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + k * FT_TILE;
+                    const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sw) * S::BST) +
+                                            (NT == 2 ? k : 0) * S::B_BYTES;
+                    const uint32_t t_sfa = tbase + 256 + (sw * NI + k) * 16;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) tc_cp_sf(t_sfa + 4 * j, sdesc_plain(a_addr + FT_CODES + 512 * j, 128));
+                    for (int j = 0; j < 4; ++j)
+                        tc_cp_sf(t_sfa + 4 * j, sdesc_plain(a_addr + FT_CODES + 512 * j, 128));
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    tc_mma_nvf4(tD + k * NCOL, sdesc_sw128(a_addr + 32 * j), sdesc_sw128(b_addr + 32 * j), idesc,
-                                t_sfa + 4 * j, t_sfb, (!first || j > 0) ? 1u : 0u);
-                tc_commit(&wempty[sw]);
-                tc_commit(&bempty[sb]);
+                    for (int j = 0; j < 4; ++j)
+                        tc_mma_nvf4(t_acc, sdesc_sw128(a_addr + 32 * j), sdesc_sw128(b_addr + 32 * j), idesc,
+                                    t_sfa + 4 * j, t_sfb, (started || j > 0) ? 1u : 0u);
+                    tc_commit(&empty[sw]);
+                    started = true;
+                }
                 if (last) {
                     tc_commit(accfull);
                     ++seg;
@@ -278,18 +291,25 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
             float acc0[TMAX], acc1[TMAX];
 #pragma unroll
             for (int t = 0; t < TMAX; ++t) { acc0[t] = 0.0f; acc1[t] = 0.0f; }
+            // groups that issued a stage of this segment
+            const int i0 = s0u - u_lo, n_seg = s1u - s0u;
 #pragma unroll
-            for (int c = 0; c < NCOL; c += 16) {
-                uint32_t d0[16], d1[16];
-                tmem_ld16(tD + lane_off + c, d0);
-                if (NI == 2) tmem_ld16(tD + NCOL + lane_off + c, d1);
+            for (int p = 0; p < P; ++p) {
+                if (n_seg < P && i0 % P != p) continue;
+                const uint32_t t_acc = tD + (p * NI) * NCOL + lane_off;
 #pragma unroll
-                for (int v = 0; v < 16; ++v) {
-                    const int col = c + v, t = col / FM_DIGITS;
-                    if (t < TMAX) {
-                        const float gf = gtab[col];
-                        acc0[t] = fmaf(gf, __uint_as_float(d0[v]), acc0[t]);
-                        if (NI == 2) acc1[t] = fmaf(gf, __uint_as_float(d1[v]), acc1[t]);
+                for (int c = 0; c < NCOL; c += 16) {
+                    uint32_t d0[16], d1[16];
+                    tmem_ld16(t_acc + c, d0);
+                    if (NI == 2) tmem_ld16(t_acc + NCOL + c, d1);
+#pragma unroll
+                    for (int v = 0; v < 16; ++v) {
+                        const int col = c + v, t = col / FM_DIGITS;
+                        if (t < TMAX) {
+                            const float gf = gtab[col];
+                            acc0[t] = fmaf(gf, __uint_as_float(d0[v]), acc0[t]);
+                            if (NI == 2) acc1[t] = fmaf(gf, __uint_as_float(d1[v]), acc1[t]);
+                        }
                     }
                 }
             }

@@ -1179,30 +1179,29 @@ static int fp4t_launch(FtArgs a, int grid, cudaStream_t stream) {
     int rc = allow_max_smem(kern, attr_done);
     if (rc != FR_OK) return rc;
     // about 110 KB of weights in flight per SM (measured best for one pass
-    // over a matrix: more only lengthens the memory queues), four activation
-    // stages; TMEM's 256 scale columns bound the weight ring
+    // over a matrix: more only lengthens the memory queues); each ring stage
+    // also holds its activation columns; TMEM's 256 scale columns bound the
+    // ring, whose depth is a multiple of the issue groups
     const int extra = 2048;                                  // scale atom, factors, barriers
     const int cap = dev_info().smem_optin - 1024 - extra;
+    const int per = S::WST + S::BST;
+    const int nw_tmem = (256 - 4 * S::NISS) / (16 * S::NI);
     // the down projection (one matrix) follows the activation kernel of the
     // GLU: a deeper ring prefetches more of its weights meanwhile
-    int nb = 4;
     int nw = std::max(2, std::min(((EPI == FM_PLAIN ? 184 : 110) * 1024 + S::WST - 1) / S::WST, 8));
-    nw = std::min(nw, (256 - 4 * S::NI) / (16 * S::NI));
-    // tuning override (FR_FP4T_RINGS="weights,activations"), within the limits
+    nw = std::min(nw, nw_tmem);
+    // tuning override (FR_FP4T_RINGS="stages"), within the limits
     static const char *ov = getenv("FR_FP4T_RINGS");
     if (ov && *ov) {
-        int w = 0, b = 0;
-        if (sscanf(ov, "%d,%d", &w, &b) == 2 && w >= 2 && b >= 1 && w * 16 * S::NI <= 256 - 4 * S::NI &&
-            w * S::WST + b * S::BST <= cap) {
-            nw = w;
-            nb = b;
-        }
+        const int w = atoi(ov);
+        if (w >= 2 && w <= nw_tmem && w * per <= cap) nw = w;
     }
-    while (nw > 2 && nw * S::WST + nb * S::BST > cap) --nw;
-    if (nw * S::WST + nb * S::BST > cap) return FR_EINVAL;
+    while (nw > 2 && nw * per > cap) --nw;
+    nw -= nw % S::P;
+    if (nw < 2 || nw * per > cap) return FR_EINVAL;
     a.n_w = nw;
-    a.n_b = nb;
-    const size_t smem = 1024 + static_cast<size_t>(nw) * S::WST + static_cast<size_t>(nb) * S::BST + extra;
+    a.n_b = nw;
+    const size_t smem = 1024 + static_cast<size_t>(nw) * per + extra;
     return launch_pdl(kern, dim3(grid), dim3(S::THREADS), smem, stream, a);
 }
 
