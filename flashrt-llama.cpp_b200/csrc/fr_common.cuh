@@ -49,6 +49,11 @@ __device__ __forceinline__ uint64_t fr_now_ns() {
 constexpr uint64_t FR_WAIT_NS = 2000000000ull;
 
 // ---------------------------------------------------------------- PDL
+// GPU-scope acquire/release fence: with a relaxed atomic it forms the
+// release (writer) and acquire (reader) halves of a message hand-off, which
+// is all the stream-K partial sums need (lighter than a sequentially
+// consistent fence).
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void fr_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void fr_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -428,24 +428,23 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
                         if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
                     }
                 }
-                __threadfence();
+                fence_acq_rel_gpu();
                 __syncwarp();
                 unsigned prev = 0;
                 if (lane == 0) prev = atomicAdd(&g.counter[rbg * 4 + q], 1u);
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 if (prev == static_cast<unsigned>(c_last - c_first)) {
-                    __threadfence();
-#pragma unroll 1
-                    for (int t = 0; t < nt; ++t) {
-                        float a0 = 0.0f, a1 = 0.0f;
-                        for (int c = c_first; c <= c_last; ++c) {
+                    fence_acq_rel_gpu();
+                    float s0[TMAX], s1[TMAX];
+                    ft_sum_parts<TMAX, DUAL>(
+                        [&](int k2) {
+                            const int c = c_first + k2;
                             const int wc = (ft_lo(c, U, G) / nsr == rbg) ? 0 : 1;
-                            const float *pb = g.part + (static_cast<int64_t>(c) * 2 + wc) * 2 * TMAX * 128;
-                            a0 += __ldcg(pb + t * 128 + erow);
-                            if (DUAL) a1 += __ldcg(pb + TMAX * 128 + t * 128 + erow);
-                        }
-                        finish(t, a0, a1);
-                    }
+                            return g.part + (static_cast<int64_t>(c) * 2 + wc) * 2 * TMAX * 128;
+                        },
+                        c_last - c_first + 1, nt, erow, s0, s1);
+#pragma unroll
+                    for (int t = 0; t < TMAX; ++t) finish(t, s0[t], s1[t]);
                     if (lane == 0) g.counter[rbg * 4 + q] = 0;
                 }
             }

@@ -85,7 +85,8 @@ __device__ __forceinline__ void act_fp4_row(const float *__restrict__ x, int64_t
                                             const uint8_t *__restrict__ q8, int64_t ldq, int K, int NCOL,
                                             uint8_t *__restrict__ bimg, uint8_t *__restrict__ sfb,
                                             float *__restrict__ gtab, int64_t t_stride, int t, int slice,
-                                            int nslices) {
+                                            int nslices, const float *__restrict__ amax_in = nullptr,
+                                            int n_amax = 0) {
     const int nq = K / Q8_ELEMS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ int s_e[8];
@@ -98,9 +99,18 @@ __device__ __forceinline__ void act_fp4_row(const float *__restrict__ x, int64_t
     if (x != nullptr && b_first < b_hi)
         x_first = x[static_cast<int64_t>(t) * ldx + static_cast<int64_t>(b_first) * Q8_ELEMS + lane];
 
-    // 1. the token's largest block-scale exponent (each CTA scans the row)
+    // 1. the token's largest block-scale exponent (each CTA scans the row, or
+    // the producer of x left the maxima of its row groups in amax_in)
     int emax = -1000;
-    if (x != nullptr) {
+    if (x != nullptr && amax_in != nullptr) {
+        float amax = 0.0f;
+        for (int i = threadIdx.x; i < n_amax; i += blockDim.x) amax = fmaxf(amax, amax_in[static_cast<int64_t>(t) * n_amax + i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        int m, E;
+        f16_split(__float2half_rn(__fdiv_rn(amax, 127.0f)), m, E);
+        emax = E;
+    } else if (x != nullptr) {
         // many independent loads in flight per thread, 16-byte loads when the
         // row allows them
         float am[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
@@ -227,10 +237,15 @@ __device__ __forceinline__ void act_fp4_row(const float *__restrict__ x, int64_t
 __global__ void __launch_bounds__(256) k_act_fp4(const float *__restrict__ x, int64_t ldx,
                                                  const uint8_t *__restrict__ q8, int64_t ldq, int K, int NCOL,
                                                  uint8_t *__restrict__ bimg, uint8_t *__restrict__ sfb,
-                                                 float *__restrict__ gtab, int64_t t_stride) {
-    fr_pdl_wait();
+                                                 float *__restrict__ gtab, int64_t t_stride,
+                                                 const float *__restrict__ amax_in, int n_amax) {
+    // Dependents may launch at once: the matvec that follows streams its
+    // weights (which need nothing from here) as soon as SMs free up, and
+    // waits for this grid's completion before it reads the columns.
     fr_pdl_trigger();
-    act_fp4_row(x, ldx, q8, ldq, K, NCOL, bimg, sfb, gtab, t_stride, blockIdx.y, blockIdx.x, gridDim.x);
+    fr_pdl_wait();
+    act_fp4_row(x, ldx, q8, ldq, K, NCOL, bimg, sfb, gtab, t_stride, blockIdx.y, blockIdx.x, gridDim.x, amax_in,
+                n_amax);
 }
 
 // ------------------------------------------------------------ matvec

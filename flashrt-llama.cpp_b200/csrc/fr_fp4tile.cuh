@@ -82,8 +82,10 @@ struct FtArgs {
     float *y;                    // [.., ldy]
     int64_t ldy;
     float *part;                 // partials [row blocks][maxp][2][TMAX][128]
+    float *amax_out;             // nullable: max |y| of each token's 32-row groups, [t][amax_ld]
     unsigned int *counter;       // [row blocks][4 quadrants], zero on entry, reset by the last arrival
     int n_w, n_b;                // ring depth (stages of weights + activation columns); n_b = n_w
+    int amax_ld;
 };
 
 // A pipeline stage is two 18 KB weight tiles -- the gate and up tiles of one
@@ -119,6 +121,38 @@ __device__ __forceinline__ int ft_lo(int c, int U, int G) {
 }
 __device__ __forceinline__ int ft_owner(int u, int U, int G) {
     return static_cast<int>(((static_cast<int64_t>(u) + 1) * G - 1) / U);
+}
+
+// a[t] (and b[t]) = sum over the n partial slices k = 0..n-1, in k order, of
+// this thread's row; slice k's [2][TMAX][128] block at part(k).  The loads of
+// several slices are issued together so that their latencies overlap.
+template <int TMAX, bool DUAL, typename F>
+__device__ __forceinline__ void ft_sum_parts(F part, int n, int T, int erow, float (&a)[TMAX], float (&b)[TMAX]) {
+    constexpr int CH = 32 / (TMAX * (DUAL ? 2 : 1)) > 0 ? 32 / (TMAX * (DUAL ? 2 : 1)) : 1;
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) { a[t] = 0.0f; b[t] = 0.0f; }
+    for (int k0 = 0; k0 < n; k0 += CH) {
+        float va[CH][TMAX], vb[CH][TMAX];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const float *pc = part(min(k0 + c, n - 1));
+#pragma unroll
+            for (int t = 0; t < TMAX; ++t) {
+                va[c][t] = t < T ? __ldcg(pc + t * 128 + erow) : 0.0f;
+                vb[c][t] = (DUAL && t < T) ? __ldcg(pc + TMAX * 128 + t * 128 + erow) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            if (k0 + c < n) {
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) {
+                    a[t] += va[c][t];
+                    if (DUAL) b[t] += vb[c][t];
+                }
+            }
+        }
+    }
 }
 
 template <int NCOL, int EPI, int NT>
@@ -260,9 +294,10 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
         const float sc0 = g.s0 ? *g.s0 : 1.0f;
         const float sc1 = (DUAL && g.s1) ? *g.s1 : 1.0f;
 
-        auto finish = [&](int rb, int t, float a0, float a1) {
+        // writes one output value; returns |value| (0 for rows past N)
+        auto finish = [&](int rb, int t, float a0, float a1) -> float {
             const int n = rb * 128 + erow;
-            if (n >= g.N || t >= T) return;
+            if (n >= g.N || t >= T) return 0.0f;
             const int64_t tt = g.t0 + t;
             float val;
             if (DUAL) {
@@ -277,6 +312,15 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
                 if (g.resid) val += g.resid[tt * g.ldr + n];
             }
             g.y[tt * g.ldy + n] = val;
+            return fabsf(val);
+        };
+        // this warp's 32 rows of row block rb, token t: their largest |value|
+        // for the next activation kernel (it then needs no scan of the row)
+        auto publish = [&](int rb, int t, float am) {
+            if (g.amax_out == nullptr || t >= T) return;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+            if (lane == 0) g.amax_out[(g.t0 + t) * static_cast<int64_t>(g.amax_ld) + rb * 4 + q] = am;
         };
         // every row-block segment: drain the accumulators, then either finish
         // the rows or publish the partial; the last of the CTAs sharing a row
@@ -326,7 +370,7 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
             }
             if (s0u == rb * nsr && s1u == (rb + 1) * nsr) {
 #pragma unroll
-                for (int t = 0; t < TMAX; ++t) finish(rb, t, acc0[t], acc1[t]);
+                for (int t = 0; t < TMAX; ++t) publish(rb, t, finish(rb, t, acc0[t], acc1[t]));
             } else {
                 const int c_first = ft_owner(rb * nsr, U, G);
                 const int nparts = ft_owner((rb + 1) * nsr - 1, U, G) - c_first + 1;
@@ -337,23 +381,19 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
                     pp[t * 128 + erow] = acc0[t];
                     if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
                 }
-                __threadfence();
+                fence_acq_rel_gpu();
                 __syncwarp();
                 unsigned prev = 0;
                 if (lane == 0) prev = atomicAdd(&g.counter[rb * 4 + q], 1u);
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 if (prev == static_cast<unsigned>(nparts - 1)) {
-                    __threadfence();
+                    fence_acq_rel_gpu();
                     const float *pb = g.part + (static_cast<int64_t>(rb) * g.maxp * 2) * TMAX * 128;
-#pragma unroll 1
-                    for (int t = 0; t < TMAX && t < T; ++t) {
-                        float a0 = 0.0f, a1 = 0.0f;
-                        for (int k2 = 0; k2 < nparts; ++k2) {
-                            a0 += __ldcg(pb + (k2 * 2) * TMAX * 128 + t * 128 + erow);
-                            if (DUAL) a1 += __ldcg(pb + (k2 * 2 + 1) * TMAX * 128 + t * 128 + erow);
-                        }
-                        finish(rb, t, a0, a1);
-                    }
+                    float s0[TMAX], s1[TMAX];
+                    ft_sum_parts<TMAX, DUAL>([&](int k2) { return pb + (k2 * 2) * TMAX * 128; }, nparts, T, erow,
+                                             s0, s1);
+#pragma unroll
+                    for (int t = 0; t < TMAX; ++t) publish(rb, t, finish(rb, t, s0[t], s1[t]));
                     if (lane == 0) g.counter[rb * 4 + q] = 0;
                 }
             }

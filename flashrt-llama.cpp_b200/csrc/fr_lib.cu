@@ -31,7 +31,8 @@ static int fp4_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N,
                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream);
 static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const float *x, int64_t ldx,
                        const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
-                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream);
+                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream,
+                       float *amax_out = nullptr, const float *amax_in = nullptr);
 constexpr int FP4_MAX_T = 16;                      // tokens per launch of the FP4 tensor-core matvecs
 // Which matvec runs on weights in ggml's layout: the dp4a kernel for up to two
 // tokens and for shapes the TMA paths cannot take, the f16 tensor-core kernel
@@ -1214,9 +1215,13 @@ static int fp4t_launch2(const FtArgs &a, int grid, bool dual, int nt, cudaStream
 // FP4 tensor-core matvec on tile-major weights (k_tile_nvfp4's layout):
 // k_act_fp4 builds the activation columns of a window of FP4_MAX_T tokens,
 // k_fp4t streams the weights once per window.
+// amax_out (nullable): per token, the largest |y| of every 32-row group
+// ([T][ceil(N / 128) * 4]); amax_in (nullable, with f32 x): the same maxima
+// of x's row, so the activation kernel needs no scan of it ([T][K / 32]).
 static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const float *x, int64_t ldx,
                        const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
-                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream) {
+                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream, float *amax_out,
+                       const float *amax_in) {
     if (!w0 || (dual && !w1) || N <= 0 || K <= 0 || K % 256 != 0 || T <= 0 || !y) return FR_EINVAL;
     if ((reinterpret_cast<uintptr_t>(w0) & 15) || (w1 && (reinterpret_cast<uintptr_t>(w1) & 15))) return FR_EINVAL;
     const DevInfo &di = dev_info();
@@ -1266,6 +1271,8 @@ static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const
     a.ldy = ldy;
     a.part = reinterpret_cast<float *>(static_cast<uint8_t *>(wsp) + part_off);
     a.counter = static_cast<unsigned int *>(wsp);
+    a.amax_out = amax_out;
+    a.amax_ld = n_rb * 4;
     const int nq = K / Q8_ELEMS;
     for (int t0 = 0; t0 < T; t0 += TW) {
         const int tw = std::min(TW, T - t0);
@@ -1275,7 +1282,9 @@ static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const
         rc = launch_pdl(k_act_fp4, dim3(slices, tw), dim3(256), 0, stream,
                         x ? x + t0 * ldx : static_cast<const float *>(nullptr), ldx,
                         q8 ? q8 + t0 * ldq * Q8_BYTES : static_cast<const uint8_t *>(nullptr), ldq, K, NCOL, bimg, sfb,
-                        gtab, static_cast<int64_t>(0));
+                        gtab, static_cast<int64_t>(0),
+                        (x && amax_in) ? amax_in + static_cast<int64_t>(t0) * nq : static_cast<const float *>(nullptr),
+                        nq);
         if (rc != FR_OK) return rc;
         switch (NCOL) {
         case 16: rc = fp4t_launch2<16>(a, G, dual, nt, stream); break;
@@ -1355,7 +1364,7 @@ static int fp4_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N,
         rc = launch_pdl(k_act_fp4, dim3(slices, tw), dim3(256), 0, stream,
                         x ? x + t0 * ldx : static_cast<const float *>(nullptr), ldx,
                         q8 ? q8 + t0 * ldq * Q8_BYTES : static_cast<const uint8_t *>(nullptr), ldq, K, NCOL, bimg,
-                        sfb, gtab, static_cast<int64_t>(0));
+                        sfb, gtab, static_cast<int64_t>(0), static_cast<const float *>(nullptr), 0);
         if (rc != FR_OK) return rc;
         a.T = tw;
         a.t0 = t0;
@@ -1569,11 +1578,16 @@ int fr_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void 
         if (rc != FR_OK) return rc;
         glu = static_cast<float *>(p);
     }
-    int rc = fp4t_matvec(static_cast<const uint8_t *>(wg_t), static_cast<const uint8_t *>(wu_t), n_ff, n_embd, x,
-                         n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, n_ff, true, stream);
+    // the gate/up epilogue leaves the GLU's row-group maxima for the down's
+    // activation kernel
+    void *am = nullptr;
+    int rc = workspace_get(WS_AMAX, static_cast<size_t>(T) * (n_ff / 32) * sizeof(float), stream, &am);
+    if (rc != FR_OK) return rc;
+    rc = fp4t_matvec(static_cast<const uint8_t *>(wg_t), static_cast<const uint8_t *>(wu_t), n_ff, n_embd, x,
+                     n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, n_ff, true, stream, static_cast<float *>(am));
     if (rc != FR_OK) return rc;
     return fp4t_matvec(static_cast<const uint8_t *>(wd_t), nullptr, n_embd, n_ff, glu, n_ff, nullptr, 0, T, sd,
-                       nullptr, resid, n_embd, out, n_embd, false, stream);
+                       nullptr, resid, n_embd, out, n_embd, false, stream, nullptr, static_cast<const float *>(am));
 }
 
 } // extern "C"
@@ -1638,7 +1652,8 @@ static int fp4e_run(FeArgs a, bool dual, const float *x, int64_t ldx, int rows, 
     if (x != nullptr) {                                      // else the images are already built
         rc = launch_pdl(k_act_fp4, dim3(slices, rows), dim3(256), 0, stream, x, ldx,
                         static_cast<const uint8_t *>(nullptr), static_cast<int64_t>(0), a.K, FM_DIGITS, img,
-                        static_cast<uint8_t *>(nullptr), gtab, static_cast<int64_t>(n_kq) * 1024);
+                        static_cast<uint8_t *>(nullptr), gtab, static_cast<int64_t>(n_kq) * 1024,
+                        static_cast<const float *>(nullptr), 0);
         if (rc != FR_OK) return rc;
     }
     const int NCOL = fe_ncol(max_tok, dual);
