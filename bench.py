@@ -359,11 +359,10 @@ def run_ours(args):
     ep = P.EpMoe(64, 2048, 768, 128, 8) if world > 1 else None
     # one GPU: the experts also repacked tile-major (same bytes) for the FP4
     # tensor-core expert matvecs; the faster layout is reported per batch
-    tsets = []
-    if world == 1:
-        tsets = [(wr, frb200.tile_experts(wg, 128, 768, 2048), frb200.tile_experts(wu, 128, 768, 2048),
-                  frb200.tile_experts(wd, 128, 2048, 768)) for wr, wg, wu, wd in msets]
-        torch.cuda.synchronize()
+    Ep = 128 // world
+    tsets = [(wr, frb200.tile_experts(wg, Ep, 768, 2048), frb200.tile_experts(wu, Ep, 768, 2048),
+              frb200.tile_experts(wd, Ep, 2048, 768)) for wr, wg, wu, wd in msets]
+    torch.cuda.synchronize()
     for T in (1, 64):
         xm = torch.from_numpy(frb200.synth_normal(0x5EED3000 + rank * 131 + T, T * 2048).reshape(T, 2048)).to(dev)
         om = torch.empty((T, 2048), dtype=torch.float32, device=dev)
@@ -374,8 +373,10 @@ def run_ours(args):
             runs["tile-major experts, FP4 tensor-core expert matvecs"] = lambda i, xm=xm, om=om: frb200.moe_ffn_tiled(
                 xm, *tsets[i % 2], 2048, 768, 128, 8, out=om, stream=stream)
         else:
-            runs["expert parallel, ggml layout"] = lambda i, xm=xm, om=om: ep(xm, *msets[i % 2], out=om,
-                                                                               stream=stream)
+            runs["expert parallel, ggml-layout experts"] = lambda i, xm=xm, om=om: ep(xm, *msets[i % 2], out=om,
+                                                                                       stream=stream)
+            runs["expert parallel, tile-major experts"] = lambda i, xm=xm, om=om: ep(
+                xm, *tsets[i % 2], out=om, stream=stream, tiled=True)
         best = None
         for name, fn in runs.items():
             mg = graphs_for(fn)

@@ -83,6 +83,13 @@ struct FtArgs {
     int64_t ldy;
     float *part;                 // partials [row blocks][maxp][2][TMAX][128]
     float *amax_out;             // nullable: max |y| of each token's 32-row groups, [t][amax_ld]
+    // tensor-parallel output (plain form; peer_base null otherwise): every
+    // finished row is stored into this rank's slot of every rank's buffer
+    // (peer_base[q] + peer_off, row stride ldy), and each CTA counts itself
+    // into every rank's flag[rank] (at flag_off) when it ends
+    uint8_t *const *peer_base;
+    int npeers, rank;
+    int64_t peer_off, flag_off;
     unsigned int *counter;       // [row blocks][4 quadrants], zero on entry, reset by the last arrival
     int n_w, n_b;                // ring depth (stages of weights + activation columns); n_b = n_w
     int amax_ld;
@@ -311,7 +318,12 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
                 val = a0 * sc0;
                 if (g.resid) val += g.resid[tt * g.ldr + n];
             }
-            g.y[tt * g.ldy + n] = val;
+            if (!DUAL && g.peer_base != nullptr) {
+                for (int q2 = 0; q2 < g.npeers; ++q2)
+                    reinterpret_cast<float *>(g.peer_base[q2] + g.peer_off)[tt * g.ldy + n] = val;
+            } else {
+                g.y[tt * g.ldy + n] = val;
+            }
             return fabsf(val);
         };
         // this warp's 32 rows of row block rb, token t: their largest |value|
@@ -402,6 +414,12 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
     }
     tc_fence_before();
     __syncthreads();
+    if (!DUAL && g.peer_base != nullptr && threadIdx.x == 0) {
+        // this CTA's rows are stored everywhere: count it into every rank
+        __threadfence_system();
+        for (int q2 = 0; q2 < g.npeers; ++q2)
+            atomicAdd_system(reinterpret_cast<unsigned int *>(g.peer_base[q2] + g.flag_off) + g.rank, 1u);
+    }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, TMEM_COLS);

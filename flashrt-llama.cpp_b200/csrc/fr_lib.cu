@@ -29,10 +29,18 @@ static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, 
 static int fp4_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, int K, const float *x, int64_t ldx,
                       const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
                       int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream);
+// tensor-parallel output of the plain form (see FtArgs); ctas_out receives
+// the number of CTAs launched, which each count into the flags
+struct TpOut {
+    uint8_t *const *peer_base;
+    int npeers, rank;
+    int64_t peer_off, flag_off;
+    unsigned *ctas_out;
+};
 static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const float *x, int64_t ldx,
                        const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
                        int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream,
-                       float *amax_out = nullptr, const float *amax_in = nullptr);
+                       float *amax_out = nullptr, const float *amax_in = nullptr, const TpOut *tp = nullptr);
 constexpr int FP4_MAX_T = 16;                      // tokens per launch of the FP4 tensor-core matvecs
 // Which matvec runs on weights in ggml's layout: the dp4a kernel for up to two
 // tokens and for shapes the TMA paths cannot take, the f16 tensor-core kernel
@@ -679,9 +687,27 @@ static int moe_launch_tt(const MoeParams &p, const MoePlan &pl, cudaStream_t str
     }
 }
 
+// fused_combine (plain form; nullable): if the combine is light enough to
+// ride on the last CTA of each row chunk (p.c_* set by the caller), it is
+// fused and *fused_combine is set; otherwise p.c_out is cleared.
 template <bool DUAL>
-static int moe_launch(MoeParams p, int max_active, int max_tok, cudaStream_t stream) {
+static int moe_launch(MoeParams p, int max_active, int max_tok, cudaStream_t stream, bool *fused_combine = nullptr) {
     const MoePlan pl = moe_plan(p.N, p.K, p.w_ld, DUAL, max_active, max_tok);
+    if (fused_combine) *fused_combine = false;
+    if (!DUAL && p.c_out != nullptr) {
+        bool ok = static_cast<long>(p.c_T) * pl.rows_per_cta <= 4096 && p.n_used <= MOE_MAX_USED;
+        if (ok) {
+            void *cnt = nullptr;
+            ok = workspace_get_zeroed(WS_MOECNT, static_cast<size_t>(pl.chunks) * sizeof(unsigned), stream, &cnt) ==
+                 FR_OK;
+            p.c_cnt = static_cast<unsigned int *>(cnt);
+        }
+        if (ok) {
+            if (fused_combine) *fused_combine = true;
+        } else {
+            p.c_out = nullptr;
+        }
+    }
     p.rows_per_cta = pl.rows_per_cta;
     p.chunks = pl.chunks;
     p.rows_per_stage = pl.RS;
@@ -842,7 +868,6 @@ int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const voi
     const size_t o_slots = take(static_cast<size_t>(S) * 4);
     const size_t o_q8x = take(static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES);
     const size_t o_glu = take(static_cast<size_t>(S) * n_ff * 4);
-    const size_t o_q8g = take(static_cast<size_t>(S) * (n_ff / 32) * Q8_BYTES);
     const size_t o_part = take(static_cast<size_t>(S) * n_embd * 4);
     void *wsp = nullptr;
     rc = workspace_get(WS_MOE, off, stream, &wsp);
@@ -856,7 +881,6 @@ int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const voi
     int32_t *slots = reinterpret_cast<int32_t *>(base + o_slots);
     uint8_t *q8x = base + o_q8x;
     float *glu = chk_glu ? chk_glu : reinterpret_cast<float *>(base + o_glu);
-    uint8_t *q8g = base + o_q8g;
     float *part = chk_part ? chk_part : reinterpret_cast<float *>(base + o_part);
 
     rc = route_launch(x, n_embd, w_r, T, n_embd, E, n_used, clamp_val, logits, ids, wts, eoff, slots, act, stream,
@@ -885,16 +909,16 @@ int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const voi
     const int max_active = std::min(E, S);
     rc = moe_launch<true>(p, max_active, T, stream);
     if (rc != FR_OK) return rc;
-    rc = quantize_launch(glu, n_ff, q8g, n_ff / 32, S, n_ff, stream);
-    if (rc != FR_OK) return rc;
+    // the down matvec quantizes the GLU rows to q8_1 as it stages them, and
+    // (for few tokens) its last CTA per row chunk does the combine
     MoeParams q{};
     q.w0 = static_cast<const uint8_t *>(wd);
     q.e_stride = ld_d * n_embd;
     q.w_ld = ld_d;
     q.N = n_embd;
     q.K = n_ff;
-    q.q8 = q8g;
-    q.ldq = n_ff / 32;
+    q.xf = glu;
+    q.ldxf = n_ff;
     q.bcast = 0;
     q.n_used = n_used;
     q.E = E;
@@ -905,8 +929,14 @@ int fr_moe_ffn_nvfp4(const float *x, const float *w_r, const void *wg, const voi
     q.out = part;
     q.ld_tok = static_cast<int64_t>(n_used) * n_embd;
     q.ld_slot = n_embd;
-    rc = moe_launch<false>(q, max_active, T, stream);
+    q.c_wts = wts;
+    q.c_resid = resid;
+    q.c_out = out;
+    q.c_T = T;
+    bool fused = false;
+    rc = moe_launch<false>(q, max_active, T, stream, &fused);
     if (rc != FR_OK) return rc;
+    if (fused) return FR_OK;
     return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream,
                       static_cast<const float *>(part), static_cast<const float *>(wts), resid, out, n_used, n_embd);
 }
@@ -1221,7 +1251,7 @@ static int fp4t_launch2(const FtArgs &a, int grid, bool dual, int nt, cudaStream
 static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const float *x, int64_t ldx,
                        const uint8_t *q8, int64_t ldq, int T, const float *s0, const float *s1, const float *resid,
                        int64_t ldr, float *y, int64_t ldy, bool dual, cudaStream_t stream, float *amax_out,
-                       const float *amax_in) {
+                       const float *amax_in, const TpOut *tp) {
     if (!w0 || (dual && !w1) || N <= 0 || K <= 0 || K % 256 != 0 || T <= 0 || !y) return FR_EINVAL;
     if ((reinterpret_cast<uintptr_t>(w0) & 15) || (w1 && (reinterpret_cast<uintptr_t>(w1) & 15))) return FR_EINVAL;
     const DevInfo &di = dev_info();
@@ -1273,6 +1303,15 @@ static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const
     a.counter = static_cast<unsigned int *>(wsp);
     a.amax_out = amax_out;
     a.amax_ld = n_rb * 4;
+    if (tp != nullptr) {
+        if (dual) return FR_EINVAL;
+        a.peer_base = tp->peer_base;
+        a.npeers = tp->npeers;
+        a.rank = tp->rank;
+        a.peer_off = tp->peer_off;
+        a.flag_off = tp->flag_off;
+        if (tp->ctas_out) *tp->ctas_out = static_cast<unsigned>(G) * static_cast<unsigned>((T + TW - 1) / TW);
+    }
     const int nq = K / Q8_ELEMS;
     for (int t0 = 0; t0 < T; t0 += TW) {
         const int tw = std::min(TW, T - t0);
@@ -1410,9 +1449,7 @@ static int moe_experts_impl(const float *x, int64_t ldx, const int32_t *eid, int
     const size_t o_eoff = take(static_cast<size_t>(E + 1) * 4);
     const size_t o_act = take(static_cast<size_t>(E + 1) * 4);
     const size_t o_slots = take(static_cast<size_t>(S) * 4);
-    const size_t o_q8x = take(static_cast<size_t>(S) * (n_embd / 32) * Q8_BYTES);
     const size_t o_glu = take(static_cast<size_t>(S) * n_ff * 4);
-    const size_t o_q8g = take(static_cast<size_t>(S) * (n_ff / 32) * Q8_BYTES);
     void *wsp = nullptr;
     int rc = workspace_get(WS_MOE, off, stream, &wsp);
     if (rc != FR_OK) return rc;
@@ -1420,9 +1457,7 @@ static int moe_experts_impl(const float *x, int64_t ldx, const int32_t *eid, int
     int32_t *eoff = reinterpret_cast<int32_t *>(base + o_eoff);
     int32_t *act = reinterpret_cast<int32_t *>(base + o_act);
     int32_t *slots = reinterpret_cast<int32_t *>(base + o_slots);
-    uint8_t *q8x = base + o_q8x;
     float *glu = reinterpret_cast<float *>(base + o_glu);
-    uint8_t *q8g = base + o_q8g;
     static bool attr_done[64] = {};
     rc = allow_max_smem(k_group_ids, attr_done);
     if (rc != FR_OK) return rc;
@@ -1430,8 +1465,7 @@ static int moe_experts_impl(const float *x, int64_t ldx, const int32_t *eid, int
     rc = launch_pdl(k_group_ids, dim3(1), dim3(1024), group_smem(S, 1), stream, eid, static_cast<int64_t>(1), S, 1, E,
                     eoff, slots, act, skip_neg);
     if (rc != FR_OK) return rc;
-    rc = quantize_launch(x, ldx, q8x, n_embd / 32, S, n_embd, stream);
-    if (rc != FR_OK) return rc;
+    // both matvecs quantize their f32 input rows to q8_1 as they stage them
     MoeParams p{};
     p.w0 = static_cast<const uint8_t *>(wg);
     p.w1 = static_cast<const uint8_t *>(wu);
@@ -1439,8 +1473,8 @@ static int moe_experts_impl(const float *x, int64_t ldx, const int32_t *eid, int
     p.w_ld = ld_gu;
     p.N = n_ff;
     p.K = n_embd;
-    p.q8 = q8x;
-    p.ldq = n_embd / 32;
+    p.xf = x;
+    p.ldxf = ldx;
     p.bcast = 1;
     p.n_used = 1;
     p.E = E;
@@ -1455,16 +1489,14 @@ static int moe_experts_impl(const float *x, int64_t ldx, const int32_t *eid, int
     const int max_active = std::min(E, S);
     rc = moe_launch<true>(p, max_active, S, stream);
     if (rc != FR_OK) return rc;
-    rc = quantize_launch(glu, n_ff, q8g, n_ff / 32, S, n_ff, stream);
-    if (rc != FR_OK) return rc;
     MoeParams q{};
     q.w0 = static_cast<const uint8_t *>(wd);
     q.e_stride = ld_d * n_embd;
     q.w_ld = ld_d;
     q.N = n_embd;
     q.K = n_ff;
-    q.q8 = q8g;
-    q.ldq = n_ff / 32;
+    q.xf = glu;
+    q.ldxf = n_ff;
     q.bcast = 1;
     q.n_used = 1;
     q.E = E;
@@ -1694,6 +1726,85 @@ static int fp4e_run(FeArgs a, bool dual, const float *x, int64_t ldx, int rows, 
 
 static bool fe_shape_ok(int N, int K) { return N > 0 && K > 0 && N % 128 == 0 && K % 256 == 0; }
 
+// Expert FFN over pre-routed rows (row s to expert eid[s]; -1 skipped when
+// skip_neg) on tile-major experts: grouping, then the gate/up pair and the
+// down projection on the FP4 tensor cores.
+static int moe_experts_tiled_impl(const float *x, int64_t ldx, const int32_t *eid, int S, const void *wg_t,
+                                  const void *wu_t, const void *wd_t, const float *sg, const float *su,
+                                  const float *sd, float *out, int64_t ldo, int n_embd, int n_ff, int E, int skip_neg,
+                                  cudaStream_t stream) {
+    if (S < 0 || E <= 0 || E > FE_MAX_E || !fe_shape_ok(n_ff, n_embd) || !fe_shape_ok(n_embd, n_ff)) return FR_EINVAL;
+    if (S == 0) return FR_OK;
+    if (!x || !eid || !wg_t || !wu_t || !wd_t || !out || ldx < n_embd || ldo < n_embd || S > MOE_MAX_SLOTS)
+        return FR_EINVAL;
+    if (!aligned16(wg_t) || !aligned16(wu_t) || !aligned16(wd_t)) return FR_EINVAL;
+    const int kq_gu = n_embd / 256, kq_d = n_ff / 256;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_eoff = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_act = take(static_cast<size_t>(E + 1) * 4);
+    const size_t o_slots = take(static_cast<size_t>(S) * 4);
+    const size_t o_gx = take(static_cast<size_t>(S) * FM_GSTRIDE * 4);
+    const size_t o_ix = take(static_cast<size_t>(S) * kq_gu * 1024);
+    const size_t o_glu = take(static_cast<size_t>(S) * n_ff * 4);
+    const size_t o_gg = take(static_cast<size_t>(S) * FM_GSTRIDE * 4);
+    const size_t o_ig = take(static_cast<size_t>(S) * kq_d * 1024);
+    void *wsp = nullptr;
+    int rc = workspace_get(WS_MOE, off, stream, &wsp);
+    if (rc != FR_OK) return rc;
+    uint8_t *base = static_cast<uint8_t *>(wsp);
+    int32_t *eoff = reinterpret_cast<int32_t *>(base + o_eoff);
+    int32_t *act = reinterpret_cast<int32_t *>(base + o_act);
+    int32_t *slots = reinterpret_cast<int32_t *>(base + o_slots);
+    float *glu = reinterpret_cast<float *>(base + o_glu);
+    static bool attr_done[64] = {};
+    rc = allow_max_smem(k_group_ids, attr_done);
+    if (rc != FR_OK) return rc;
+    rc = launch_pdl(k_group_ids, dim3(1), dim3(1024), group_smem(S, 1), stream, eid, static_cast<int64_t>(1), S, 1, E,
+                    eoff, slots, act, skip_neg);
+    if (rc != FR_OK) return rc;
+    const int max_active = std::min(E, S);
+    FeArgs a{};
+    a.N = n_ff;
+    a.K = n_embd;
+    a.n_rb = n_ff / 128;
+    a.E = E;
+    a.n_used = 1;
+    a.bcast = 0;
+    a.eoff = eoff;
+    a.slots = slots;
+    a.act = act;
+    a.w0 = static_cast<const uint8_t *>(wg_t);
+    a.w1 = static_cast<const uint8_t *>(wu_t);
+    a.e_stride = static_cast<int64_t>(n_ff / 128) * kq_gu * FT_TILE;
+    a.s0 = sg;
+    a.s1 = su;
+    a.y = glu;
+    a.ld_tok = n_ff;
+    a.ld_slot = 0;
+    rc = fp4e_run(a, true, x, ldx, S, S, max_active, base + o_ix, reinterpret_cast<float *>(base + o_gx), stream);
+    if (rc != FR_OK) return rc;
+    FeArgs d{};
+    d.N = n_embd;
+    d.K = n_ff;
+    d.n_rb = n_embd / 128;
+    d.E = E;
+    d.n_used = 1;
+    d.bcast = 0;
+    d.eoff = eoff;
+    d.slots = slots;
+    d.act = act;
+    d.w0 = static_cast<const uint8_t *>(wd_t);
+    d.w1 = d.w0;
+    d.e_stride = static_cast<int64_t>(n_embd / 128) * kq_d * FT_TILE;
+    d.s0 = sd;
+    d.y = out;
+    d.ld_tok = ldo;
+    d.ld_slot = 0;
+    return fp4e_run(d, false, glu, n_ff, S, S, max_active, base + o_ig, reinterpret_cast<float *>(base + o_gg),
+                    stream);
+}
+
 } // namespace frb
 
 extern "C" {
@@ -1868,11 +1979,14 @@ int64_t fr_ep_buffer_bytes(int T_max, int n_embd, int n_used, int nranks) {
     return ep_layout(T_max, n_embd, n_used, nranks).total;
 }
 
-int fr_ep_moe_nvfp4(const float *x, const float *w_r, const void *wg_local, const void *wu_local,
-                    const void *wd_local, const float *sg, const float *su, const float *sd, const float *resid,
-                    float *out, int T, int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val, int nranks,
-                    int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream) {
-    if (fault_hit("fr_ep_moe_nvfp4")) return FR_EINJECTED;
+} // extern "C"
+
+namespace frb {
+static int ep_moe_impl(const float *x, const float *w_r, const void *wg_local, const void *wu_local,
+                       const void *wd_local, const float *sg, const float *su, const float *sd, const float *resid,
+                       float *out, int T, int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val,
+                       int nranks, int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes,
+                       bool tiled, cudaStream_t stream) {
     int rc = check_route_shape(T, n_embd, E, n_used);
     if (rc != FR_OK) return rc;
     if (!x || !w_r || !wg_local || !wu_local || !wd_local || !out || !peer_base || !local_base) return FR_EINVAL;
@@ -1920,9 +2034,14 @@ int fr_ep_moe_nvfp4(const float *x, const float *w_r, const void *wg_local, cons
                     static_cast<int64_t>(0));
     if (rc != FR_OK) return rc;
     // this rank's experts over everything it received (empty slots skipped)
-    rc = moe_experts_impl(reinterpret_cast<const float *>(base + L.recv_x), n_embd,
-                          reinterpret_cast<const int32_t *>(base + L.recv_eid), nranks * cap, wg_local, wu_local,
-                          wd_local, sg, su, sd, y, n_embd, n_embd, n_ff, E_p, 1, stream);
+    if (tiled)
+        rc = moe_experts_tiled_impl(reinterpret_cast<const float *>(base + L.recv_x), n_embd,
+                                    reinterpret_cast<const int32_t *>(base + L.recv_eid), nranks * cap, wg_local,
+                                    wu_local, wd_local, sg, su, sd, y, n_embd, n_embd, n_ff, E_p, 1, stream);
+    else
+        rc = moe_experts_impl(reinterpret_cast<const float *>(base + L.recv_x), n_embd,
+                              reinterpret_cast<const int32_t *>(base + L.recv_eid), nranks * cap, wg_local, wu_local,
+                              wd_local, sg, su, sd, y, n_embd, n_embd, n_ff, E_p, 1, stream);
     if (rc != FR_OK) return rc;
     // outputs back to the slots they came from
     rc = launch_pdl(k_ep_return, dim3(EP_CTAS), dim3(256), 0, stream, static_cast<const float *>(y),
@@ -1938,6 +2057,27 @@ int fr_ep_moe_nvfp4(const float *x, const float *w_r, const void *wg_local, cons
     return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream,
                       reinterpret_cast<const float *>(base + L.back), static_cast<const float *>(wts), resid, out,
                       n_used, n_embd);
+}
+} // namespace frb
+
+extern "C" {
+
+int fr_ep_moe_nvfp4(const float *x, const float *w_r, const void *wg_local, const void *wu_local,
+                    const void *wd_local, const float *sg, const float *su, const float *sd, const float *resid,
+                    float *out, int T, int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val, int nranks,
+                    int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream) {
+    if (fault_hit("fr_ep_moe_nvfp4")) return FR_EINJECTED;
+    return ep_moe_impl(x, w_r, wg_local, wu_local, wd_local, sg, su, sd, resid, out, T, T_max, n_embd, n_ff, E,
+                       n_used, clamp_val, nranks, rank, peer_base, local_base, buffer_bytes, false, stream);
+}
+
+int fr_ep_moe_tiled(const float *x, const float *w_r, const void *wg_t, const void *wu_t, const void *wd_t,
+                    const float *sg, const float *su, const float *sd, const float *resid, float *out, int T,
+                    int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val, int nranks, int rank,
+                    void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream) {
+    if (fault_hit("fr_ep_moe_tiled")) return FR_EINJECTED;
+    return ep_moe_impl(x, w_r, wg_t, wu_t, wd_t, sg, su, sd, resid, out, T, T_max, n_embd, n_ff, E, n_used,
+                       clamp_val, nranks, rank, peer_base, local_base, buffer_bytes, true, stream);
 }
 
 int fr_ipc_alloc(int64_t bytes, void **dev_ptr, void *handle64) {
@@ -2007,28 +2147,41 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
 
     unsigned expect;
     if (tiled || (use_tc(wg_shard, wu_shard, ld_gu, n_embd, T) && use_tc(wd_shard, nullptr, ld_d, F_p, T))) {
-        // tensor-core matvecs, the partial output into this rank's own slot,
-        // then a push kernel stores it into every peer's slot
+        // tensor-core matvecs: on tile-major shards the down matvec's
+        // epilogue stores the partial output into every rank's slot itself;
+        // on ggml's layout it goes into this rank's own slot and a push
+        // kernel stores it into every peer's slot
         constexpr int PUSH_CTAS = 64;
         float *slot = reinterpret_cast<float *>(base + slot_off);
         if (tiled) {
-            rc = fp4t_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), F_p,
-                             n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
+            // the down matvec's epilogue stores its rows into every rank's
+            // slot and counts each CTA into the flags: no push kernel
+            void *am = nullptr;
+            rc = workspace_get(WS_AMAX, static_cast<size_t>(T) * (F_p / 32) * sizeof(float), stream, &am);
             if (rc != FR_OK) return rc;
+            rc = fp4t_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), F_p,
+                             n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream,
+                             static_cast<float *>(am));
+            if (rc != FR_OK) return rc;
+            unsigned ctas = 0;
+            const TpOut to{pb, nranks, rank, slot_off, L.flags, &ctas};
             rc = fp4t_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, n_embd, F_p, glu, F_p, nullptr, 0, T,
-                             sd, nullptr, nullptr, 0, slot, n_embd, false, stream);
+                             sd, nullptr, nullptr, 0, slot, n_embd, false, stream, nullptr,
+                             static_cast<const float *>(am), &to);
+            if (rc != FR_OK) return rc;
+            expect = ctas;
         } else {
             rc = tcx_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), ld_gu,
                             F_p, n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
             if (rc != FR_OK) return rc;
             rc = tcx_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, ld_d, n_embd, F_p, glu, F_p, nullptr, 0,
                             T, sd, nullptr, nullptr, 0, slot, n_embd, false, stream);
+            if (rc != FR_OK) return rc;
+            rc = launch_pdl(k_tp_push, dim3(PUSH_CTAS), dim3(256), 0, stream, pb, nranks, rank, slot_off,
+                            static_cast<int64_t>(n_embd), static_cast<int64_t>(0), T, n_embd, L.flags);
+            expect = PUSH_CTAS;
         }
         if (rc != FR_OK) return rc;
-        rc = launch_pdl(k_tp_push, dim3(PUSH_CTAS), dim3(256), 0, stream, pb, nranks, rank, slot_off,
-                        static_cast<int64_t>(n_embd), static_cast<int64_t>(0), T, n_embd, L.flags);
-        if (rc != FR_OK) return rc;
-        expect = PUSH_CTAS;
     } else {
         void *q8x = nullptr, *q8g = nullptr;
         rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES, stream, &q8x);

@@ -347,13 +347,31 @@ struct MoeParams {
     int N, K;                   // rows per expert, row length
     const uint8_t *q8;          // q8_1 rows: token rows (bcast) or slot rows
     int64_t ldq;                // blocks per q8 row
+    const float *xf;            // or f32 rows (same indexing), quantized to q8_1 while staged
+    int64_t ldxf;
     int bcast, n_used, E;
     const int32_t *eoff, *slots, *act;
     const float *s0, *s1;       // per-expert scales [E] (nullable)
     float *out;                 // row of slot (t, k): out + t*ld_tok + k*ld_slot
     int64_t ld_tok, ld_slot;
     int rows_per_cta, chunks, rows_per_stage, slot_bytes, word_mode;
+    // fused combine (plain form, slot rows packed [T][n_used][N]; c_out null
+    // otherwise): the last CTA of a row chunk to finish, over the active
+    // experts, writes c_out[t][rows] = sum_k out[t][k][rows] * c_wts[t][k]
+    // (+ c_resid) -- k_moe_combine's arithmetic; c_cnt[chunk] zero on entry
+    const float *c_wts, *c_resid;
+    float *c_out;
+    unsigned int *c_cnt;
+    int c_T;
 };
+
+// out[t, r] of the slot-order combine (k ascending); shared by k_moe_combine
+// and the fused form, so both round alike
+__device__ __forceinline__ float moe_combine_value(const float *pt, const float *ws, int n_used, int64_t n_embd) {
+    float sum = pt[0] * ws[0];
+    for (int k = 1; k < n_used; ++k) sum += pt[static_cast<int64_t>(k) * n_embd] * ws[k];
+    return sum;
+}
 
 template <int LG, int TT, bool DUAL>
 __global__ void __launch_bounds__(GV_THREADS) k_moe_gemv(const MoeParams p) {
@@ -363,6 +381,7 @@ __global__ void __launch_bounds__(GV_THREADS) k_moe_gemv(const MoeParams p) {
     const int RS = p.rows_per_stage;
     __shared__ int tok_row[TT];       // q8 row per staged token
     __shared__ int out_off[TT];       // t*ld_tok + k*ld_slot
+    bool bad = false;                 // a bounded wait of this warp gave up
 
     fr_pdl_wait();
     const int a = blockIdx.x / p.chunks, chunk = blockIdx.x % p.chunks;
@@ -435,18 +454,34 @@ __global__ void __launch_bounds__(GV_THREADS) k_moe_gemv(const MoeParams p) {
             float *ad = reinterpret_cast<float *>(act_d);
             for (int c = warp; c < nt * nc; c += GV_CWARPS) {
                 const int t = c / nc, ch = c % nc;
-                const uint8_t *blk = p.q8 + (static_cast<int64_t>(tok_row[t]) * p.ldq + ch) * Q8_BYTES;
-                const int8_t q = static_cast<int8_t>(blk[4 + lane]);
+                int8_t q;
+                float dh;                            // the f16-rounded q8_1 scale
+                if (p.xf != nullptr) {
+                    const q8_lane r = q8_1_chunk(
+                        p.xf[static_cast<int64_t>(tok_row[t]) * p.ldxf + static_cast<int64_t>(ch) * Q8_ELEMS + lane]);
+                    q = static_cast<int8_t>(r.q);
+                    dh = __half2float(__float2half_rn(r.d));
+                } else {
+                    const uint8_t *blk = p.q8 + (static_cast<int64_t>(tok_row[t]) * p.ldq + ch) * Q8_BYTES;
+                    q = static_cast<int8_t>(blk[4 + lane]);
+                    dh = __low2float(*reinterpret_cast<const __half2 *>(blk));
+                }
                 const int b = ch >> 1;
                 const int s = ((ch & 1) << 1) | (lane >> 4);
                 const int sl = (t * NB + b) * 4 + (s ^ ((b >> 1) & 3));
                 aq[sl * 16 + act_perm(lane & 15)] = static_cast<uint8_t>(q);
-                if (lane == 0) ad[(t * NB + b) * 2 + (ch & 1)] = 0.5f * __low2float(*reinterpret_cast<const __half2 *>(blk));
+                if (lane == 0) ad[(t * NB + b) * 2 + (ch & 1)] = 0.5f * dh;
             }
         }
         named_bar(1, GV_CWARPS * 32);
         for (int i = warp; i < n_st; i += GV_CWARPS) {
-            if (!waited && !mbar_wait(&full[i], 0, 3)) return;
+            // after a copy that never arrived (status word flagged) the warp
+            // computes nothing more, but stays for the named barriers
+            if (bad) continue;
+            if (!waited && !mbar_wait(&full[i], 0, 3)) {
+                bad = true;
+                continue;
+            }
             const int rows = min(RS, n_rows - i * RS);
             const uint8_t *st = ring + static_cast<size_t>(i) * p.slot_bytes;
             float acc0[TT], acc1[TT];
@@ -494,6 +529,34 @@ __global__ void __launch_bounds__(GV_THREADS) k_moe_gemv(const MoeParams p) {
         named_bar(1, GV_CWARPS * 32);
     }
     fr_pdl_trigger();
+    if (!DUAL && p.c_out != nullptr) {
+        // this CTA's slot rows are written: count it for its chunk; the last
+        // of the chunk's active experts combines the chunk's rows
+        __shared__ int s_last;
+        __shared__ float s_w[4 * MOE_MAX_USED];
+        fence_acq_rel_gpu();
+        named_bar(1, GV_CWARPS * 32);
+        if (threadIdx.x == 0)
+            s_last = atomicAdd(&p.c_cnt[chunk], 1u) == static_cast<unsigned>(n_act - 1);
+        named_bar(1, GV_CWARPS * 32);
+        if (!s_last) return;
+        fence_acq_rel_gpu();
+        for (int t0 = 0; t0 < p.c_T; t0 += 4) {
+            const int tn = min(4, p.c_T - t0);
+            for (int i = threadIdx.x; i < tn * p.n_used; i += GV_CWARPS * 32)
+                s_w[i] = p.c_wts[static_cast<int64_t>(t0) * p.n_used + i];
+            named_bar(1, GV_CWARPS * 32);
+            for (int i = threadIdx.x; i < tn * n_rows; i += GV_CWARPS * 32) {
+                const int tl = i / n_rows, r = r_begin + i % n_rows, t = t0 + tl;
+                const float *pt = p.out + static_cast<int64_t>(t) * p.n_used * p.N + r;
+                float sum = moe_combine_value(pt, s_w + tl * p.n_used, p.n_used, p.N);
+                if (p.c_resid) sum = sum + p.c_resid[static_cast<int64_t>(t) * p.N + r];
+                p.c_out[static_cast<int64_t>(t) * p.N + r] = sum;
+            }
+            named_bar(1, GV_CWARPS * 32);
+        }
+        if (threadIdx.x == 0) p.c_cnt[chunk] = 0;
+    }
 }
 
 // ------------------------------------------------------------ combine
@@ -510,8 +573,7 @@ __global__ void __launch_bounds__(256) k_moe_combine(const float *__restrict__ p
     __syncthreads();
     if (r >= n_embd) return;
     const float *pt = part + static_cast<int64_t>(t) * n_used * n_embd + r;
-    float sum = pt[0] * ws[0];
-    for (int k = 1; k < n_used; ++k) sum += pt[static_cast<int64_t>(k) * n_embd] * ws[k];
+    float sum = moe_combine_value(pt, ws, n_used, n_embd);
     if (resid) sum = sum + resid[static_cast<int64_t>(t) * n_embd + r];
     out[static_cast<int64_t>(t) * n_embd + r] = sum;
 }

@@ -72,6 +72,8 @@ SIGNATURES = {
     "fr_ep_buffer_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "fr_ep_moe_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
                                _f32, _i32, _i32, _vp, _vp, _i64, _vp]),
+    "fr_ep_moe_tiled": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
+                               _f32, _i32, _i32, _vp, _vp, _i64, _vp]),
     "fr_ipc_alloc": (_i32, [_i64, C.POINTER(C.c_void_p), _vp]),
     "fr_ipc_open": (_i32, [_vp, C.POINTER(C.c_void_p)]),
     "fr_ipc_close": (_i32, [_vp]),

@@ -197,14 +197,16 @@ class EpMoe(_PeerBuffer):
         self.max_tokens, self.n_embd, self.n_ff, self.E, self.n_used = max_tokens, n_embd, n_ff, E, n_used
 
     def __call__(self, x, w_r, wg_local, wu_local, wd_local, sg=None, su=None, sd=None, resid=None, out=None,
-                 clamp=6.103515625e-5, stream=None):
+                 clamp=6.103515625e-5, stream=None, tiled=False):
+        """tiled: the local experts are tile-major (frb200.tile_experts), run
+        on the FP4 tensor cores (fr_ep_moe_tiled)."""
         import torch
         T = x.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
         if out is None:
             out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
-        call("fr_ep_moe_nvfp4", _ptr(x), _ptr(w_r), _ptr(wg_local), _ptr(wu_local), _ptr(wd_local), _ptr(sg), _ptr(su),
+        call("fr_ep_moe_tiled" if tiled else "fr_ep_moe_nvfp4", _ptr(x), _ptr(w_r), _ptr(wg_local), _ptr(wu_local), _ptr(wd_local), _ptr(sg), _ptr(su),
              _ptr(sd), _ptr(resid), _ptr(out), T, self.max_tokens, self.n_embd, self.n_ff, self.E, self.n_used,
              clamp, self.world, self.rank, _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes,
              _stream(stream))

@@ -309,6 +309,15 @@ int fr_ep_moe_nvfp4(const float *x, const float *w_r, const void *wg_local, cons
                     const void *wd_local, const float *sg, const float *su, const float *sd, const float *resid,
                     float *out, int T, int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val, int nranks,
                     int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream);
+/* The same layer with this rank's experts repacked tile-major
+ * (fr_nvfp4_tile on its stacked [E/P * N, K] expert tensors): the received
+ * rows run on the FP4 tensor cores (windows of up to 8 rows per expert);
+ * results equal fr_moe_ffn_tiled's to the f32 rounding of the split-K
+ * partial sums.  n_embd, n_ff multiples of 256. */
+int fr_ep_moe_tiled(const float *x, const float *w_r, const void *wg_t, const void *wu_t, const void *wd_t,
+                    const float *sg, const float *su, const float *sd, const float *resid, float *out, int T,
+                    int T_max, int n_embd, int n_ff, int E, int n_used, float clamp_val, int nranks, int rank,
+                    void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream);
 
 /* Peer buffers for fr_tp_ffn_nvfp4 without any library-side multicast
  * object: fr_ipc_alloc returns a zeroed device buffer and its 64-byte CUDA

@@ -82,6 +82,22 @@ def _worker(rank, world, port, q):
                 bad.append(f"graph replay {i}: max |d| {float((yg - ref).abs().max()):.3e}")
         del g
         torch.cuda.synchronize()
+        # tile-major experts (fr_ep_moe_tiled) against the single-GPU tiled
+        # layer: equal to the f32 rounding of the split-K partial sums, whose
+        # grouping follows each launch's work split (normwise 1e-5)
+        tg, tu, td = (frb200.tile_experts(lg, Ep, nf, ne), frb200.tile_experts(lu, Ep, nf, ne),
+                      frb200.tile_experts(ld, Ep, ne, nf))
+        Fg, Fu, Fd = (frb200.tile_experts(fg, E, nf, ne), frb200.tile_experts(fu, E, nf, ne),
+                      frb200.tile_experts(fd, E, ne, nf))
+        for i, T in enumerate((1, 16, 7)):
+            x = t(frb200.synth_normal(90 + 7 * rank + i, T * ne).reshape(T, ne))
+            y = ep(x, wr, tg, tu, td, tiled=True)
+            ref = frb200.moe_ffn_tiled(x, wr, Fg, Fu, Fd, ne, nf, E, n_used)
+            torch.cuda.synchronize()
+            err = float((y - ref).norm() / ref.norm())
+            if not (err <= 1e-5 and bool(torch.isfinite(y).all())):
+                bad.append(f"tiled T={T}: normwise {err:.3e}")
+        torch.cuda.synchronize()
         q.put((rank, bad, frb200.device_status()))
     except Exception as e:  # noqa: BLE001 - report to the parent instead of hanging it
         q.put((rank, bad + [repr(e)], -1))
