@@ -79,6 +79,63 @@ __device__ __forceinline__ void f16_split(__half h, int &m, int &E) {
 // expert windows); sfb may then be null.  x_k follows quantize_q8_1 exactly
 // (d = f16(amax / 127), q = roundf(x / d)); the input is f32 rows or q8_1
 // blocks.  Grid (slices, T), 256 threads; warp per q8_1 block.
+// The eight E2M1 digit nibbles of this lane's value of one q8_1 block (q,
+// f16 scale hd) against the token's reference exponent e0:
+// r = q * m * 2^(E - e0) exact for E >= e0, rounded half away from zero below.
+__device__ __forceinline__ void fp4_digits(int q, __half hd, int e0, uint32_t (&nib)[FM_DIGITS]) {
+    int m, E;
+    f16_split(hd, m, E);
+    const int v = q * m;
+    int r = 0;
+    if (m != 0) {
+        const int sh = E - e0;
+        if (sh >= 0) {
+            r = v * (1 << sh);
+        } else if (sh > -31) {
+            const int s2 = -sh;
+            const int a = (v < 0 ? -v : v);
+            const int ra = (a + (1 << (s2 - 1))) >> s2;
+            r = v < 0 ? -ra : ra;
+        }
+    }
+    int R = r + FM_BIAS;                             // 0 <= R < 9^8
+#pragma unroll
+    for (int p = 0; p < FM_DIGITS; ++p) {
+        const int dgt = R % 9;
+        R /= 9;
+        const int c = dgt - 4;
+        nib[p] = c < 0 ? (8u | static_cast<uint32_t>(-c)) : static_cast<uint32_t>(c);
+    }
+}
+
+// Store a warp's digits of q8_1 block `c` (0..7) of a 256-value K stage into
+// the stage's column tile (rows n0 .. n0+7, 128-byte-swizzled K-major):
+// lanes j and j+8 of a sub-block share a byte, as ggml packs the weights.
+__device__ __forceinline__ void fp4_digits_store(const uint32_t (&nib)[FM_DIGITS], uint8_t *tile, int n0, int c) {
+    const int lane = threadIdx.x & 31;
+    const int kbl = c >> 1;
+    const int sbk = (c & 1) * 2 + (lane >> 4);       // sub-block inside the 64-block
+    const int j = lane & 15;
+#pragma unroll
+    for (int p = 0; p < FM_DIGITS; ++p) {
+        const uint32_t hi = __shfl_xor_sync(0xffffffffu, nib[p], 8);
+        if (j < 8) {
+            const int n = n0 + p;
+            const int idx = kbl * 32 + sbk * 8 + j;
+            const int c16 = idx >> 4;
+            tile[n * 128 + ((c16 ^ (n & 7)) << 4) + (idx & 15)] = static_cast<uint8_t>(nib[p] | (hi << 4));
+        }
+    }
+}
+
+// f16 exponent of amax / 127 (the q8_1 scale of the row's largest block),
+// -1000 for a zero row
+__device__ __forceinline__ int fp4_row_emax(float amax) {
+    int m, E;
+    f16_split(__float2half_rn(__fdiv_rn(amax, 127.0f)), m, E);
+    return E;
+}
+
 // One CTA's share (slice `slice` of `nslices`) of token t's columns; every
 // thread of the 256-thread CTA calls it.
 __device__ __forceinline__ void act_fp4_row(const float *__restrict__ x, int64_t ldx,
@@ -107,9 +164,7 @@ __device__ __forceinline__ void act_fp4_row(const float *__restrict__ x, int64_t
         for (int i = threadIdx.x; i < n_amax; i += blockDim.x) amax = fmaxf(amax, amax_in[static_cast<int64_t>(t) * n_amax + i]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        int m, E;
-        f16_split(__float2half_rn(__fdiv_rn(amax, 127.0f)), m, E);
-        emax = E;
+        emax = fp4_row_emax(amax);
     } else if (x != nullptr) {
         // many independent loads in flight per thread, 16-byte loads when the
         // row allows them
@@ -183,47 +238,14 @@ __device__ __forceinline__ void act_fp4_row(const float *__restrict__ x, int64_t
             q = static_cast<int8_t>(blk[4 + lane]);
             hd = __low2half(*reinterpret_cast<const __half2 *>(blk));
         }
-        int m, E;
-        f16_split(hd, m, E);
-        // r = q * m * 2^(E - e0): exact for E >= e0, rounded half away from
-        // zero below
-        const int v = q * m;
-        int r = 0;
-        if (m != 0) {
-            const int sh = E - e0;
-            if (sh >= 0) {
-                r = v * (1 << sh);
-            } else if (sh > -31) {
-                const int s2 = -sh;
-                const int a = (v < 0 ? -v : v);
-                const int ra = (a + (1 << (s2 - 1))) >> s2;
-                r = v < 0 ? -ra : ra;
-            }
-        }
-        int R = r + FM_BIAS;                         // 0 <= R < 9^8
         uint32_t nib[FM_DIGITS];
-#pragma unroll
-        for (int p = 0; p < FM_DIGITS; ++p) {
-            const int dgt = R % 9;
-            R /= 9;
-            const int c = dgt - 4;
-            nib[p] = c < 0 ? (8u | static_cast<uint32_t>(-c)) : static_cast<uint32_t>(c);
-        }
-        const int kb = b >> 1, kq = kb >> 2, kbl = kb & 3;
+        fp4_digits(q, hd, e0, nib);
+        const int kb = b >> 1, kq = kb >> 2;
         const int sbk = (b & 1) * 2 + (lane >> 4);   // sub-block inside the 64-block
         const int j = lane & 15;
         uint8_t *img = bimg + t * t_stride + static_cast<int64_t>(kq) * NCOL * 128;
         const int n0 = t_stride > 0 ? 0 : FM_DIGITS * t;
-#pragma unroll
-        for (int p = 0; p < FM_DIGITS; ++p) {
-            const uint32_t hi = __shfl_xor_sync(0xffffffffu, nib[p], 8);
-            if (j < 8) {
-                const int n = n0 + p;
-                const int idx = kbl * 32 + sbk * 8 + j;
-                const int c16 = idx >> 4;
-                img[n * 128 + ((c16 ^ (n & 7)) << 4) + (idx & 15)] = static_cast<uint8_t>(nib[p] | (hi << 4));
-            }
-        }
+        fp4_digits_store(nib, img, n0, b & 7);
         if (j == 0 && sfb != nullptr) {
 #pragma unroll
             for (int p = 0; p < FM_DIGITS; ++p) {
