@@ -44,9 +44,11 @@ __device__ __forceinline__ uint64_t fr_now_ns() {
     return t;
 }
 
-// Every spin in these kernels gives up after this long (kernels run for
-// microseconds; the bound only matters when something is broken).
-constexpr uint64_t FR_WAIT_NS = 2000000000ull;
+// Every spin in these kernels gives up after g_fr_wait_ns nanoseconds
+// (kernels run for microseconds; the bound only matters when something is
+// broken).  2 s unless fr_set_wait_ns shortened it.
+constexpr uint64_t FR_WAIT_NS_MAX = 2000000000ull;
+__device__ unsigned long long g_fr_wait_ns = FR_WAIT_NS_MAX;
 
 // ---------------------------------------------------------------- PDL
 // GPU-scope acquire/release fence: with a relaxed atomic it forms the
@@ -87,13 +89,13 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait on phase `parity`: false (and the status word flagged with
-// `site`) when the phase did not complete within FR_WAIT_NS.
+// `site`) when the phase did not complete within g_fr_wait_ns.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned site) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = fr_now_ns();
     for (uint32_t i = 0;; ++i) {
         if (mbar_try(bar, parity)) return true;
-        if ((i & 63) == 0 && fr_now_ns() - t0 > FR_WAIT_NS) {
+        if ((i & 63) == 0 && fr_now_ns() - t0 > g_fr_wait_ns) {
             fr_flag(FR_ST_TIMEOUT | (site << FR_ST_SITE_SHIFT));
             return false;
         }

@@ -90,6 +90,8 @@ struct FtArgs {
     uint8_t *const *peer_base;
     int npeers, rank;
     int64_t peer_off, flag_off;
+    const unsigned int *epoch;   // step parity of the receiving slots (as GvParams::epoch)
+    int64_t par_bytes;
     unsigned int *counter;       // [row blocks][4 quadrants], zero on entry, reset by the last arrival
     int n_w, n_b;                // ring depth (stages of weights + activation columns); n_b = n_w
     int amax_ld;
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
         named_bar(1, 128);
         const float sc0 = g.s0 ? *g.s0 : 1.0f;
         const float sc1 = (DUAL && g.s1) ? *g.s1 : 1.0f;
+        const int64_t peer_off = g.peer_off + (g.epoch ? static_cast<int64_t>(*g.epoch & 1u) * g.par_bytes : 0);
 
         // writes one output value; returns |value| (0 for rows past N)
         auto finish = [&](int rb, int t, float a0, float a1) -> float {
@@ -320,7 +323,7 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
             }
             if (!DUAL && g.peer_base != nullptr) {
                 for (int q2 = 0; q2 < g.npeers; ++q2)
-                    reinterpret_cast<float *>(g.peer_base[q2] + g.peer_off)[tt * g.ldy + n] = val;
+                    reinterpret_cast<float *>(g.peer_base[q2] + peer_off)[tt * g.ldy + n] = val;
             } else {
                 g.y[tt * g.ldy + n] = val;
             }

@@ -90,6 +90,11 @@ struct GvParams {
     uint8_t *const *peer_base;
     int npeers, rank;
     int64_t peer_off, flag_off, col_off;
+    // step parity of the receiving slots: the values go to peer_off +
+    // (epoch[0] & 1) * par_bytes (the reduce's step count, final by the time
+    // the epilogue runs; null = parity 0)
+    const unsigned int *epoch;
+    int64_t par_bytes;
 };
 
 // Bounded wait of one lane for flags[r] to reach seen + expect (counters only
@@ -102,7 +107,7 @@ __device__ __forceinline__ void tp_flag_wait(const unsigned int *flags, unsigned
         unsigned int v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
         if (static_cast<int>(v - target) >= 0) break;
-        if (fr_now_ns() - t0 > FR_WAIT_NS) {
+        if (fr_now_ns() - t0 > g_fr_wait_ns) {
             fr_flag(FR_ST_TIMEOUT | (30u << FR_ST_SITE_SHIFT));
             break;
         }
@@ -356,6 +361,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
 
     const float sc0 = p.s0 ? *p.s0 : 1.0f;
     const float sc1 = (DUAL && p.s1) ? *p.s1 : 1.0f;
+    const int64_t peer_off = p.peer_off + (p.epoch ? static_cast<int64_t>(*p.epoch & 1u) * p.par_bytes : 0);
     const int g = lane / LG, j = lane % LG;
     const int rg0 = (warp * GPW + g) * R2;              // first stage row of this lane group
 
@@ -434,7 +440,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
                             }
                             if (p.npeers > 0) {
                                 for (int q = 0; q < p.npeers; ++q) {
-                                    float *py = reinterpret_cast<float *>(p.peer_base[q] + p.peer_off);
+                                    float *py = reinterpret_cast<float *>(p.peer_base[q] + peer_off);
                                     py[tt * p.ldy + p.col_off + row] = v;
                                 }
                             } else {
@@ -461,23 +467,25 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
     }
 }
 
-// Tensor-parallel push: copy this rank's [T, cols] block (row stride ld, at
-// column col_off of the buffer at byte offset buf_off) from its own copy into
-// every other rank's copy, then count the CTA into every rank's flag[rank]
-// (same publication protocol as the matvec epilogue).
-__global__ void __launch_bounds__(256) k_tp_push(uint8_t *const *peer_base, int npeers, int rank, int64_t buf_off,
-                                                 int64_t ld, int64_t col_off, int T, int cols, int64_t flag_off) {
+// Tensor-parallel push: copy this rank's [T, cols] block (row stride ld) from
+// its local staging area (byte offset src_off of its own buffer) into its slot
+// of every rank's buffer, this rank's included (byte offset dst_off, plus
+// par_bytes when the step parity epoch[0] is odd), then count the CTA into
+// every rank's flag[rank] (same publication protocol as the matvec epilogue).
+__global__ void __launch_bounds__(256) k_tp_push(uint8_t *const *peer_base, int npeers, int rank, int64_t src_off,
+                                                 int64_t dst_off, int64_t par_bytes, const unsigned int *epoch,
+                                                 int64_t ld, int T, int cols, int64_t flag_off) {
     fr_pdl_wait();
-    const float *src = reinterpret_cast<const float *>(peer_base[rank] + buf_off);
+    const float *src = reinterpret_cast<const float *>(peer_base[rank] + src_off);
+    const int64_t off = dst_off + static_cast<int64_t>(*epoch & 1u) * par_bytes;
     const int64_t n = static_cast<int64_t>(T) * cols;
     const int64_t per = (n + gridDim.x - 1) / gridDim.x;
     const int64_t lo = blockIdx.x * per, hi = min(n, lo + per);
     for (int q = 0; q < npeers; ++q) {
-        if (q == rank) continue;
-        float *dst = reinterpret_cast<float *>(peer_base[q] + buf_off);
+        float *dst = reinterpret_cast<float *>(peer_base[q] + off);
         for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
             const int64_t t = i / cols, c = i % cols;
-            dst[t * ld + col_off + c] = src[t * ld + col_off + c];
+            dst[t * ld + c] = src[t * ld + c];
         }
     }
     __syncthreads();
@@ -497,20 +505,30 @@ __global__ void __launch_bounds__(256) k_tp_push(uint8_t *const *peer_base, int 
 // ranks' partial outputs in rank order (identical on every rank), adds the
 // residual and writes `out`.  The wait is bounded (status bit 0, site 30).
 //
-// The kernel releases its dependents at once and does not wait for the
-// previous kernel: it may poll while the producing matvec still runs -- all of
-// whose CTAs are resident by then, since a PDL dependent launches only after
-// every CTA of its primary has triggered -- and the kernel after it waits for
-// this one to complete.  The consumed counts are ordered between steps because
-// every later kernel of a step waits for its predecessor's completion.
+// Step parity (epoch non-null): the partial outputs are double-buffered.
+// epoch[blockIdx.x] counts this CTA's completed steps; a step reads the half
+// `parts + (epoch & 1) * par_floats` and then advances the count.  The
+// producers of the next step read epoch[0] to pick the other half, so a fast
+// rank's next partials never land in the half a slower rank is still summing:
+// a rank can only be one step ahead, because its step s+1 needs every rank's
+// step-s+1 partials, which each rank produces only after its own step-s
+// reduce completed.  (epoch null: a single buffer, wait only.)
+//
+// The kernel releases its dependents at once, then waits for its predecessor
+// in the stream to complete: the consumed counts and the step count it reads
+// are the previous step's final values, whatever the depth of the launch
+// chain ahead of it.
 __global__ void __launch_bounds__(256) k_tp_reduce(const unsigned int *flags, unsigned int *seen, int nranks,
                                                    unsigned int expect, const float *parts, int64_t n,
                                                    const float *resid, int64_t ldr, int64_t width, float *out,
-                                                   int64_t ldo) {
+                                                   int64_t ldo, unsigned int *epoch, int64_t par_floats) {
     fr_pdl_trigger();
+    fr_pdl_wait();
+    const unsigned int e = epoch ? epoch[blockIdx.x] : 0u;
     if (threadIdx.x < static_cast<unsigned>(nranks))
         tp_flag_wait(flags, seen + blockIdx.x * 32 + threadIdx.x, threadIdx.x, expect);
     __syncthreads();
+    parts += static_cast<int64_t>(e & 1u) * par_floats;
     const int64_t per = (n + gridDim.x - 1) / gridDim.x;
     const int64_t lo = blockIdx.x * per, hi = min(n, lo + per);
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
@@ -519,6 +537,10 @@ __global__ void __launch_bounds__(256) k_tp_reduce(const unsigned int *flags, un
         const int64_t t = i / width, c = i % width;
         if (resid) v += resid[t * ldr + c];
         out[t * ldo + c] = v;
+    }
+    if (epoch) {
+        __syncthreads();
+        if (threadIdx.x == 0) epoch[blockIdx.x] = e + 1u;
     }
 }
 

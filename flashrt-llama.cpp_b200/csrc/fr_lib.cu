@@ -35,6 +35,8 @@ struct TpOut {
     uint8_t *const *peer_base;
     int npeers, rank;
     int64_t peer_off, flag_off;
+    const unsigned int *epoch;   // step parity of the receiving slots
+    int64_t par_bytes;
     unsigned *ctas_out;
 };
 static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const float *x, int64_t ldx,
@@ -349,6 +351,17 @@ int fr_device_status(uint32_t *status, int clear) {
         if (e != cudaSuccess) return cuda_rc(e);
     }
     return FR_OK;
+}
+
+int64_t fr_set_wait_ns(int64_t ns) {
+    if (ns < 1000 || ns > static_cast<int64_t>(FR_WAIT_NS_MAX)) return FR_EINVAL;
+    unsigned long long prev = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&prev, g_fr_wait_ns, sizeof(prev));
+    if (e != cudaSuccess) return cuda_rc(e);
+    const unsigned long long v = static_cast<unsigned long long>(ns);
+    e = cudaMemcpyToSymbol(g_fr_wait_ns, &v, sizeof(v));
+    if (e != cudaSuccess) return cuda_rc(e);
+    return static_cast<int64_t>(prev);
 }
 
 int fr_fault_inject(const char *site) {
@@ -1310,6 +1323,8 @@ static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const
         a.rank = tp->rank;
         a.peer_off = tp->peer_off;
         a.flag_off = tp->flag_off;
+        a.epoch = tp->epoch;
+        a.par_bytes = tp->par_bytes;
         if (tp->ctas_out) *tp->ctas_out = static_cast<unsigned>(G) * static_cast<unsigned>((T + TW - 1) / TW);
     }
     const int nq = K / Q8_ELEMS;
@@ -1538,19 +1553,36 @@ int fr_moe_combine(const float *part, const float *wts, const float *resid, floa
 namespace frb {
 
 // shared buffer layout: [flags 32] u32, the reduce kernel's per-CTA consumed
-// counts [TP_WAIT_CTAS][32] u32, then (256-byte aligned) the ranks' partial
-// outputs [P][T][n_embd] f32 -- slot r written by rank r
+// counts [TP_WAIT_CTAS][32] u32 and step counts [TP_WAIT_CTAS] u32, then
+// (256-byte aligned) two parity halves of the ranks' partial outputs, each
+// [P][T][n_embd] f32 with slot r written by rank r, then this rank's local
+// staging rows [T][n_embd] f32 (the push path's matvec output).  The halves'
+// size follows from the buffer's size -- T_cap tokens, the T the buffer was
+// sized for -- so every call on one buffer agrees on where they lie whatever
+// its own T.
 constexpr int TP_WAIT_CTAS = 32;
 struct TpLayout {
-    int64_t flags, seen, part, total;
+    int64_t flags, seen, epoch, part, half, stage, total;
+    int64_t t_cap;
 };
-static TpLayout tp_layout(int T, int n_embd, int P) {
+static int64_t tp_part_off() { return (4LL * 32 + 4LL * 32 * TP_WAIT_CTAS + 4LL * TP_WAIT_CTAS + 255) / 256 * 256; }
+static TpLayout tp_layout_cap(int64_t t_cap, int n_embd, int P) {
     TpLayout l{};
     l.flags = 0;
     l.seen = 4LL * 32;
-    l.part = (l.seen + 4LL * 32 * TP_WAIT_CTAS + 255) / 256 * 256;
-    l.total = l.part + static_cast<int64_t>(P) * T * n_embd * 4;
+    l.epoch = l.seen + 4LL * 32 * TP_WAIT_CTAS;
+    l.part = tp_part_off();
+    l.t_cap = t_cap;
+    l.half = static_cast<int64_t>(P) * t_cap * n_embd * 4;
+    l.stage = l.part + 2 * l.half;
+    l.total = l.stage + t_cap * n_embd * 4;
     return l;
+}
+// the layout of a buffer of `bytes` bytes (t_cap = 0 when it holds no token)
+static TpLayout tp_layout_buf(int64_t bytes, int n_embd, int P) {
+    const int64_t per_tok = (2LL * P + 1) * n_embd * 4;
+    const int64_t t_cap = bytes > tp_part_off() ? (bytes - tp_part_off()) / per_tok : 0;
+    return tp_layout_cap(t_cap, n_embd, P);
 }
 
 // CTAs the matvec launches for (N, K, T) -- what each rank counts into the flags
@@ -2031,7 +2063,7 @@ static int ep_moe_impl(const float *x, const float *w_r, const void *wg_local, c
                     reinterpret_cast<unsigned int *>(base + L.seen_d), nranks, static_cast<unsigned>(EP_CTAS),
                     static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<const float *>(nullptr),
                     static_cast<int64_t>(0), static_cast<int64_t>(1), static_cast<float *>(nullptr),
-                    static_cast<int64_t>(0));
+                    static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr), static_cast<int64_t>(0));
     if (rc != FR_OK) return rc;
     // this rank's experts over everything it received (empty slots skipped)
     if (tiled)
@@ -2052,7 +2084,7 @@ static int ep_moe_impl(const float *x, const float *w_r, const void *wg_local, c
                     reinterpret_cast<unsigned int *>(base + L.seen_r), nranks, static_cast<unsigned>(EP_CTAS),
                     static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<const float *>(nullptr),
                     static_cast<int64_t>(0), static_cast<int64_t>(1), static_cast<float *>(nullptr),
-                    static_cast<int64_t>(0));
+                    static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr), static_cast<int64_t>(0));
     if (rc != FR_OK) return rc;
     return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream,
                       reinterpret_cast<const float *>(base + L.back), static_cast<const float *>(wts), resid, out,
@@ -2111,7 +2143,7 @@ int fr_ipc_free(void *dev_ptr) { return dev_ptr ? cuda_rc(cudaFree(dev_ptr)) : F
 
 int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks) {
     if (T <= 0 || n_embd <= 0 || n_ff <= 0 || nranks <= 0) return -1;
-    return tp_layout(T, n_embd, nranks).total;
+    return tp_layout_cap(T, n_embd, nranks).total;
 }
 
 } // extern "C"
@@ -2128,8 +2160,8 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
     // the n_ff shard boundary falls on NVFP4 block (64) boundaries, so the
     // GLU's q8_1 blocks and the down rows' NVFP4 blocks never straddle it
     if (n_embd % 64 != 0 || n_ff % (64 * nranks) != 0) return FR_EINVAL;
-    const TpLayout L = tp_layout(T, n_embd, nranks);
-    if (buffer_bytes < L.total) return FR_EINVAL;
+    const TpLayout L = tp_layout_buf(buffer_bytes, n_embd, nranks);
+    if (T > L.t_cap) return FR_EINVAL;
     uint8_t *base = static_cast<uint8_t *>(local_base);
     uint8_t *const *pb = reinterpret_cast<uint8_t *const *>(peer_base);
     const int F_p = n_ff / nranks;
@@ -2138,6 +2170,7 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
     const int64_t slot_off = L.part + static_cast<int64_t>(rank) * T * n_embd * 4;
     const unsigned int *flags = reinterpret_cast<const unsigned int *>(base + L.flags);
     unsigned int *seen = reinterpret_cast<unsigned int *>(base + L.seen);
+    unsigned int *epoch = reinterpret_cast<unsigned int *>(base + L.epoch);
     const float *parts = reinterpret_cast<const float *>(base + L.part);
     const int64_t n_out = static_cast<int64_t>(T) * n_embd;
     void *glu_p = nullptr;
@@ -2152,7 +2185,6 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
         // on ggml's layout it goes into this rank's own slot and a push
         // kernel stores it into every peer's slot
         constexpr int PUSH_CTAS = 64;
-        float *slot = reinterpret_cast<float *>(base + slot_off);
         if (tiled) {
             // the down matvec's epilogue stores its rows into every rank's
             // slot and counts each CTA into the flags: no push kernel
@@ -2164,9 +2196,10 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
                              static_cast<float *>(am));
             if (rc != FR_OK) return rc;
             unsigned ctas = 0;
-            const TpOut to{pb, nranks, rank, slot_off, L.flags, &ctas};
+            const TpOut to{pb, nranks, rank, slot_off, L.flags, epoch, L.half, &ctas};
             rc = fp4t_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, n_embd, F_p, glu, F_p, nullptr, 0, T,
-                             sd, nullptr, nullptr, 0, slot, n_embd, false, stream, nullptr,
+                             sd, nullptr, nullptr, 0, reinterpret_cast<float *>(base + L.stage), n_embd, false,
+                             stream, nullptr,
                              static_cast<const float *>(am), &to);
             if (rc != FR_OK) return rc;
             expect = ctas;
@@ -2174,11 +2207,16 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
             rc = tcx_matvec(static_cast<const uint8_t *>(wg_shard), static_cast<const uint8_t *>(wu_shard), ld_gu,
                             F_p, n_embd, x, n_embd, nullptr, 0, T, sg, su, nullptr, 0, glu, F_p, true, stream);
             if (rc != FR_OK) return rc;
+            // the down matvec writes this rank's partial rows into its local
+            // staging area; the push kernel stores them into this rank's slot
+            // of every rank (the step's parity half)
             rc = tcx_matvec(static_cast<const uint8_t *>(wd_shard), nullptr, ld_d, n_embd, F_p, glu, F_p, nullptr, 0,
-                            T, sd, nullptr, nullptr, 0, slot, n_embd, false, stream);
+                            T, sd, nullptr, nullptr, 0, reinterpret_cast<float *>(base + L.stage), n_embd, false,
+                            stream);
             if (rc != FR_OK) return rc;
-            rc = launch_pdl(k_tp_push, dim3(PUSH_CTAS), dim3(256), 0, stream, pb, nranks, rank, slot_off,
-                            static_cast<int64_t>(n_embd), static_cast<int64_t>(0), T, n_embd, L.flags);
+            rc = launch_pdl(k_tp_push, dim3(PUSH_CTAS), dim3(256), 0, stream, pb, nranks, rank, L.stage, slot_off,
+                            L.half, static_cast<const unsigned int *>(epoch), static_cast<int64_t>(n_embd), T, n_embd,
+                            L.flags);
             expect = PUSH_CTAS;
         }
         if (rc != FR_OK) return rc;
@@ -2225,6 +2263,8 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
         q.peer_off = slot_off;
         q.flag_off = L.flags;
         q.col_off = 0;
+        q.epoch = epoch;
+        q.par_bytes = L.half;
         rc = gemv_run(q, T, false, stream);
         if (rc != FR_OK) return rc;
         expect = gemv_ctas(n_embd, F_p, ld_d, T, false);
@@ -2233,12 +2273,29 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
     // Always TP_WAIT_CTAS CTAs: each keeps its own consumed count.
     return launch_pdl(k_tp_reduce, dim3(TP_WAIT_CTAS), dim3(256), 0, stream, flags, seen, nranks, expect, parts,
                       n_out, resid, static_cast<int64_t>(n_embd), static_cast<int64_t>(n_embd), out,
-                      static_cast<int64_t>(n_embd));
+                      static_cast<int64_t>(n_embd), epoch, L.half / 4);
 }
 
 } // namespace frb
 
 extern "C" {
+
+int fr_tp_wait(void *local_base, int64_t buffer_bytes, int n_embd, int nranks, unsigned expect,
+               cudaStream_t stream) {
+    if (fault_hit("fr_tp_wait")) return FR_EINJECTED;
+    if (!local_base || n_embd <= 0 || nranks <= 0 || nranks > 32) return FR_EINVAL;
+    const TpLayout L = tp_layout_buf(buffer_bytes, n_embd, nranks);
+    if (L.t_cap <= 0) return FR_EINVAL;
+    uint8_t *base = static_cast<uint8_t *>(local_base);
+    // every consumed-count row advances, as in a step's reduce; nothing is summed
+    return launch_pdl(k_tp_reduce, dim3(TP_WAIT_CTAS), dim3(256), 0, stream,
+                      reinterpret_cast<const unsigned int *>(base + L.flags),
+                      reinterpret_cast<unsigned int *>(base + L.seen), nranks, expect,
+                      static_cast<const float *>(nullptr), static_cast<int64_t>(0),
+                      static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<int64_t>(1),
+                      static_cast<float *>(nullptr), static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr),
+                      static_cast<int64_t>(0));
+}
 
 int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard, const float *sg,
                     const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,

@@ -44,6 +44,7 @@ SIGNATURES = {
     "fr_strerror": (C.c_char_p, [_i32]),
     "fr_device_status": (_i32, [C.POINTER(C.c_uint32), _i32]),
     "fr_fault_inject": (_i32, [C.c_char_p]),
+    "fr_set_wait_ns": (_i64, [_i64]),
     "fr_kernel_launches": (C.c_uint64, []),
     "fr_set_matvec_path": (_i32, [_i32]),
     "fr_nvfp4_row_bytes": (_i64, [_i64]),
@@ -65,6 +66,7 @@ SIGNATURES = {
     "fr_moe_ffn_tiled": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
                                 C.c_float, _vp, _vp, _vp, _vp, _vp]),
     "fr_tp_buffer_bytes": (_i64, [_i32, _i32, _i32, _i32]),
+    "fr_tp_wait": (_i32, [_vp, _i64, _i32, _i32, C.c_uint32, _vp]),
     "fr_tp_ffn_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                _i64, _vp]),
     "fr_tp_ffn_tiled": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp,

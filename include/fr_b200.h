@@ -49,6 +49,12 @@ const char *fr_strerror(int rc);
  * word of the current device.  Synchronises the device. */
 int fr_device_status(uint32_t *status, int clear);
 
+/* Limit of every bounded device-side wait, in nanoseconds (default and
+ * maximum 2 s, minimum 1 us).  A wait that runs out sets status bit 0 with its
+ * site and lets its kernel return.  Applies to the current device, from the
+ * next launch on.  Returns the previous limit, or a negative code. */
+int64_t fr_set_wait_ns(int64_t ns);
+
 /* Host-side fault injection (test aid): the next call of the entry point
  * whose name equals `site` returns FR_EINJECTED before launching anything.
  * NULL clears.  Also read once from the environment variable FR_FAULT. */
@@ -279,6 +285,18 @@ int fr_moe_ffn_tiled(const float *x, const float *w_r, const void *wg_t, const v
  * first use; local_base is this rank's own base.  All ranks call with the
  * same T.  The reference is single-device; no counterpart. */
 int64_t fr_tp_buffer_bytes(int T, int n_embd, int n_ff, int nranks);
+/* The partial outputs are double-buffered by step parity inside the buffer (a
+ * device-side step count picks the half), so a rank that runs a step ahead
+ * never overwrites partials a slower rank is still summing; consecutive steps
+ * need no host synchronisation.  The buffer's size fixes its token capacity
+ * (the T given to fr_tp_buffer_bytes): every call on it passes the same
+ * buffer_bytes and T up to that capacity.
+ * fr_tp_wait: the step's completion wait alone (nothing summed): returns once
+ * each of the nranks flag counters of this rank's buffer grew by `expect`
+ * publications since the last wait, or when the wait limit runs out (status
+ * bit 0, site 30).  For failure handling and tests; a step already waits. */
+int fr_tp_wait(void *local_base, int64_t buffer_bytes, int n_embd, int nranks, unsigned expect,
+               cudaStream_t stream);
 /* fr_tp_ffn_nvfp4 on tile-major shards (fr_nvfp4_tile of the gate/up row
  * shards [F_p, n_embd] and of the down K-shard [n_embd, F_p]);
  * n_ff % (256 * nranks) == 0 and n_embd % 256 == 0. */

@@ -105,6 +105,27 @@ def _worker(rank, world, port, q):
             check(yg, frb200.ffn(xi, wg, wu, wd, ne, nf), f"graph replay {i}", False)
         del g
         torch.cuda.synchronize()
+        # consecutive steps on one stream with no host synchronisation between
+        # them, the last rank delayed before every other step so that the
+        # others run a step ahead: each step's partial rows must land in the
+        # other parity half of the shared buffer, never in the half a slower
+        # rank is still summing
+        xs = [t(frb200.synth_normal(200 + i, 4 * ne).reshape(4, ne)) for i in range(8)]
+        for name, fn, tc in (("dp4a", lambda x, o: tps[0](x, *shards, out=o, stream=s), False),
+                             ("tiled", lambda x, o: tpt(x, *tshards, out=o, stream=s, tiled=True), True)):
+            frb200.set_matvec_path(1 if name == "dp4a" else 0)
+            ys = [torch.empty((4, ne), dtype=torch.float32, device=dev) for _ in xs]
+            torch.cuda.synchronize()
+            dist.barrier()
+            with torch.cuda.stream(s):
+                for i, (x, o) in enumerate(zip(xs, ys)):
+                    if rank == world - 1 and i % 2 == 1:
+                        torch.cuda._sleep(2_000_000)
+                    fn(x, o)
+            s.synchronize()
+            for i, (x, o) in enumerate(zip(xs, ys)):
+                check(o, frb200.ffn(x, wg, wu, wd, ne, nf), f"chained {name} step {i}", tc)
+        frb200.set_matvec_path(0)
         q.put((rank, bad, frb200.device_status(), sums))
     except Exception as e:  # noqa: BLE001 - report to the parent instead of hanging it
         q.put((rank, bad + [repr(e)], -1, sums))

@@ -5,8 +5,12 @@ capture, hosts (such as ggml) whose allocator plans all device buffers up
 front, processes with a fixed device-memory budget -- and keeps its
 intermediates in a static device array instead of a grown workspace.  This
 test calls it through the C-ABI twice in a row, with different inputs, and
-checks each result against the regular entry point fr_ffn_nvfp4 within the
-tolerance the parity tests use (max rel err 1e-3).  It also checks the size
+checks each result against the regular entry point fr_ffn_nvfp4 and against
+the CPU oracle's restatement of the same FFN (q8_1 of x, SwiGLU of the
+gate/up dot products, q8_1 of the GLU, down dot products, residual), within
+the tolerance the parity tests use (max rel err 1e-3).  The allocation-free
+entry always runs the dp4a matvec, whatever the matvec-path setting, so it
+can differ from fr_ffn_nvfp4 within that tolerance.  It also checks the size
 limit.  The file is named so that pytest collects it last.
 """
 import ctypes as C
@@ -36,15 +40,23 @@ def _noalloc(fr, x, wg, wu, wd, n_embd, n_ff, out, resid=None):
                                          fr._ptr(resid), fr._ptr(out), x.shape[0], n_embd, n_ff, fr._stream())
 
 
-def test_noalloc_ffn_matches_regular_entry_twice(fr, dev):
+def _oracle_ffn(O, x, wg, wu, wd, n_embd, n_ff, r):
+    qx = O.quantize_q8_1(x)
+    g = O.gemv_q8_1(wg, qx, n_ff, n_embd)
+    u = O.gemv_q8_1(wu, qx, n_ff, n_embd)
+    glu = (u * (g / (1.0 + np.exp(-g)))).astype(np.float32)
+    return O.gemv_q8_1(wd, O.quantize_q8_1(glu), n_embd, n_ff) + r.astype(np.float64)
+
+
+def test_noalloc_ffn_matches_regular_entry_twice(fr, dev, O):
     import torch
     n_embd, n_ff, T = 1024, 2816, 4
-    wg = _t(fr.synth_nvfp4(901, n_ff, n_embd), dev)
-    wu = _t(fr.synth_nvfp4(902, n_ff, n_embd), dev)
-    wd = _t(fr.synth_nvfp4(903, n_embd, n_ff), dev)
+    hw = [fr.synth_nvfp4(901, n_ff, n_embd), fr.synth_nvfp4(902, n_ff, n_embd), fr.synth_nvfp4(903, n_embd, n_ff)]
+    wg, wu, wd = (_t(w, dev) for w in hw)
     for call, seed in enumerate((904, 905)):
-        x = _t(fr.synth_normal(seed, T * n_embd).reshape(T, n_embd), dev)
-        r = _t(fr.synth_normal(seed + 10, T * n_embd).reshape(T, n_embd), dev)
+        hx = fr.synth_normal(seed, T * n_embd).reshape(T, n_embd)
+        hr = fr.synth_normal(seed + 10, T * n_embd).reshape(T, n_embd)
+        x, r = _t(hx, dev), _t(hr, dev)
         out = torch.full((T, n_embd), float("nan"), dtype=torch.float32, device=dev)
         rc = _noalloc(fr, x, wg, wu, wd, n_embd, n_ff, out, resid=r)
         assert rc == 0, f"call {call}: rc={rc}"
@@ -53,6 +65,7 @@ def test_noalloc_ffn_matches_regular_entry_twice(fr, dev):
         mine = out.cpu().numpy()
         assert np.all(np.isfinite(mine)), f"call {call}"
         assert _rel(mine, ref.cpu().numpy()) <= RTOL, f"call {call}"
+        assert O.rel_err(mine, _oracle_ffn(O, hx, *hw, n_embd, n_ff, hr)) <= RTOL, f"call {call} vs oracle"
     assert fr.device_status() == 0
 
 
