@@ -33,10 +33,14 @@ METRIC = "NVFP4 GEMV GB/s vs HBM peak; MoE decode tok/s at batch 1/64, 1–8 B20
 N_EMBD, N_FF = 4096, 14336
 N_SETS = 4
 HBM_FALLBACK = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the gate/up SwiGLU
-# FP4 tensor-core matvec on tile-major weights (T=1), from the ncu capture
-# summarised in profiles/k_fp4t_gateup_T1.md
-TRAFFIC_GATEUP = 66.17e6
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the gate/up
+# SwiGLU FP4 tensor-core matvec on tile-major weights at T=1 (k_fp4t<16,1,1>):
+# 66,132,992 + 326,912 bytes, as `ncu --metrics dram__bytes_read.sum,
+# dram__bytes_write.sum,gpu__time_duration.sum --clock-control none -k
+# regex:k_fp4t -s 8 -c 2 python bench.py --profile-case --layout tiled
+# --tokens 1 --steps 8` reports it (step 5 of 8: the four weight sets rotate,
+# so its weights come from HBM)
+TRAFFIC_GATEUP = 66459904
 
 
 def _peaks():
@@ -113,20 +117,37 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- reference arm
 
+def _host_nvfp4(seed: int, rows: int, K: int):
+    """NVFP4 blocks with BASELINE's distribution generated on the host without
+    the product library (numpy RNG; scales e4m3(|N(0,1)| * 0.05), RNE through
+    torch's float8_e4m3fn): E2M1 codes uniform over all 16 values."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(seed)
+    nb = rows * (K // 64)
+    blk = np.empty((nb, 36), np.uint8)
+    blk[:, 4:] = rng.integers(0, 256, size=(nb, 32), dtype=np.uint8)
+    sc = np.abs(rng.standard_normal((nb, 4))) * 0.05
+    blk[:, :4] = torch.from_numpy(sc.astype(np.float32)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    return blk.reshape(rows, K // 64 * 36)
+
+
 def cpu_reference_line(args, T: int = 1, budget_s: float = 12.0):
     """Time the CPU restatement of the FFN matvecs (oracle/, fp32 accumulation
-    with int32 sub-block sums, all host threads) on a bounded sample."""
+    with int32 sub-block sums, all host threads) on a bounded sample.  Its
+    inputs are generated on the host (numpy), so this leg loads nothing of the
+    product."""
     import numpy as np
-    import frb200
     from oracle import oracle as O
 
     ncores = os.cpu_count() or 1
     # sample: one FFN layer's three matrices, rows subsampled to bound the time
     rows = 2048
-    wg = frb200.synth_nvfp4(0x5EED0000 + 1, rows, N_EMBD)
-    wd = frb200.synth_nvfp4(0x5EED0000 + 3, rows, N_FF)
-    x = frb200.synth_normal(0x5EED0000 + 10, T * N_EMBD).reshape(T, N_EMBD)
-    g = frb200.synth_normal(0x5EED0000 + 11, T * N_FF).reshape(T, N_FF)
+    rng = np.random.default_rng(0x5EED0000 + 10)
+    wg = _host_nvfp4(0x5EED0000 + 1, rows, N_EMBD)
+    wd = _host_nvfp4(0x5EED0000 + 3, rows, N_FF)
+    x = rng.standard_normal((T, N_EMBD)).astype(np.float32)
+    g = rng.standard_normal((T, N_FF)).astype(np.float32)
     qx = O.quantize_q8_1(x)
     qg = O.quantize_q8_1(g)
     O.gemv_q8_1_f32(wg, qx, rows, N_EMBD, nthreads=ncores)          # warm-up
@@ -183,6 +204,102 @@ def _moe_sets(frb200, torch, dev, rank, world, n_sets):
         wd = torch.from_numpy(frb200.synth_nvfp4(base + 3, E * ne, nf)[rank * Ep * ne:(rank + 1) * Ep * ne]).to(dev)
         sets.append((wr, wg, wu, wd))
     return sets
+
+
+GEMV0_N = GEMV0_K = 4096
+GEMV0_COPIES = 32
+
+
+def gemv0_bytes() -> int:
+    return GEMV0_N * (GEMV0_K // 64 * 36) + GEMV0_K * 4 + GEMV0_N * 4
+
+
+def _gemv_config0(frb200, torch, dev, stream, time_fn, graphs_for, hbm, args):
+    """y = W . q8_1(x), W 4096x4096 NVFP4, x 1x4096 f32 -- through
+    fr_mul_mat_nvfp4 on ggml's layout, and through fr_gemv_tiled on the
+    tile-major copy (same bytes).  Each timed launch reads a different weight
+    copy (32 copies, 302 MB > 2x L2), all captured in one CUDA graph."""
+    ws = [torch.from_numpy(frb200.synth_nvfp4(0x5EED0100 + c, GEMV0_N, GEMV0_K)).to(dev) for c in range(GEMV0_COPIES)]
+    wts = [frb200.tile_nvfp4(w, GEMV0_N, GEMV0_K) for w in ws]
+    x = torch.from_numpy(frb200.synth_normal(0x5EED0110, GEMV0_K).reshape(1, GEMV0_K)).to(dev)
+    y = torch.empty((1, GEMV0_N), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    res = {}
+    for name, call in (("ggml layout, fr_mul_mat_nvfp4",
+                        lambda i: frb200.mul_mat(ws[i], x, GEMV0_N, GEMV0_K, out=y, stream=stream)),
+                       ("tile-major layout, fr_gemv_tiled",
+                        lambda i: frb200.gemv_tiled(wts[i], GEMV0_N, GEMV0_K, x=x, out=y, stream=stream))):
+        with torch.cuda.stream(stream):
+            for i in range(GEMV0_COPIES):
+                call(i)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(GEMV0_COPIES):
+                call(i)
+        ms = time_fn(lambda i: g.replay(), max(10, args.steps // 4), 3) / GEMV0_COPIES
+        del g
+        res[name] = ms
+    best = min(res, key=res.get)
+    us = res[best] * 1e3
+    gbs = gemv0_bytes() / (us * 1e-6) / 1e9
+    out = {"gemv_4096_us": round(us, 3), "gemv_4096_gbs": round(gbs, 1), "gemv_4096_frac_hbm": round(gbs / hbm, 4),
+           "gemv_4096_path": best, "gemv_4096_target_us_at_0.8": round(gemv0_bytes() / (0.8 * hbm * 1e9) * 1e6, 3)}
+    for name, ms in res.items():
+        out[f"gemv_4096_us[{name}]"] = round(ms * 1e3, 3)
+    del ws, wts
+    return out
+
+
+FP4_DENSE_NOMINAL_TFLOPS = 9000.0
+
+
+def _prefill_config3(frb200, torch, dev, stream, time_fn, graphs_for, hbm, args):
+    """a 512-token ubatch (and 4 x 512 = 2048 rows) x the NVFP4
+    weights 14336x4096 and 4096x14336 through the reference's W4A4 launch
+    interface: fr_quantize_act_f32 (f32 -> NVFP4 + scale atoms) then
+    fr_gemm_f32out (tcgen05 kind::mxf4nvf4, f32 out).  Weights repacked once
+    (fr_repack_weight), 6 sets rotating (> L2)."""
+    out = {}
+    n_sets = 6
+    for (M, N, K) in ((512, 14336, 4096), (512, 4096, 14336), (2048, 4096, 14336)):
+        Bs = []
+        for s_ in range(n_sets):
+            w = torch.from_numpy(frb200.synth_nvfp4(0x5EED0200 + 7 * s_ + N, N, K)).to(dev)
+            Bs.append(frb200.repack_weight(w, N, K))
+            del w
+        x = torch.from_numpy(frb200.synth_normal(0x5EED0210 + K, M * K).reshape(M, K)).to(dev)
+        A = torch.empty((M, K // 2), dtype=torch.uint8, device=dev)
+        SFA = torch.zeros(frb200.sf_bytes(M, K), dtype=torch.uint8, device=dev)
+        D = torch.empty((M, N), dtype=torch.float32, device=dev)
+
+        def step(i, gemm_only=False):
+            if not gemm_only:
+                frb200.call("fr_quantize_act_f32", frb200._ptr(x), frb200._ptr(A), frb200._ptr(SFA), M, K,
+                            frb200._stream(stream))
+            B, SFB = Bs[i % n_sets]
+            frb200.gemm_f32out(A, SFA, B, SFB, M, N, K, out=D, stream=stream)
+
+        gs = graphs_for(step)
+        ms = time_fn(lambda i: gs[i % 4].replay(), max(10, args.steps // 4), 3)
+        gg = graphs_for(lambda i: step(i, True))
+        ms_g = time_fn(lambda i: gg[i % 4].replay(), max(10, args.steps // 4), 3)
+        del gs, gg
+        flop = 2.0 * M * N * K
+        tf = flop / (ms_g * 1e-3) / 1e12
+        byts = N * K // 2 + frb200.sf_bytes(N, K) + M * K // 2 + frb200.sf_bytes(M, K) + 4 * M * N
+        attain = min(FP4_DENSE_NOMINAL_TFLOPS, flop / byts * hbm / 1e3)
+        key = f"prefill_{M}x{N}x{K}"
+        out[f"{key}_gemm_us"] = round(ms_g * 1e3, 2)
+        out[f"{key}_gemm_tflops"] = round(tf, 1)
+        out[f"{key}_frac_fp4_nominal"] = round(tf / FP4_DENSE_NOMINAL_TFLOPS, 4)
+        out[f"{key}_frac_attainable"] = round(tf / attain, 4)
+        out[f"{key}_quant_plus_gemm_us"] = round(ms * 1e3, 2)
+        del Bs, x, A, SFA, D
+    out["prefill_note"] = ("TFLOP/s of fr_gemm_f32out alone (2MNK); frac_fp4_nominal against the 9 PFLOP/s dense FP4 "
+                           "figure (nominal, no measured FP4 peak); frac_attainable against min(FP4 nominal, "
+                           "FLOP/byte x measured HBM), bytes = packed A/B + scale atoms + f32 D")
+    return out
 
 
 def run_ours(args):
@@ -388,6 +505,13 @@ def run_ours(args):
     egs = graphs_for(e2e_step)
     ec = chain_for(e2e_step)
     e_ms = time_steps(ec, egs, args.steps, max(args.warmup, 3))
+
+    # ---------------- one 4096x4096 NVFP4 x q8_1 matvec through the
+    # ggml_mul_mat op surface (f32 activation quantized to q8_1 in the call),
+    # rotating 32 weight copies (302 MB > 2x L2) captured as one graph
+    if world == 1:
+        extra.update(_gemv_config0(frb200, torch, dev, stream, time_fn, graphs_for, hbm, args))
+        extra.update(_prefill_config3(frb200, torch, dev, stream, time_fn, graphs_for, hbm, args))
 
     # ---------------- MoE layer (config 3): fused on one GPU, expert-parallel over ranks
     msets = _moe_sets(frb200, torch, dev, rank, world, 2)

@@ -128,3 +128,44 @@ def test_gemm_matches_reference_cutlass(R, fr, O, dev, M, N, K):
     assert err <= RTOL, f"M={M} N={N} K={K}: max rel err {err:.3e} against the reference GEMM"
     assert O.norm_err(mine, ref) <= NTOL
     assert fr.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 14336, 4096), (512, 4096, 14336), (2048, 4096, 14336)])
+def test_gemm_time_beside_reference(R, fr, dev, M, N, K, capsys):
+    """Device time of fr_gemm_f32out and of the reference's CUTLASS GEMM on the
+    same operands (CUDA events, 20 launches after 5 warm-up ones, weights
+    rotating over 4 copies).  Reported, not asserted: the figures go into the
+    performance notes."""
+    import torch
+    x = fr.synth_normal(0x5EED4400 + M, M * K).reshape(M, K)
+    A, SFA = fr.quantize_act_f32(_t(x, dev))
+    Bs = [fr.repack_weight(_t(fr.synth_nvfp4(0x5EED4500 + c + N, N, K), dev), N, K) for c in range(4)]
+    D = torch.empty((M, N), dtype=torch.float32, device=dev)
+    s = torch.cuda.current_stream()
+
+    def ours(i):
+        B, SFB = Bs[i % 4]
+        fr.gemm_f32out(A, SFA, B, SFB, M, N, K, out=D)
+
+    def ref(i):
+        B, SFB = Bs[i % 4]
+        assert R.frref_gemm_f32out(fr._ptr(A), fr._ptr(SFA), fr._ptr(B), fr._ptr(SFB), fr._ptr(D), M, N, K, 1.0, 0,
+                                   fr._stream()) == 0
+
+    res = {}
+    for name, fn in (("ours", ours), ("reference", ref)):
+        for i in range(5):
+            fn(i)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for i in range(20):
+            fn(i)
+        e1.record(s)
+        e1.synchronize()
+        res[name] = e0.elapsed_time(e1) / 20 * 1e3
+    tf = {k: 2.0 * M * N * K / (v * 1e-6) / 1e12 for k, v in res.items()}
+    with capsys.disabled():
+        print(f"\n[gemm timing] M={M} N={N} K={K}: ours {res['ours']:.1f} us ({tf['ours']:.0f} TFLOP/s), "
+              f"reference CUTLASS {res['reference']:.1f} us ({tf['reference']:.0f} TFLOP/s)")
+    assert fr.device_status() == 0

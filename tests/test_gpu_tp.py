@@ -3,8 +3,11 @@ the down matvec's epilogue (fr_tp_ffn_nvfp4, frb200.parallel.TpFfn).  Every
 rank must produce the same output, and it must match the single-GPU FFN on
 the unsharded weights: the GLU bit for bit (the same dot products; q8_1 blocks
 never straddle a shard), the output up to the f32 rounding of summing the
-ranks' K-range partials (max |d| <= 1e-5 * max|ref| on the dp4a matvec;
-normwise 1e-4 on the tensor-core matvec, whose split-K order differs too).
+ranks' K-range partials (max |d| <= 1e-5 * max|ref| on the dp4a matvec; on
+the tensor-core matvecs, whose split-K order differs too, the matvec
+tolerance max |d| / max(|ref|, 1% rms) <= 1e-3).  Consecutive steps run with
+no host synchronisation, one rank delayed, to show the double-buffered
+partial slots.
 Runs one rank per visible GPU, at most 2 (world 1 on a one-GPU box exercises
 the same peer-store, flag and reduce code with one peer), including CUDA-graph
 replays with new inputs."""
@@ -58,9 +61,15 @@ def _worker(rank, world, port, q):
             if not bool(torch.isfinite(y).all()):
                 bad.append(f"{what}: non-finite")
             elif tc:
-                nerr = float((y - ref).double().norm() / ref.double().norm())
-                if nerr > 1e-4:
-                    bad.append(f"{what}: norm err {nerr:.3e}")
+                # the tensor-core paths sum K in another order, so a GLU value
+                # can round to the other side of a q8_1 step: one such flip
+                # moves an output by ~3e-4 of its rms -- within the matvec
+                # tolerance (max |d| / max(|ref|, 1% rms) <= 1e-3)
+                d, r = (y - ref).double().abs(), ref.double()
+                floor = 1e-2 * float(r.pow(2).mean().sqrt())
+                err = float((d / r.abs().clamp_min(floor)).max())
+                if err > 1e-3:
+                    bad.append(f"{what}: max rel err {err:.3e}")
             else:
                 err = float((y - ref).abs().max() / ref.abs().max())
                 if err > 1e-5:
@@ -110,11 +119,18 @@ def _worker(rank, world, port, q):
         # others run a step ahead: each step's partial rows must land in the
         # other parity half of the shared buffer, never in the half a slower
         # rank is still summing
+        # (the kernels are deterministic, so each chained step must equal the
+        # same step run with the host synchronised after it, bit for bit)
         xs = [t(frb200.synth_normal(200 + i, 4 * ne).reshape(4, ne)) for i in range(8)]
-        for name, fn, tc in (("dp4a", lambda x, o: tps[0](x, *shards, out=o, stream=s), False),
-                             ("tiled", lambda x, o: tpt(x, *tshards, out=o, stream=s, tiled=True), True)):
+        for name, fn in (("dp4a", lambda x, o: tps[0](x, *shards, out=o, stream=s)),
+                         ("tiled", lambda x, o: tpt(x, *tshards, out=o, stream=s, tiled=True))):
             frb200.set_matvec_path(1 if name == "dp4a" else 0)
             ys = [torch.empty((4, ne), dtype=torch.float32, device=dev) for _ in xs]
+            yr = [torch.empty((4, ne), dtype=torch.float32, device=dev) for _ in xs]
+            with torch.cuda.stream(s):
+                for x, o in zip(xs, yr):
+                    fn(x, o)
+                    s.synchronize()
             torch.cuda.synchronize()
             dist.barrier()
             with torch.cuda.stream(s):
@@ -123,8 +139,11 @@ def _worker(rank, world, port, q):
                         torch.cuda._sleep(2_000_000)
                     fn(x, o)
             s.synchronize()
-            for i, (x, o) in enumerate(zip(xs, ys)):
-                check(o, frb200.ffn(x, wg, wu, wd, ne, nf), f"chained {name} step {i}", tc)
+            for i in range(len(xs)):
+                sums.append(float(ys[i].double().sum()))
+                if not torch.equal(ys[i], yr[i]):
+                    bad.append(f"chained {name} step {i}: differs from the synchronised step by "
+                               f"{float((ys[i] - yr[i]).abs().max()):.3e}")
         frb200.set_matvec_path(0)
         q.put((rank, bad, frb200.device_status(), sums))
     except Exception as e:  # noqa: BLE001 - report to the parent instead of hanging it
