@@ -610,6 +610,24 @@ def run_profile_case(args):
     torch.cuda.set_device(dev)
     if args.matvec is not None:
         frb200.set_matvec_path(args.matvec)
+    if args.case == "gemm":
+        # the prefill GEMM: M = --tokens rows against the
+        # 14336x4096 and 4096x14336 weights, alternating
+        M = args.tokens
+        ops = []
+        for (N, K) in ((14336, 4096), (4096, 14336)):
+            w = torch.from_numpy(frb200.synth_nvfp4(0x5EED0200 + N, N, K)).to(dev)
+            B, SFB = frb200.repack_weight(w, N, K)
+            x = torch.from_numpy(frb200.synth_normal(0x5EED0210 + K, M * K).reshape(M, K)).to(dev)
+            A, SFA = frb200.quantize_act_f32(x)
+            D = torch.empty((M, N), dtype=torch.float32, device=dev)
+            ops.append((A, SFA, B, SFB, D, N, K))
+        for i in range(args.steps):
+            A, SFA, B, SFB, D, N, K = ops[i % 2]
+            frb200.gemm_f32out(A, SFA, B, SFB, M, N, K, out=D)
+            torch.cuda.synchronize()
+        print(f"profile case done: {args.steps} GEMMs, M={M}, status {frb200.device_status()}")
+        return
     if args.case == "moe":
         msets = _moe_sets(frb200, torch, dev, 0, 1, 2)
         if args.layout == "tiled":
@@ -659,7 +677,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step of --profile-case")
     ap.add_argument("--matvec", type=int, default=None, help="force the matvec kernel (1 dp4a, 2 tc-f16, 3 tc-fp4)")
     ap.add_argument("--layout", choices=["ggml", "tiled"], default="ggml", help="weight layout of --profile-case")
-    ap.add_argument("--case", choices=["ffn", "moe"], default="ffn", help="workload of --profile-case")
+    ap.add_argument("--case", choices=["ffn", "moe", "gemm"], default="ffn", help="workload of --profile-case")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)

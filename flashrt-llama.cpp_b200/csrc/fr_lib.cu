@@ -11,6 +11,7 @@
 #include "fr_gemv.cuh"
 #include "fr_moe.cuh"
 #include "fr_w4a4.cuh"
+#include "fr_gemm.cuh"
 #include "fr_tcgemv.cuh"
 #include "fr_fp4mv.cuh"
 #include "fr_fp4tile.cuh"
@@ -975,18 +976,72 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// [rows, row_bytes] uint8 matrix, box 128 rows x 128 bytes, 128-byte swizzle
-static int make_map_sw128(CUtensorMap *map, const void *base, int64_t rows, int64_t row_bytes) {
+// [rows, row_bytes] uint8 matrix, box `box_rows` rows x 128 bytes, 128-byte swizzle
+static int make_map_sw128(CUtensorMap *map, const void *base, int64_t rows, int64_t row_bytes,
+                          uint32_t box_rows = 128) {
     auto enc = tensor_map_encoder();
     if (!enc) return FR_ENODEVICE;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-    cuuint32_t box[2] = {128, 128};
+    cuuint32_t box[2] = {128, box_rows};
     cuuint32_t es[2] = {1, 1};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
+}
+
+// The persistent stream-K GEMM (fr_gemm.cuh): grid = one CTA per SM (or one
+// per unit when there are fewer), the partial slots [grid][2][128 x 256] f32
+// and the per-tile arrival counters in grow-only workspaces.
+static int gemm_p_run(int epi, const void *A_packed, const void *SFA, const void *B_packed, const void *SFB, float *D,
+                      int M, int N, int K, float alpha, cudaStream_t stream) {
+    if (!A_packed || !SFA || !B_packed || !SFB || !D || M <= 0 || N <= 0 || K <= 0) return FR_EINVAL;
+    if (K % 64 != 0 || N % 16 != 0) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(D) & 15) || (reinterpret_cast<uintptr_t>(A_packed) & 15) ||
+        (reinterpret_cast<uintptr_t>(B_packed) & 15) || (reinterpret_cast<uintptr_t>(SFA) & 15) ||
+        (reinterpret_cast<uintptr_t>(SFB) & 15))
+        return FR_EINVAL;
+    const DevInfo &di = dev_info();
+    if (di.cc_major != 10) return FR_ENODEVICE;
+    PGemmArgs g{};
+    g.sfa = static_cast<const uint8_t *>(SFA);
+    g.sfb = static_cast<const uint8_t *>(SFB);
+    g.D = D;
+    g.ldd = epi == P_SWIGLU ? N / 2 : N;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.nkt = (K + P_BK - 1) / P_BK;
+    g.n_m = (M + P_BM - 1) / P_BM;
+    g.n_n = (N + P_BN - 1) / P_BN;
+    const int64_t tiles = static_cast<int64_t>(g.n_m) * g.n_n;
+    if (tiles > (1 << 24)) return FR_EINVAL;
+    g.units = tiles * g.nkt;
+    g.alpha = alpha;
+    const int grid = static_cast<int>(std::min<int64_t>(di.sms, g.units));
+    void *part = nullptr, *cnt = nullptr;
+    int rc = workspace_get(WS_GPART, static_cast<size_t>(grid) * 2 * P_SLOT_FLOATS * sizeof(float), stream, &part);
+    if (rc != FR_OK) return rc;
+    rc = workspace_get_zeroed(WS_GCNT, static_cast<size_t>(tiles) * sizeof(unsigned int), stream, &cnt);
+    if (rc != FR_OK) return rc;
+    g.part = static_cast<float *>(part);
+    g.counter = static_cast<unsigned int *>(cnt);
+    CUtensorMap ma, mb;
+    rc = make_map_sw128(&ma, A_packed, M, K / 2, P_BM);
+    if (rc != FR_OK) return rc;
+    rc = make_map_sw128(&mb, B_packed, N, K / 2, P_BN);
+    if (rc != FR_OK) return rc;
+    if (epi == P_SWIGLU) {
+        static bool done[64] = {};
+        rc = allow_max_smem(k_gemm_p<P_SWIGLU>, done);
+        if (rc != FR_OK) return rc;
+        return launch_pdl(k_gemm_p<P_SWIGLU>, dim3(grid), dim3(P_THREADS), P_SMEM, stream, ma, mb, g);
+    }
+    static bool done[64] = {};
+    rc = allow_max_smem(k_gemm_p<P_PLAIN>, done);
+    if (rc != FR_OK) return rc;
+    return launch_pdl(k_gemm_p<P_PLAIN>, dim3(grid), dim3(P_THREADS), P_SMEM, stream, ma, mb, g);
 }
 
 } // namespace frb
@@ -1015,30 +1070,38 @@ int fr_repack_weight(const void *ggml_blocks, void *dst_packed, void *dst_sf, in
     const int K16 = K / 16;
     return launch_pdl(k_repack, dim3((K16 + 127) / 128, N), dim3(128), 0, stream,
                       static_cast<const uint8_t *>(ggml_blocks), static_cast<uint2 *>(dst_packed),
-                      static_cast<uint8_t *>(dst_sf), N, K);
+                      static_cast<uint8_t *>(dst_sf), N, K, 1, 0);
 }
 
 int fr_gemm_f32out(const void *A_packed, const void *SFA, const void *B_packed, const void *SFB, float *D, int M,
                    int N, int K, float alpha, bool widen, cudaStream_t stream) {
     (void) widen;   // the reference ignores it too (src/fr_gemm_f32out.cu:196-197)
     if (fault_hit("fr_gemm_f32out")) return FR_EINJECTED;
-    if (!A_packed || !SFA || !B_packed || !SFB || !D || M <= 0 || N <= 0 || K <= 0) return FR_EINVAL;
-    if (K % 64 != 0 || N % 16 != 0) return FR_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(D) & 15) || (reinterpret_cast<uintptr_t>(A_packed) & 15) ||
-        (reinterpret_cast<uintptr_t>(B_packed) & 15) || (reinterpret_cast<uintptr_t>(SFA) & 15) ||
-        (reinterpret_cast<uintptr_t>(SFB) & 15))
-        return FR_EINVAL;
-    CUtensorMap ma, mb;
-    int rc = make_map_sw128(&ma, A_packed, M, K / 2);
+    return gemm_p_run(P_PLAIN, A_packed, SFA, B_packed, SFB, D, M, N, K, alpha, stream);
+}
+
+int fr_gemm_swiglu_f32out(const void *A_packed, const void *SFA, const void *B_pair, const void *SFB_pair, float *D,
+                          int M, int n_ff, int K, float alpha, cudaStream_t stream) {
+    if (fault_hit("fr_gemm_swiglu_f32out")) return FR_EINJECTED;
+    if (n_ff <= 0 || n_ff % 8 != 0) return FR_EINVAL;
+    return gemm_p_run(P_SWIGLU, A_packed, SFA, B_pair, SFB_pair, D, M, 2 * n_ff, K, alpha, stream);
+}
+
+int fr_repack_weight_pair_interleaved(const void *gate_blocks, const void *up_blocks, void *dst_packed, void *dst_sf,
+                                      int n_ff, int K, cudaStream_t stream) {
+    if (fault_hit("fr_repack_weight_pair_interleaved")) return FR_EINJECTED;
+    if (!gate_blocks || !up_blocks || !dst_packed || !dst_sf || n_ff <= 0 || K <= 0 || K % 64 != 0) return FR_EINVAL;
+    if (reinterpret_cast<uintptr_t>(dst_packed) & 7) return FR_EINVAL;
+    const int N2 = 2 * n_ff;
+    if (sf_offset(N2 - 1, K - 16, K) + 1 > fr_sf_bytes(N2, K)) return FR_ELAYOUT;
+    const int K16 = K / 16;
+    int rc = launch_pdl(k_repack, dim3((K16 + 127) / 128, n_ff), dim3(128), 0, stream,
+                        static_cast<const uint8_t *>(gate_blocks), static_cast<uint2 *>(dst_packed),
+                        static_cast<uint8_t *>(dst_sf), n_ff, K, 2, 0);
     if (rc != FR_OK) return rc;
-    rc = make_map_sw128(&mb, B_packed, N, K / 2);
-    if (rc != FR_OK) return rc;
-    static bool attr_done[64] = {};
-    rc = allow_max_smem(k_gemm_nvf4, attr_done);
-    if (rc != FR_OK) return rc;
-    GemmArgs g{static_cast<const uint8_t *>(SFA), static_cast<const uint8_t *>(SFB), D, M, N, K, alpha};
-    return launch_pdl(k_gemm_nvf4, dim3((N + G_BN - 1) / G_BN, (M + G_BM - 1) / G_BM), dim3(G_THREADS), G_SMEM,
-                      stream, ma, mb, g);
+    return launch_pdl(k_repack, dim3((K16 + 127) / 128, n_ff), dim3(128), 0, stream,
+                      static_cast<const uint8_t *>(up_blocks), static_cast<uint2 *>(dst_packed),
+                      static_cast<uint8_t *>(dst_sf), n_ff, K, 2, 1);
 }
 
 } // extern "C"

@@ -93,6 +93,8 @@ SIGNATURES = {
     "fr_quantize_act_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "fr_repack_weight": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "fr_gemm_f32out": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, C.c_bool, _vp]),
+    "fr_gemm_swiglu_f32out": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _vp]),
+    "fr_repack_weight_pair_interleaved": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _vp]),
     "fr_synth_nvfp4": (None, [C.c_uint64, _i64, _i64, C.c_double, _vp]),
     "fr_synth_normal": (None, [C.c_uint64, _i64, C.c_double, C.c_double, _vp]),
 }
@@ -416,5 +418,23 @@ def gemm_f32out(A, SFA, B, SFB, M, N, K, alpha=1.0, out=None, stream=None):
     if out is None:
         out = torch.empty((M, N), dtype=torch.float32, device=A.device)
     call("fr_gemm_f32out", _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(out), M, N, K, alpha, False,
+         _stream(stream))
+    return out
+
+
+def repack_weight_pair_interleaved(gate_blocks, up_blocks, n_ff, K, stream=None):
+    import torch
+    packed = torch.empty((2 * n_ff, K // 2), dtype=torch.uint8, device=gate_blocks.device)
+    sf = torch.zeros(sf_bytes(2 * n_ff, K), dtype=torch.uint8, device=gate_blocks.device)
+    call("fr_repack_weight_pair_interleaved", _ptr(gate_blocks), _ptr(up_blocks), _ptr(packed), _ptr(sf), n_ff, K,
+         _stream(stream))
+    return packed, sf
+
+
+def gemm_swiglu_f32out(A, SFA, B_pair, SFB_pair, M, n_ff, K, alpha=1.0, out=None, stream=None):
+    import torch
+    if out is None:
+        out = torch.empty((M, n_ff), dtype=torch.float32, device=A.device)
+    call("fr_gemm_swiglu_f32out", _ptr(A), _ptr(SFA), _ptr(B_pair), _ptr(SFB_pair), _ptr(out), M, n_ff, K, alpha,
          _stream(stream))
     return out

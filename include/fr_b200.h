@@ -146,7 +146,11 @@ int fr_ffn_nvfp4(const float *x, const void *wg, const void *wu, const void *wd,
  *     Every intermediate is fully rewritten by each call, so nothing needs
  *     clearing, but calls that overlap on the GPU (different streams without
  *     ordering between them) race on the array: order them on one stream or
- *     with events. */
+ *     with events.
+ *   - It always runs the dp4a matvec (the kernel that needs no workspace),
+ *     whatever fr_set_matvec_path says, so its results can differ from
+ *     fr_ffn_nvfp4's within the matvec tolerance, and at larger T it is
+ *     slower than the tensor-core path fr_ffn_nvfp4 would pick. */
 #define FR_FFN_NOALLOC_SCRATCH_BYTES (8u << 20)
 #define FR_ETOOBIG    (-904)  /* request larger than the static scratch */
 int fr_ffn_nvfp4_noalloc(const float *x, const void *wg, const void *wu, const void *wd,
@@ -359,10 +363,27 @@ int fr_quantize_act_f32(const float *src, void *dst_packed, void *dst_sfa,
 int fr_repack_weight(const void *ggml_blocks, void *dst_packed, void *dst_sf,
                      int N, int K, cudaStream_t stream);
 /* D [M, N] = alpha * A [M, K] . B [N, K]^T, NVFP4 x NVFP4 block-scaled on
- * tcgen05 (kind::mxf4nvf4), f32 out.  K % 64 == 0, N % 16 == 0.
+ * tcgen05 (kind::mxf4nvf4), f32 out: a persistent kernel, one CTA per SM,
+ * 128 x 256 tiles whose K stages are divided evenly over the CTAs (partial
+ * tiles added in a fixed order: deterministic).  K % 64 == 0, N % 16 == 0.
  * include/fr_kernels.h:41-44 */
 int fr_gemm_f32out(const void *A_packed, const void *SFA, const void *B_packed, const void *SFB,
                    float *D, int M, int N, int K, float alpha, bool widen, cudaStream_t stream);
+/* include/fr_kernels.h:59-65: repack a gate and an up matrix (ggml
+ * block_nvfp4, each [n_ff, K]) into one B operand of 2 * n_ff rows, row 2j =
+ * gate row j, row 2j+1 = up row j (packed [2 n_ff, K/2], dst_sf of
+ * fr_sf_bytes(2 n_ff, K)), byte for byte the reference's
+ * repack_weight_pair_interleaved (src/fr_repack.cu:66-136). */
+int fr_repack_weight_pair_interleaved(const void *gate_blocks, const void *up_blocks, void *dst_packed,
+                                      void *dst_sf, int n_ff, int K, cudaStream_t stream);
+/* The prefill FFN's gate/up GEMM with the SwiGLU fused into its epilogue:
+ * D [M, n_ff] f32 = silu(alpha * A . G^T) * (alpha * A . U^T), B_pair from
+ * fr_repack_weight_pair_interleaved, so the [M, 2 n_ff] gate/up product is
+ * never written.  The reference fuses GeGLU the same way
+ * (vendor/csrc/gemm/fp4/cutlass_fp4_gemm_geglu_il_sm100.cuh:1-25); this is
+ * its SiLU form.  K % 64 == 0, n_ff % 8 == 0. */
+int fr_gemm_swiglu_f32out(const void *A_packed, const void *SFA, const void *B_pair, const void *SFB_pair,
+                          float *D, int M, int n_ff, int K, float alpha, cudaStream_t stream);
 
 /* ------------------------------------------------------ synthetic inputs
  * Host-side, deterministic (splitmix64 + Box-Muller in double) generator of

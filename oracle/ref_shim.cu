@@ -22,6 +22,11 @@ int frref_gemm_f32out(const void *A, const void *SFA, const void *B, const void 
     return ggml_cuda_flashrt::gemm_f32out(A, SFA, B, SFB, D, M, N, K, alpha, widen != 0, s);
 }
 
+int frref_repack_weight_pair_interleaved(const void *gate, const void *up, void *dst_packed, void *dst_sf, int n_ff,
+                                         int K, cudaStream_t s) {
+    return ggml_cuda_flashrt::repack_weight_pair_interleaved(gate, up, dst_packed, dst_sf, n_ff, K, s);
+}
+
 long long frref_sf_bytes(long long rows, long long K) { return ggml_cuda_flashrt::sf_bytes(rows, K); }
 
 } // extern "C"

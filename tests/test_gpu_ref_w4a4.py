@@ -169,3 +169,25 @@ def test_gemm_time_beside_reference(R, fr, dev, M, N, K, capsys):
         print(f"\n[gemm timing] M={M} N={N} K={K}: ours {res['ours']:.1f} us ({tf['ours']:.0f} TFLOP/s), "
               f"reference CUTLASS {res['reference']:.1f} us ({tf['reference']:.0f} TFLOP/s)")
     assert fr.device_status() == 0
+
+
+@pytest.mark.parametrize("n_ff,K", [(14336, 4096), (200, 512), (64, 64)])
+def test_pair_interleaved_repack_equals_reference(R, fr, dev, n_ff, K):
+    """fr_repack_weight_pair_interleaved against the reference's
+    repack_weight_pair_interleaved, byte for byte (packed and scales)."""
+    import ctypes as C
+    import torch
+    if not hasattr(R, "frref_repack_weight_pair_interleaved"):
+        pytest.skip("reference shim without the pair repack")
+    R.frref_repack_weight_pair_interleaved.restype = C.c_int
+    R.frref_repack_weight_pair_interleaved.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_int, C.c_void_p]
+    g = _t(fr.synth_nvfp4(0x5EED4600 + n_ff, n_ff, K), dev)
+    u = _t(fr.synth_nvfp4(0x5EED4700 + n_ff, n_ff, K), dev)
+    rp = torch.zeros((2 * n_ff, K // 2), dtype=torch.uint8, device=dev)
+    rsf = torch.zeros(fr.sf_bytes(2 * n_ff, K), dtype=torch.uint8, device=dev)
+    assert R.frref_repack_weight_pair_interleaved(fr._ptr(g), fr._ptr(u), fr._ptr(rp), fr._ptr(rsf), n_ff, K,
+                                                  fr._stream()) == 0
+    mp, msf = fr.repack_weight_pair_interleaved(g, u, n_ff, K)
+    torch.cuda.synchronize()
+    assert torch.equal(mp, rp)
+    assert torch.equal(msf, rsf)

@@ -133,3 +133,58 @@ def test_gemm_rejects_bad_shapes(fr, dev):
     p = fr._ptr(buf)
     assert L.fr_gemm_f32out(p, p, p, p, p, 128, 100, 256, 1.0, False, fr._stream()) == -1   # N % 16
     assert L.fr_gemm_f32out(p, p, p, p, p, 128, 128, 96, 1.0, False, fr._stream()) == -1    # K % 64
+
+
+@pytest.mark.parametrize("M,n_ff,K", [(512, 14336, 4096), (100, 768, 2048), (7, 208, 320)])
+def test_gemm_swiglu_fused_epilogue(fr, O, dev, M, n_ff, K):
+    """The prefill FFN's gate/up GEMM with the SwiGLU in its epilogue
+    (fr_gemm_swiglu_f32out on fr_repack_weight_pair_interleaved weights):
+    silu(g) * u against the fp64 products of the dequantized operands, and
+    against two plain GEMMs, within the GEMM tolerance (max rel err 1e-3
+    against max(|ref|, 1% rms), normwise 1e-5)."""
+    import torch
+    x = fr.synth_normal(0x5EED4800 + M, M * K).reshape(M, K)
+    wg = fr.synth_nvfp4(0x5EED4810 + n_ff, n_ff, K)
+    wu = fr.synth_nvfp4(0x5EED4820 + n_ff, n_ff, K)
+    A, SFA = fr.quantize_act_f32(_t(x, dev))
+    Bp, SFBp = fr.repack_weight_pair_interleaved(_t(wg, dev), _t(wu, dev), n_ff, K)
+    out = fr.gemm_swiglu_f32out(A, SFA, Bp, SFBp, M, n_ff, K, alpha=0.75)
+    Bg, SFBg = fr.repack_weight(_t(wg, dev), n_ff, K)
+    Bu, SFBu = fr.repack_weight(_t(wu, dev), n_ff, K)
+    g = fr.gemm_f32out(A, SFA, Bg, SFBg, M, n_ff, K, alpha=0.75)
+    u = fr.gemm_f32out(A, SFA, Bu, SFBu, M, n_ff, K, alpha=0.75)
+    torch.cuda.synchronize()
+    two = (u * (g / (1.0 + torch.exp(-g)))).cpu().numpy()
+    _check(out.cpu().numpy(), two, O, "fused vs two GEMMs")
+    rows = np.arange(M) if M <= 128 else np.sort(np.random.default_rng(1).choice(M, 64, replace=False))
+    a = dequant(A.cpu().numpy(), SFA.cpu().numpy(), M, K, O)[rows]
+    gd = 0.75 * (a @ dequant(Bg.cpu().numpy(), SFBg.cpu().numpy(), n_ff, K, O).T)
+    ud = 0.75 * (a @ dequant(Bu.cpu().numpy(), SFBu.cpu().numpy(), n_ff, K, O).T)
+    _check(out.cpu().numpy()[rows], ud * (gd / (1.0 + np.exp(-gd))), O, "fused vs fp64")
+    assert fr.device_status() == 0
+
+
+def test_gemm_deterministic_and_graph_replay(fr, dev):
+    """Stream-K partial tiles are added in CTA order: the same inputs give the
+    same bits on every launch, eager or replayed from a CUDA graph."""
+    import torch
+    M, N, K = 300, 4096, 14336
+    A, SFA = fr.quantize_act_f32(_t(fr.synth_normal(0x5EED4900, M * K).reshape(M, K), dev))
+    B, SFB = fr.repack_weight(_t(fr.synth_nvfp4(0x5EED4901, N, K), dev), N, K)
+    d0 = fr.gemm_f32out(A, SFA, B, SFB, M, N, K)
+    d1 = fr.gemm_f32out(A, SFA, B, SFB, M, N, K)
+    s = torch.cuda.Stream(dev)
+    out = torch.empty_like(d0)
+    with torch.cuda.stream(s):
+        fr.gemm_f32out(A, SFA, B, SFB, M, N, K, out=out, stream=s)
+    s.synchronize()
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph, stream=s):
+        fr.gemm_f32out(A, SFA, B, SFB, M, N, K, out=out, stream=s)
+    for _ in range(3):
+        out.zero_()
+        gph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, d0)
+    assert torch.equal(d0, d1)
+    assert fr.device_status() == 0
