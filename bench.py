@@ -302,6 +302,60 @@ def _prefill_config3(frb200, torch, dev, stream, time_fn, graphs_for, hbm, args)
     return out
 
 
+def _decoder_config4(frb200, torch, dev, stream, args):
+    """48 layers, hidden 2048, GQA 32/4 x 128, RoPE 1e6, RMSNorm,
+    128 experts top-8 FFN 768, vocab 151936, NVFP4 weights (generated on the
+    device), f16 KV cache.  A random 1024-token prompt (token ids uniform) is
+    fed by 1024 replays of the captured step, then decode steps are timed
+    (CUDA events around graph replays; each replay decodes one token per
+    sequence, reading the whole model's weights and the KV cache)."""
+    from frb200.decoder import Config, MoeDecoder
+    out = {}
+    P = 1024
+    for T, dense, experts in ((1, "ggml", "ggml"), (64, "ggml", "tiled")):
+        cfg = Config(ctx=2048)
+        dec = MoeDecoder(cfg, T, dense=dense, experts=experts, device=dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(0x5EED7000 + T)
+        prompt = torch.randint(0, cfg.vocab, (T, P), generator=g, device=dev, dtype=torch.int32)
+        dec.set_prompt(prompt)
+        with torch.cuda.stream(stream):
+            dec.step(stream=stream)                       # eager warm-up: workspaces
+        torch.cuda.synchronize()
+        dec.set_prompt(prompt)
+        dec.kc.zero_()
+        dec.vc.zero_()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            dec.step(stream=stream)
+        dec.pos.zero_()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for _ in range(P):                              # the prompt
+                graph.replay()
+        torch.cuda.synchronize()
+        n_dec = max(8, min(args.decode_steps, 2048 - P))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(n_dec):
+                graph.replay()
+            e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / n_dec
+        assert int(dec.pos) == P + n_dec and frb200.device_status() == 0
+        out[f"decode_b{T}_tok_s"] = round(T / (ms * 1e-3), 1)
+        out[f"decode_b{T}_ms_per_step"] = round(ms, 4)
+        out[f"decode_b{T}_layout"] = f"dense {dense}, experts {experts}"
+        del graph, dec
+        torch.cuda.empty_cache()
+    out["decode_note"] = (f"configs[4] model, {P}-token prompt then {n_dec} timed decode steps (positions "
+                          f"{P}..{P + n_dec - 1}), one CUDA graph per step, greedy arg-max feeding the next step")
+    return out
+
+
 def run_ours(args):
     import torch
     import frb200
@@ -513,6 +567,11 @@ def run_ours(args):
         extra.update(_gemv_config0(frb200, torch, dev, stream, time_fn, graphs_for, hbm, args))
         extra.update(_prefill_config3(frb200, torch, dev, stream, time_fn, graphs_for, hbm, args))
 
+    # ---------------- the synthetic 48-layer MoE decoder, 1024-token
+    # prompt then timed decode steps at 1 and 64 sequences (one GPU)
+    if world == 1 and not args.no_decoder:
+        extra.update(_decoder_config4(frb200, torch, dev, stream, args))
+
     # ---------------- MoE layer (config 3): fused on one GPU, expert-parallel over ranks
     msets = _moe_sets(frb200, torch, dev, rank, world, 2)
     ep = P.EpMoe(64, 2048, 768, 128, 8) if world > 1 else None
@@ -672,6 +731,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the configs[4] decoder lines")
+    ap.add_argument("--decode-steps", type=int, default=64, help="timed decode steps of the configs[4] decoder")
     ap.add_argument("--profile-case", action="store_true",
                     help="run a short fixed kernel sequence for profiler captures (no benchmark line)")
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step of --profile-case")

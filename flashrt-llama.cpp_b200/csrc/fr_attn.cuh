@@ -1,0 +1,434 @@
+// fr_attn.cuh -- the decode-step kernels around the NVFP4 matmuls of the
+// synthetic MoE decoder: RMSNorm, RoPE + f16 KV-cache
+// append, GQA decode attention on the tcgen05 tensor cores, NVFP4 token
+// embedding rows, greedy arg-max, and the step's position counter.
+//
+// Reference: the Flint windows' decode attention frt_fa_decode /
+// frt_fa_combine and their split plan (src/fr_win_flint_sm120.cu:2411-2846,
+// :2866-2930), the QK-norm / RoPE front (:478-884), the host restatements of
+// RMSNorm and SiLU (src/fr_win_flint_batched.cuh:466-476), and the fused QKV
+// post (include/fr_kernels.h qkv_post: RoPE + f16 store of K, f16 store of V).
+//
+// Layouts:
+//   x, xn         [T, H] f32 (T = sequences of the batch, one token each)
+//   qkv           [T, (nh + 2 nkv) * d] f32: q heads, then k heads, then v heads
+//   q_r           [T, nh, d] f32, RoPE'd and pre-scaled by 1/sqrt(d)
+//   K / V cache   per layer [T, nkv, ctx, d] f16 (a sequence's rows of one KV
+//                 head contiguous, so a chunk of keys is one contiguous box)
+//   attention out [T, nh * d] f32
+#pragma once
+
+#include "fr_tc.cuh"
+
+namespace frb {
+
+constexpr int AT_D = 128;          // head dimension
+constexpr int AT_G = 8;            // query heads per KV head (32 / 4)
+constexpr int AT_CH = 128;         // keys per CTA (one split)
+constexpr int AT_THREADS = 128;
+
+// ------------------------------------------------------------------ RMSNorm
+// y = x / sqrt(mean(x^2) + eps) * w (w nullable = 1); one CTA per row.
+__global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w,
+                                                 float *__restrict__ y, int H, float eps) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    const float *xr = x + static_cast<int64_t>(blockIdx.x) * H;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    __shared__ float red[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float scale = rsqrtf(red[0] / static_cast<float>(H) + eps);
+    float *yr = y + static_cast<int64_t>(blockIdx.x) * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) yr[i] = w ? xr[i] * scale * w[i] : xr[i] * scale;
+}
+
+// ------------------------------------------------------------ RoPE + KV append
+// NeoX rotation (dimension pairs i, i + d/2) at position *pos with
+// theta_i = pos * theta_scale^i, theta_scale = base^(-2/d), cos / sin of
+// theta in f32 -- the arithmetic of ggml's rope_neox as the reference's QKV
+// post restates it (src/fr_qkv_post.cu:71-131, no YaRN correction, freq_scale
+// and attn_factor 1); q rows scaled by qscale; K and V rows of the step stored
+// as f16 at row *pos of the layer's cache.  grid (T).
+__global__ void __launch_bounds__(256) k_rope_kv(const float *__restrict__ qkv, const int32_t *__restrict__ pos_p,
+                                                 float *__restrict__ q_r, __half *__restrict__ kc,
+                                                 __half *__restrict__ vc, int nh, int nkv, int ctx, float base,
+                                                 float qscale) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    const int t = blockIdx.x;
+    const int pos = *pos_p;
+    const int half = AT_D / 2;
+    const int width = (nh + 2 * nkv) * AT_D;
+    const float *row = qkv + static_cast<int64_t>(t) * width;
+    // rotated pairs of the q and k heads
+    const float theta_scale = powf(base, -2.0f / static_cast<float>(AT_D));
+    for (int i = threadIdx.x; i < (nh + nkv) * half; i += blockDim.x) {
+        const int hd = i / half, j = i % half;
+        const float theta = static_cast<float>(pos) * powf(theta_scale, static_cast<float>(j));
+        const float cs = cosf(theta), sn = sinf(theta);
+        const float a = row[hd * AT_D + j], b = row[hd * AT_D + j + half];
+        const float ra = a * cs - b * sn, rb = a * sn + b * cs;
+        if (hd < nh) {
+            float *qo = q_r + (static_cast<int64_t>(t) * nh + hd) * AT_D;
+            qo[j] = ra * qscale;
+            qo[j + half] = rb * qscale;
+        } else {
+            const int g = hd - nh;
+            __half *ko = kc + ((static_cast<int64_t>(t) * nkv + g) * ctx + pos) * AT_D;
+            ko[j] = __float2half_rn(ra);
+            ko[j + half] = __float2half_rn(rb);
+        }
+    }
+    // V rows copied as f16
+    for (int i = threadIdx.x; i < nkv * AT_D; i += blockDim.x) {
+        const int g = i / AT_D, c = i % AT_D;
+        vc[((static_cast<int64_t>(t) * nkv + g) * ctx + pos) * AT_D + c] =
+            __float2half_rn(row[(nh + nkv) * AT_D + i]);
+    }
+}
+
+// ggml's kvalues_mxfp4 (twice the E2M1 value) of a 4-bit code
+__device__ __forceinline__ float kvalue_nvfp4(int c) {
+    const int m = c & 7;
+    const int mag = m < 5 ? m : (m == 5 ? 6 : (m == 6 ? 8 : 12));
+    return static_cast<float>((c & 8) ? -mag : mag);
+}
+
+// --------------------------------------------------------- NVFP4 embedding rows
+// x[t, :] = dequant(table row tok[t]) with ggml's NVFP4 reading (value =
+// E2M1(code) * UE4M3(scale), scale sign ignored, 0x7F -> 0); the token is
+// prompt[t * prompt_ld + pos] while pos < prompt_len, else gen[t] (the last
+// step's arg-max).  One CTA per token, one thread per 64-value block.
+__global__ void __launch_bounds__(256) k_embed_nvfp4(const uint8_t *__restrict__ table, int64_t row_bytes,
+                                                     const int32_t *__restrict__ prompt, int prompt_ld,
+                                                     int prompt_len, const int32_t *__restrict__ gen,
+                                                     const int32_t *__restrict__ pos_p, float *__restrict__ x, int H,
+                                                     int vocab) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    const int t = blockIdx.x;
+    const int pos = *pos_p;
+    int tok = pos < prompt_len ? prompt[static_cast<int64_t>(t) * prompt_ld + pos] : gen[t];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0) fr_flag(FR_ST_BADINPUT);
+        tok = 0;
+    }
+    const uint8_t *r = table + static_cast<int64_t>(tok) * row_bytes;
+    float *xo = x + static_cast<int64_t>(t) * H;
+    for (int b = threadIdx.x; b < H / 64; b += blockDim.x) {
+        const uint8_t *blk = r + static_cast<int64_t>(b) * NV_BYTES;
+        float sc[4];
+        ue4m3x4(*reinterpret_cast<const uint32_t *>(blk), sc);   // ggml's value: kvalue * ue4m3 / 2
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint8_t byte = blk[4 + 8 * s + j];
+                xo[64 * b + 16 * s + j] = kvalue_nvfp4(byte & 15) * sc[s] * 0.5f;
+                xo[64 * b + 16 * s + j + 8] = kvalue_nvfp4(byte >> 4) * sc[s] * 0.5f;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------- arg-max
+// tok[t] = argmax_v logits[t, v] (ties: the lowest index; NaN never wins).
+// One CTA per row.
+__global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ logits, int V, int32_t *__restrict__ tok) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    const float *r = logits + static_cast<int64_t>(blockIdx.x) * V;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float f = r[v];
+        if (f > best) { best = f; bi = v; }      // v ascending per thread: the first max is kept
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    __shared__ float sb[32];
+    __shared__ int si[32];
+    if ((threadIdx.x & 31) == 0) { sb[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const bool in = threadIdx.x < (blockDim.x >> 5);
+        best = in ? sb[threadIdx.x] : -INFINITY;
+        bi = in ? si[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        if (threadIdx.x == 0) tok[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+// the step's position advances once every kernel of the step has read it
+__global__ void k_pos_advance(int32_t *pos_p) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    if (threadIdx.x == 0) *pos_p += 1;
+}
+
+// ------------------------------------------------------ GQA decode attention
+// One CTA per (split of AT_CH keys, KV head g, sequence t): the KV head's
+// keys [s * 128, s * 128 + 128) of sequence t against its 8 query heads,
+// both matmuls on the tensor cores (tcgen05.mma kind::f16, f32 in TMEM):
+//   S^T [128 keys x 16] = K_chunk [128 x 128] . Q^T   (Q: 8 heads, 8 zero rows)
+//   softmax over the keys (thread = key = TMEM lane), P^T in f16
+//   O^T [128 dims x 16] = V_chunk^T [128 x 128] . P^T (V transposed in shared memory)
+// so K and V are read once per KV head for all 8 heads.  Each split writes
+// (m, l, o) per head; the last CTA of (t, g) to finish merges the splits in
+// split order (deterministic) into out.  K / V chunks arrive by TMA
+// (128-byte swizzle) straight from the cache; rows past the step's keys are
+// masked (the cache is zero-initialised, so they are finite).
+struct AtArgs {
+    const float *q;              // [T, nh, d], RoPE'd, pre-scaled
+    const int32_t *pos;          // keys = *pos + 1
+    int nh, nkv, ctx;
+    float *part;                 // [T][nkv][splits][16 + 8 * 128]: m[8], l[8], o[8][128]
+    unsigned int *counter;       // [T * nkv], zero on entry, reset by the merging CTA
+    float *out;                  // [T, nh * d]
+};
+
+constexpr int AT_SLAB = 128 * 128;                 // 128 rows x 128 B
+constexpr int AT_QSLAB = 16 * 128;                 // 16 rows x 128 B
+constexpr int AT_PART = 16 + AT_G * AT_D;
+constexpr size_t AT_SMEM = 1024 + 6 * AT_SLAB + 4 * AT_QSLAB + 512 + 64;
+
+__device__ __forceinline__ void tc_mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16_f32acc(int M, int N) {
+    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constant__ CUtensorMap tmK,
+                                                            const __grid_constant__ CUtensorMap tmV,
+                                                            const AtArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *Ks = smem;                        // 2 slabs: keys x dims [0, 64) and [64, 128)
+    uint8_t *Vs = Ks + 2 * AT_SLAB;            // same for V
+    uint8_t *Vt = Vs + 2 * AT_SLAB;            // 2 slabs: dims x keys [0, 64) and [64, 128)
+    uint8_t *Qs = Vt + 2 * AT_SLAB;            // 2 slabs: 16 heads x dims
+    uint8_t *Pt = Qs + 2 * AT_QSLAB;           // 2 slabs: 16 heads x keys
+    float *red = reinterpret_cast<float *>(Pt + 2 * AT_QSLAB);     // [4 warps][8] x 2, then M[8], L[8]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(red + 96);       // tma, mma
+    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(bars + 2);
+    int *flag = reinterpret_cast<int *>(tmem_s + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int s = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 0) tmem_alloc(tmem_s, 32);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = *tmem_s;
+    fr_pdl_wait();                                     // q, the cache rows and pos come from earlier kernels
+    const int n = *a.pos + 1;
+    const int k0 = s * AT_CH;
+    const int splits = gridDim.x;
+    float *part = a.part + ((static_cast<int64_t>(t) * a.nkv + g) * splits + s) * AT_PART;
+    bool ok = true;
+    if (k0 < n) {
+        const int nk = min(AT_CH, n - k0);
+        if (tid == 0) {
+            const int row0 = (t * a.nkv + g) * a.ctx + k0;
+            mbar_expect_tx(&bars[0], 4 * AT_SLAB);
+            tma_load_2d(Ks, &tmK, 0, row0, &bars[0]);
+            tma_load_2d(Ks + AT_SLAB, &tmK, 64, row0, &bars[0]);
+            tma_load_2d(Vs, &tmV, 0, row0, &bars[0]);
+            tma_load_2d(Vs + AT_SLAB, &tmV, 64, row0, &bars[0]);
+        }
+        // Q tile (f16, 128-byte swizzled K-major): 16 rows x 16 chunks of 8 dims; rows 8..15 zero
+        for (int i = tid; i < 16 * 16; i += AT_THREADS) {
+            const int h = i >> 4, c = i & 15;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (h < AT_G) {
+                const float4 *qp = reinterpret_cast<const float4 *>(
+                    a.q + (static_cast<int64_t>(t) * a.nh + g * AT_G + h) * AT_D + 8 * c);
+                const float4 f0 = qp[0], f1 = qp[1];
+                const __half2 h0 = __floats2half2_rn(f0.x, f0.y), h1 = __floats2half2_rn(f0.z, f0.w);
+                const __half2 h2 = __floats2half2_rn(f1.x, f1.y), h3 = __floats2half2_rn(f1.z, f1.w);
+                v = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                               *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+            }
+            *reinterpret_cast<uint4 *>(Qs + (c >> 3) * AT_QSLAB + h * 128 + (((c & 7) ^ (h & 7)) << 4)) = v;
+        }
+        // P^T rows 8..15 stay zero
+        for (int i = tid; i < 8 * 16; i += AT_THREADS) {
+            const int h = 8 + (i >> 4), c = i & 15;
+            *reinterpret_cast<uint4 *>(Pt + (c >> 3) * AT_QSLAB + h * 128 + (((c & 7) ^ (h & 7)) << 4)) =
+                make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async();
+        __syncthreads();
+        ok = mbar_wait(&bars[0], 0, 50);
+        if (tid == 0 && ok) {
+            tc_fence_after();
+            const uint32_t idesc = idesc_f16_f32acc(128, 16);
+            for (int j = 0; j < 8; ++j) {
+                const int sl = j >> 2, ko = (j & 3) * 32;
+                tc_mma_f16_ss(tm, sdesc_sw128(smem_u32(Ks + sl * AT_SLAB) + ko),
+                              sdesc_sw128(smem_u32(Qs + sl * AT_QSLAB) + ko), idesc, j > 0 ? 1u : 0u);
+            }
+            tc_commit(&bars[1]);
+        }
+        if (ok) {
+            // V [keys x dims] -> V^T [dims x keys], 8x8 blocks of halves
+            for (int blk = tid; blk < 256; blk += AT_THREADS) {
+                const int kg = blk >> 4, dg = blk & 15;
+                uint32_t in[8][4];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int key = 8 * kg + r;
+                    const uint4 w = *reinterpret_cast<const uint4 *>(Vs + (dg >> 3) * AT_SLAB + key * 128 +
+                                                                      (((dg & 7) ^ (key & 7)) << 4));
+                    in[r][0] = w.x; in[r][1] = w.y; in[r][2] = w.z; in[r][3] = w.w;
+                }
+#pragma unroll
+                for (int d = 0; d < 8; ++d) {
+                    uint32_t o[4];
+#pragma unroll
+                    for (int r2 = 0; r2 < 4; ++r2) {
+                        const uint32_t lo = (in[2 * r2][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
+                        const uint32_t hi = (in[2 * r2 + 1][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
+                        o[r2] = lo | (hi << 16);
+                    }
+                    const int dim = 8 * dg + d;
+                    *reinterpret_cast<uint4 *>(Vt + (kg >> 3) * AT_SLAB + dim * 128 + (((kg & 7) ^ (dim & 7)) << 4)) =
+                        make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            ok = mbar_wait(&bars[1], 0, 51);
+        }
+        tc_fence_after();
+        // scores: thread = key = TMEM lane
+        const int key = warp * 32 + lane;
+        float sv[AT_G];
+        {
+            uint32_t r[16];
+            tmem_ld16(tm + (static_cast<uint32_t>(warp * 32) << 16), r);
+#pragma unroll
+            for (int h = 0; h < AT_G; ++h) sv[h] = (ok && key < nk) ? __uint_as_float(r[h]) : -INFINITY;
+        }
+        float *M = red + 64, *L = red + 72;
+#pragma unroll
+        for (int h = 0; h < AT_G; ++h) {
+            float m = sv[h];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) red[warp * 8 + h] = m;
+        }
+        __syncthreads();
+        if (tid < AT_G) M[tid] = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < AT_G; ++h) {
+            const float mh = M[h];
+            const __half p16 = __float2half_rn(key < nk && mh > -INFINITY ? expf(sv[h] - mh) : 0.0f);
+            float l = __half2float(p16);               // the sum of the probabilities the MMA multiplies
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if (lane == 0) red[32 + warp * 8 + h] = l;
+            const int kk = key & 63;
+            *reinterpret_cast<__half *>(Pt + (key >> 6) * AT_QSLAB + h * 128 + (((kk >> 3) ^ (h & 7)) << 4) +
+                                        (kk & 7) * 2) = p16;
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        __syncthreads();
+        if (tid < AT_G) L[tid] = (red[32 + tid] + red[40 + tid]) + (red[48 + tid] + red[56 + tid]);
+        if (tid == 0 && ok) {
+            tc_fence_after();
+            const uint32_t idesc = idesc_f16_f32acc(128, 16);
+            for (int j = 0; j < 8; ++j) {
+                const int sl = j >> 2, ko = (j & 3) * 32;
+                tc_mma_f16_ss(tm + 16, sdesc_sw128(smem_u32(Vt + sl * AT_SLAB) + ko),
+                              sdesc_sw128(smem_u32(Pt + sl * AT_QSLAB) + ko), idesc, j > 0 ? 1u : 0u);
+            }
+            tc_commit(&bars[1]);
+        }
+        if (ok) ok = mbar_wait(&bars[1], 1, 52);
+        tc_fence_after();
+        {
+            uint32_t r[16];
+            tmem_ld16(tm + (static_cast<uint32_t>(warp * 32) << 16) + 16, r);
+            const int d = warp * 32 + lane;             // thread = head dimension = TMEM lane
+#pragma unroll
+            for (int h = 0; h < AT_G; ++h) part[16 + h * AT_D + d] = ok ? __uint_as_float(r[h]) : 0.0f;
+        }
+        __syncthreads();
+        if (tid < AT_G) {
+            part[tid] = M[tid];
+            part[8 + tid] = L[tid];
+        }
+    }
+    // the last CTA of (t, g) merges the splits
+    __threadfence();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        unsigned int *c = a.counter + t * a.nkv + g;
+        const unsigned prev = atomicAdd(c, 1u);
+        *flag = prev == static_cast<unsigned>(splits - 1);
+        if (*flag) *c = 0u;
+    }
+    __syncthreads();
+    if (*flag) {
+        __threadfence();
+        const int ns = min(splits, (n + AT_CH - 1) / AT_CH);
+        const float *base = a.part + (static_cast<int64_t>(t) * a.nkv + g) * splits * AT_PART;
+        const int d = tid;
+#pragma unroll 1
+        for (int h = 0; h < AT_G; ++h) {
+            float mx = -INFINITY;
+            for (int s2 = 0; s2 < ns; ++s2) mx = fmaxf(mx, __ldcg(base + s2 * AT_PART + h));
+            float lsum = 0.0f, o = 0.0f;
+            for (int s2 = 0; s2 < ns; ++s2) {
+                const float w = expf(__ldcg(base + s2 * AT_PART + h) - mx);
+                lsum = fmaf(w, __ldcg(base + s2 * AT_PART + 8 + h), lsum);
+                o = fmaf(w, __ldcg(base + s2 * AT_PART + 16 + h * AT_D + d), o);
+            }
+            a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h) * AT_D + d] = o / lsum;
+        }
+    }
+    fr_pdl_trigger();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tm, 32);
+    }
+}
+
+} // namespace frb

@@ -49,7 +49,9 @@ constexpr int P_EPI_WARPS = 8;
 constexpr int P_CW = P_BN / (P_EPI_WARPS / 4);               // accumulator columns per epilogue thread
 constexpr int P_THREADS = (4 + P_EPI_WARPS) * 32;             // warpgroup 0: producer, MMA, 2 idle
 constexpr uint32_t P_TMEM_COLS = 512;                      // acc [0,256) + 4 stages x 48 SF columns
-constexpr size_t P_SMEM = 1024 + static_cast<size_t>(P_STAGES) * P_STAGE + 256;
+constexpr int P_STG_FLOATS = 32 * 9;                       // per epilogue warp: 32 rows x 8 columns (+1 pad)
+constexpr size_t P_SMEM = 1024 + static_cast<size_t>(P_STAGES) * P_STAGE + 256 +
+                          static_cast<size_t>(P_EPI_WARPS) * P_STG_FLOATS * sizeof(float);
 constexpr int P_SLOT_FLOATS = P_BM * P_BN;                 // one partial accumulator
 
 enum PEpi : int { P_PLAIN = 0, P_SWIGLU = 1 };
@@ -108,47 +110,57 @@ __device__ __forceinline__ void tmem_ld_wait_dep(uint32_t *r) {
                  :: "memory");
 }
 
-// 32 accumulator columns [c0, c0 + 32) of tile row m of a finished tile.
-// Plain: D[m, n0 + c0 + i] = alpha v[i]; SwiGLU: pairs (2i, 2i+1) = (gate,
-// up) of output column (n0 + c0) / 2 + i.
-template <int EPI>
-__device__ __forceinline__ void p_store32(const PGemmArgs &g, int m, int n0, int c0, const float *v) {
-    if (m >= g.M) return;
-    if (EPI == P_PLAIN) {
-        const int cb = n0 + c0;
-        float *dst = g.D + static_cast<int64_t>(m) * g.ldd + cb;
+// Stores the finished values of one epilogue warp: v[i] is column c0 + i of
+// tile row rbase + lane (i < ncols, ncols % 8 == 0).  Plain: D[m, n0 + c] =
+// alpha v; SwiGLU: v holds (gate, up) pairs, output column (n0 + c) / 2.  The
+// values go through a 32 x 8 shared-memory tile per warp so that each store
+// instruction writes whole 32-byte sectors of 16 rows instead of 16 bytes of
+// 32 rows.
+template <int EPI, int NC>
+__device__ __forceinline__ void p_store_rows(const PGemmArgs &g, int rbase, int n0, int c0, const float *v,
+                                             float *stg, int lane) {
+    if (EPI == P_SWIGLU) {
+        float o[NC / 2];
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-            if (cb + i + 4 <= g.N) {
-                *reinterpret_cast<float4 *>(dst + i) =
-                    make_float4(v[i] * g.alpha, v[i + 1] * g.alpha, v[i + 2] * g.alpha, v[i + 3] * g.alpha);
-            } else {
+        for (int i = 0; i < NC / 2; ++i) {
+            float up = v[2 * i + 1] * g.alpha;
+            const float gate = v[2 * i] * g.alpha;
+            up *= silu_f(gate);
+            o[i] = up;
+        }
+        const int nout = g.N / 2;
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (cb + i + k < g.N) dst[i + k] = v[i + k] * g.alpha;
+        for (int cc = 0; cc < NC / 2; cc += 8) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) stg[lane * 9 + i] = o[cc + i];
+            __syncwarp();
+#pragma unroll
+            for (int rep = 0; rep < 2; ++rep) {
+                const int rr = (lane >> 1) + 16 * rep, hf = lane & 1;
+                const int m = rbase + rr, col = (n0 + c0) / 2 + cc + 4 * hf;
+                if (m < g.M && col < nout)
+                    *reinterpret_cast<float4 *>(g.D + static_cast<int64_t>(m) * g.ldd + col) =
+                        make_float4(stg[rr * 9 + 4 * hf], stg[rr * 9 + 4 * hf + 1], stg[rr * 9 + 4 * hf + 2],
+                                    stg[rr * 9 + 4 * hf + 3]);
             }
+            __syncwarp();
         }
     } else {
-        const int nout = g.N / 2;
-        const int cb = (n0 + c0) / 2;
-        float *dst = g.D + static_cast<int64_t>(m) * g.ldd + cb;
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-            float o[4];
+        for (int cc = 0; cc < NC; cc += 8) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float up = v[2 * (i + k) + 1] * g.alpha;
-                const float gate = v[2 * (i + k)] * g.alpha;
-                up *= silu_f(gate);
-                o[k] = up;
+            for (int i = 0; i < 8; ++i) stg[lane * 9 + i] = v[cc + i];
+            __syncwarp();
+#pragma unroll
+            for (int rep = 0; rep < 2; ++rep) {
+                const int rr = (lane >> 1) + 16 * rep, hf = lane & 1;
+                const int m = rbase + rr, col = n0 + c0 + cc + 4 * hf;
+                if (m < g.M && col < g.N)
+                    *reinterpret_cast<float4 *>(g.D + static_cast<int64_t>(m) * g.ldd + col) =
+                        make_float4(stg[rr * 9 + 4 * hf] * g.alpha, stg[rr * 9 + 4 * hf + 1] * g.alpha,
+                                    stg[rr * 9 + 4 * hf + 2] * g.alpha, stg[rr * 9 + 4 * hf + 3] * g.alpha);
             }
-            if (cb + i + 4 <= nout) {
-                *reinterpret_cast<float4 *>(dst + i) = make_float4(o[0], o[1], o[2], o[3]);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (cb + i + k < nout) dst[i + k] = o[k];
-            }
+            __syncwarp();
         }
     }
 }
@@ -163,7 +175,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
     uint64_t *empty = full + P_STAGES;
     uint64_t *acc_full = empty + P_STAGES;
     uint64_t *acc_empty = acc_full + 1;
-    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(acc_empty + 1);
+    uint64_t *epi_done = acc_empty + 1;                // every epilogue warp is past its last TMEM read
+    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(epi_done + 1);
     volatile int *bcast = reinterpret_cast<volatile int *>(tmem_s + 1);     // [4]: last arrival, lo, hi, abort
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -180,6 +193,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, P_EPI_WARPS);
+        mbar_init(epi_done, P_EPI_WARPS);
         bcast[3] = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -282,7 +296,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
         asm volatile("setmaxnreg.inc.sync.aligned.u32 232;" ::: "memory");
         const int q = warp & 3;                             // TMEM lane quadrant this warp may access
         const int cw0 = ((warp - 4) >> 2) * P_CW;           // first accumulator column of this warp
-        const int row = 32 * q + lane;                      // tile row
+        const int wb = q + 4 * ((warp - 4) >> 2);           // this warp's block of a partial slot
+        float *stg = reinterpret_cast<float *>(smem + P_STAGES * P_STAGE + 256) + (warp - 4) * P_STG_FLOATS;
         const bool leader = threadIdx.x == 128;
         int seg = 0;
         for (int64_t u = u_begin; u < u_end; ++seg) {
@@ -291,7 +306,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
             const int kt1 = static_cast<int>(min(static_cast<int64_t>(nkt), kt0 + (u_end - u)));
             int mb, nb;
             p_tile_mn(g, t, mb, nb);
-            const int m = mb * P_BM + row, n0 = nb * P_BN;
+            const int n0 = nb * P_BN;
             const bool ok = mbar_wait(acc_full, static_cast<uint32_t>(seg) & 1u, 44);
             tc_fence_after();
             uint32_t r[P_CW];
@@ -311,16 +326,17 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
             if (bcast[3]) break;                            // a wait gave up (flagged): all epilogue warps stop
             const float *v = reinterpret_cast<const float *>(r);
             if (kt0 == 0 && kt1 == nkt) {
-#pragma unroll
-                for (int c = 0; c < P_CW / 32; ++c) p_store32<EPI>(g, m, n0, cw0 + 32 * c, v + 32 * c);
+                p_store_rows<EPI, P_CW>(g, mb * P_BM + 32 * q, n0, cw0, v, stg, lane);
             } else {
                 // part of a tile shared with neighbouring CTAs: publish this
-                // CTA's partial in its slot (0: first segment, 1: last one)
+                // CTA's partial in its slot (0: first segment, 1: last one),
+                // laid out [warp block][column / 4][row][4] so that the
+                // warp's stores (and the merging loads) are 512-byte lines
                 float *slot = g.part + (static_cast<int64_t>(blockIdx.x) * 2 + (u == u_begin ? 0 : 1)) * P_SLOT_FLOATS;
-                float4 *dst = reinterpret_cast<float4 *>(slot + row * P_BN + cw0);
+                float4 *blk = reinterpret_cast<float4 *>(slot + wb * (32 * P_CW)) + lane;
 #pragma unroll
                 for (int i = 0; i < P_CW / 4; ++i)
-                    dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    blk[i * 32] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 fence_acq_rel_gpu();
                 named_bar(1, P_EPI_WARPS * 32);
                 if (leader) {
@@ -341,35 +357,59 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
                     // slot) added in CTA order, whoever arrived last; 32
                     // columns at a time
 #pragma unroll 1
-                    for (int ch = 0; ch < P_CW / 32; ++ch) {
+                    for (int ch = 0; ch < P_CW; ch += 32) {
                         float acc[32];
+                        // two contributors' loads in flight at a time, then
+                        // their sums in CTA order
 #pragma unroll 1
-                        for (int c = c_lo; c <= c_hi; ++c) {
-                            const int sl = (p_u0(c, U, G) / nkt == t) ? 0 : 1;
-                            const float4 *src = reinterpret_cast<const float4 *>(
-                                g.part + (static_cast<int64_t>(c) * 2 + sl) * P_SLOT_FLOATS + row * P_BN + cw0 + 32 * ch);
+                        for (int c0 = c_lo; c0 <= c_hi; c0 += 2) {
+                            float4 w[2][8];
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const float4 w = __ldcg(src + i);
-                                if (c == c_lo) {
-                                    acc[4 * i] = w.x; acc[4 * i + 1] = w.y; acc[4 * i + 2] = w.z; acc[4 * i + 3] = w.w;
-                                } else {
-                                    acc[4 * i] += w.x; acc[4 * i + 1] += w.y; acc[4 * i + 2] += w.z;
-                                    acc[4 * i + 3] += w.w;
+                            for (int j = 0; j < 2; ++j) {
+                                const int c = min(c0 + j, c_hi);           // a spare slot re-reads the last
+                                const int sl = (p_u0(c, U, G) / nkt == t) ? 0 : 1;
+                                const float4 *src = reinterpret_cast<const float4 *>(
+                                                        g.part + (static_cast<int64_t>(c) * 2 + sl) * P_SLOT_FLOATS +
+                                                        wb * (32 * P_CW)) + (ch / 4) * 32 + lane;
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) w[j][i] = __ldcg(src + i * 32);
+                            }
+#pragma unroll
+                            for (int j = 0; j < 2; ++j) {
+                                if (c0 + j > c_hi) continue;
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    if (c0 + j == c_lo) {
+                                        acc[4 * i] = w[j][i].x; acc[4 * i + 1] = w[j][i].y;
+                                        acc[4 * i + 2] = w[j][i].z; acc[4 * i + 3] = w[j][i].w;
+                                    } else {
+                                        acc[4 * i] += w[j][i].x; acc[4 * i + 1] += w[j][i].y;
+                                        acc[4 * i + 2] += w[j][i].z; acc[4 * i + 3] += w[j][i].w;
+                                    }
                                 }
                             }
                         }
-                        p_store32<EPI>(g, m, n0, cw0 + 32 * ch, acc);
+                        p_store_rows<EPI, 32>(g, mb * P_BM + 32 * q, n0, cw0 + ch, acc, stg, lane);
                     }
                 }
             }
             u += kt1 - kt0;
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(epi_done);
     }
+    // the role branches ran on one lane of warps 0 and 1: reconverge every
+    // warp before the block-wide barrier
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     fr_pdl_trigger();
     if (warp == 1) {
+        // free TMEM only once every epilogue warp has read its last
+        // accumulator (bounded; the status word says if it gave up)
+        if (lane == 0) mbar_wait(epi_done, 0, 45);
+        __syncwarp();
         tc_fence_after();
         tmem_dealloc(tbase, P_TMEM_COLS);
     }

@@ -12,6 +12,7 @@
 #include "fr_moe.cuh"
 #include "fr_w4a4.cuh"
 #include "fr_gemm.cuh"
+#include "fr_attn.cuh"
 #include "fr_tcgemv.cuh"
 #include "fr_fp4mv.cuh"
 #include "fr_fp4tile.cuh"
@@ -2377,6 +2378,144 @@ int fr_tp_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const vo
     if (nranks <= 0 || n_embd % 256 != 0 || n_ff % (256 * nranks) != 0) return FR_EINVAL;
     return tp_ffn_impl(x, wg_t, wu_t, wd_t, sg, su, sd, resid, out, T, n_embd, n_ff, nranks, rank, peer_base,
                        local_base, buffer_bytes, true, stream);
+}
+
+} // extern "C"
+
+// ======================================================================
+// Decode-step kernels of the synthetic MoE decoder
+// ======================================================================
+namespace frb {
+
+// [rows, 128] f16 rows (256 B), box 64 halves x 128 rows, 128-byte swizzle
+static int make_map_kv(CUtensorMap *map, const void *base, int64_t rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return FR_ENODEVICE;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(AT_D), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(AT_D * 2)};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
+}
+
+// splitmix64
+__device__ __forceinline__ uint64_t sm64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// NVFP4 blocks with BASELINE's distribution, generated on the device (for
+// multi-GB synthetic models): codes uniform over 0..15, sub-block scales
+// e4m3(|N(0,1)| * sigma) RNE (Box-Muller on two hashed uniforms).
+__global__ void k_synth_nvfp4(uint64_t seed, int64_t nblocks, float sigma, uint8_t *out) {
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    uint8_t *blk = out + b * NV_BYTES;
+    uint64_t h = sm64(seed ^ (static_cast<uint64_t>(b) * 0xD1B54A32D192ED03ull));
+#pragma unroll
+    for (int s = 0; s < 4; s += 2) {
+        const uint64_t r = sm64(h + s);
+        const double u1 = (static_cast<double>(r >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+        const double u2 = static_cast<double>(sm64(r) >> 11) * (1.0 / 9007199254740992.0);
+        const double rad = sqrt(-2.0 * log(u1));
+        const float n0 = static_cast<float>(fabs(rad * cos(6.283185307179586 * u2))) * sigma;
+        const float n1 = static_cast<float>(fabs(rad * sin(6.283185307179586 * u2))) * sigma;
+        blk[s] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(n0, __NV_SATFINITE, __NV_E4M3));
+        blk[s + 1] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(n1, __NV_SATFINITE, __NV_E4M3));
+    }
+    // 32 bytes of codes (uniform over all 16 values); blocks are 36 bytes
+    // apart, so 4-byte stores
+    uint32_t *codes = reinterpret_cast<uint32_t *>(blk + 4);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const uint64_t r = sm64(h ^ (0xA5A5A5A5ull + w));
+        codes[2 * w] = static_cast<uint32_t>(r);
+        codes[2 * w + 1] = static_cast<uint32_t>(r >> 32);
+    }
+}
+
+} // namespace frb
+
+extern "C" {
+
+int fr_synth_nvfp4_device(uint64_t seed, int64_t rows, int64_t K, double scale_sigma, void *out,
+                          cudaStream_t stream) {
+    if (!out || rows <= 0 || K <= 0 || K % 64 != 0) return FR_EINVAL;
+    const int64_t nb = rows * (K / 64);
+    const unsigned grid = static_cast<unsigned>((nb + 255) / 256);
+    k_synth_nvfp4<<<grid, 256, 0, stream>>>(seed, nb, static_cast<float>(scale_sigma), static_cast<uint8_t *>(out));
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cuda_rc(e);
+}
+
+int fr_rmsnorm_f32(const float *x, const float *w, float *y, int T, int H, float eps, cudaStream_t stream) {
+    if (fault_hit("fr_rmsnorm_f32")) return FR_EINJECTED;
+    if (!x || !y || T <= 0 || H <= 0) return FR_EINVAL;
+    return launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, stream, x, w, y, H, eps);
+}
+
+int fr_rope_kv_f16(const float *qkv, const int32_t *pos, float *q_r, void *kcache, void *vcache, int T, int nh,
+                   int nkv, int head_dim, int ctx, float rope_base, cudaStream_t stream) {
+    if (fault_hit("fr_rope_kv_f16")) return FR_EINJECTED;
+    if (!qkv || !pos || !q_r || !kcache || !vcache || T <= 0 || nh <= 0 || nkv <= 0 || ctx <= 0) return FR_EINVAL;
+    if (head_dim != AT_D) return FR_EINVAL;
+    return launch_pdl(k_rope_kv, dim3(T), dim3(256), 0, stream, qkv, pos, q_r, static_cast<__half *>(kcache),
+                      static_cast<__half *>(vcache), nh, nkv, ctx, rope_base, 1.0f / sqrtf(static_cast<float>(AT_D)));
+}
+
+int fr_attn_decode_f16(const float *q_r, const void *kcache, const void *vcache, const int32_t *pos, float *out,
+                       int T, int nh, int nkv, int head_dim, int ctx, cudaStream_t stream) {
+    if (fault_hit("fr_attn_decode_f16")) return FR_EINJECTED;
+    if (!q_r || !kcache || !vcache || !pos || !out || T <= 0 || nkv <= 0) return FR_EINVAL;
+    if (head_dim != AT_D || nh != AT_G * nkv || ctx <= 0 || ctx % AT_CH != 0) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(kcache) & 15) || (reinterpret_cast<uintptr_t>(vcache) & 15) ||
+        (reinterpret_cast<uintptr_t>(q_r) & 15))
+        return FR_EINVAL;
+    const DevInfo &di = dev_info();
+    if (di.cc_major != 10) return FR_ENODEVICE;
+    const int splits = ctx / AT_CH;
+    void *part = nullptr, *cnt = nullptr;
+    int rc = workspace_get(WS_ATPART, static_cast<size_t>(T) * nkv * splits * AT_PART * sizeof(float), stream, &part);
+    if (rc != FR_OK) return rc;
+    rc = workspace_get_zeroed(WS_ATCNT, static_cast<size_t>(T) * nkv * sizeof(unsigned int), stream, &cnt);
+    if (rc != FR_OK) return rc;
+    CUtensorMap mk, mv;
+    const int64_t rows = static_cast<int64_t>(T) * nkv * ctx;
+    rc = make_map_kv(&mk, kcache, rows);
+    if (rc != FR_OK) return rc;
+    rc = make_map_kv(&mv, vcache, rows);
+    if (rc != FR_OK) return rc;
+    static bool done[64] = {};
+    rc = allow_max_smem(k_attn_decode, done);
+    if (rc != FR_OK) return rc;
+    AtArgs a{q_r, pos, nh, nkv, ctx, static_cast<float *>(part), static_cast<unsigned int *>(cnt), out};
+    return launch_pdl(k_attn_decode, dim3(splits, nkv, T), dim3(AT_THREADS), AT_SMEM, stream, mk, mv, a);
+}
+
+int fr_embed_nvfp4(const void *table, int vocab, int H, const int32_t *prompt, int prompt_ld, int prompt_len,
+                   const int32_t *gen, const int32_t *pos, float *x, int T, cudaStream_t stream) {
+    if (fault_hit("fr_embed_nvfp4")) return FR_EINJECTED;
+    if (!table || !pos || !x || !gen || T <= 0 || vocab <= 0 || H <= 0 || H % 64 != 0) return FR_EINVAL;
+    if (prompt_len > 0 && !prompt) return FR_EINVAL;
+    return launch_pdl(k_embed_nvfp4, dim3(T), dim3(256), 0, stream, static_cast<const uint8_t *>(table),
+                      static_cast<int64_t>(H / 64 * NV_BYTES), prompt, prompt_ld, prompt_len, gen, pos, x, H, vocab);
+}
+
+int fr_argmax_f32(const float *logits, int T, int V, int32_t *tok, cudaStream_t stream) {
+    if (fault_hit("fr_argmax_f32")) return FR_EINJECTED;
+    if (!logits || !tok || T <= 0 || V <= 0) return FR_EINVAL;
+    return launch_pdl(k_argmax, dim3(T), dim3(1024), 0, stream, logits, V, tok);
+}
+
+int fr_pos_advance(int32_t *pos, cudaStream_t stream) {
+    if (!pos) return FR_EINVAL;
+    return launch_pdl(k_pos_advance, dim3(1), dim3(32), 0, stream, pos);
 }
 
 } // extern "C"

@@ -95,6 +95,13 @@ SIGNATURES = {
     "fr_gemm_f32out": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, C.c_bool, _vp]),
     "fr_gemm_swiglu_f32out": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _vp]),
     "fr_repack_weight_pair_interleaved": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _vp]),
+    "fr_rmsnorm_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _f32, _vp]),
+    "fr_rope_kv_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp]),
+    "fr_attn_decode_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "fr_embed_nvfp4": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _vp]),
+    "fr_argmax_f32": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "fr_pos_advance": (_i32, [_vp, _vp]),
+    "fr_synth_nvfp4_device": (_i32, [C.c_uint64, _i64, _i64, C.c_double, _vp, _vp]),
     "fr_synth_nvfp4": (None, [C.c_uint64, _i64, _i64, C.c_double, _vp]),
     "fr_synth_normal": (None, [C.c_uint64, _i64, C.c_double, C.c_double, _vp]),
 }

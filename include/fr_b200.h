@@ -385,6 +385,47 @@ int fr_repack_weight_pair_interleaved(const void *gate_blocks, const void *up_bl
 int fr_gemm_swiglu_f32out(const void *A_packed, const void *SFA, const void *B_pair, const void *SFB_pair,
                           float *D, int M, int n_ff, int K, float alpha, cudaStream_t stream);
 
+/* ------------------------------------- (f1/f2) decode step of the MoE decoder
+ * The kernels around the NVFP4 matmuls of a decode step of the synthetic
+ * 48-layer MoE decoder (llama.cpp runs these ops as
+ * ggml graph nodes, and the reference replaces the attention part with its
+ * Flint windows frt_fa_decode / frt_fa_combine, src/fr_win_flint_sm120.cu:
+ * 2411-2846, and the QKV post, include/fr_kernels.h qkv_post).  T sequences
+ * decode one token each per step; `pos` is a device int32 holding the step's
+ * position (the same for every sequence); it is read after the previous
+ * kernel completes, so a whole step can be captured once as a CUDA graph and
+ * replayed.
+ *   fr_rmsnorm_f32     y = x / sqrt(mean(x^2) + eps) * w  (w nullable = 1), [T, H]
+ *   fr_rope_kv_f16     qkv [T, (nh + 2 nkv) * d] (q heads, k heads, v heads):
+ *                      NeoX RoPE (pairs i, i + d/2, theta_i = pos *
+ *                      base^(-2i/d)) of q (scaled by 1/sqrt(d), into q_r
+ *                      [T, nh, d] f32) and k, which with v is appended as f16
+ *                      at row pos of the caches [T, nkv, ctx, d]
+ *   fr_attn_decode_f16 GQA decode attention over keys 0..pos: out [T, nh * d]
+ *                      = softmax(q k^T) v per head, KV head of head h = h /
+ *                      (nh / nkv); tcgen05 tensor cores (f16 operands, f32
+ *                      accumulation, probabilities rounded to f16 for the PV
+ *                      product); d == 128, nh == 8 nkv, ctx % 128 == 0; the
+ *                      caches zero-initialised before first use
+ *   fr_embed_nvfp4     x[t] = NVFP4 row of token prompt[t * prompt_ld + pos]
+ *                      while pos < prompt_len, else of gen[t]
+ *   fr_argmax_f32      tok[t] = argmax logits[t, :] (ties: lowest index)
+ *   fr_pos_advance     *pos += 1 (the step's last kernel)
+ *   fr_synth_nvfp4_device  NVFP4 rows with the synthetic weight distribution
+ *                      (codes uniform over 0..15, scales e4m3(|N(0,1)| *
+ *                      sigma)), generated on the device for multi-GB models */
+int fr_rmsnorm_f32(const float *x, const float *w, float *y, int T, int H, float eps, cudaStream_t stream);
+int fr_rope_kv_f16(const float *qkv, const int32_t *pos, float *q_r, void *kcache, void *vcache, int T, int nh,
+                   int nkv, int head_dim, int ctx, float rope_base, cudaStream_t stream);
+int fr_attn_decode_f16(const float *q_r, const void *kcache, const void *vcache, const int32_t *pos, float *out,
+                       int T, int nh, int nkv, int head_dim, int ctx, cudaStream_t stream);
+int fr_embed_nvfp4(const void *table, int vocab, int H, const int32_t *prompt, int prompt_ld, int prompt_len,
+                   const int32_t *gen, const int32_t *pos, float *x, int T, cudaStream_t stream);
+int fr_argmax_f32(const float *logits, int T, int V, int32_t *tok, cudaStream_t stream);
+int fr_pos_advance(int32_t *pos, cudaStream_t stream);
+int fr_synth_nvfp4_device(uint64_t seed, int64_t rows, int64_t K, double scale_sigma, void *out,
+                          cudaStream_t stream);
+
 /* ------------------------------------------------------ synthetic inputs
  * Host-side, deterministic (splitmix64 + Box-Muller in double) generator of
  * the benchmark inputs: NVFP4 rows with E2M1 codes uniform over 0..15 and

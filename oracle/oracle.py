@@ -298,3 +298,50 @@ def ref_lib():
         L.frref_sf_bytes.argtypes = [C.c_longlong, C.c_longlong]
         _ref = L
     return _ref
+
+
+# ---------------------------------------------------------------- decode-step restatements (numpy, fp64)
+
+def rmsnorm(x, w=None, eps=1e-6):
+    """RMSNorm as the reference's host check states it (src/fr_win_flint_batched.cuh:468-474):
+    sum of squares in double, scale = 1/sqrt(mean + eps)."""
+    x = np.asarray(x, np.float64)
+    scale = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
+    y = x * scale
+    return y if w is None else y * np.asarray(w, np.float64)
+
+
+def rope_neox(x, pos, base=1e6):
+    """NeoX RoPE of heads x [..., d] at position pos: pairs (i, i + d/2),
+    theta_i = pos * base^(-2i/d) (src/fr_qkv_post.cu:71-131), in fp64."""
+    x = np.asarray(x, np.float64)
+    d = x.shape[-1]
+    i = np.arange(d // 2, dtype=np.float64)
+    th = pos * base ** (-2.0 * i / d)
+    c, s = np.cos(th), np.sin(th)
+    a, b = x[..., : d // 2], x[..., d // 2:]
+    return np.concatenate([a * c - b * s, a * s + b * c], -1)
+
+
+def attention_decode(q, k, v):
+    """Softmax attention of one token's query heads q [nh, d] (already scaled)
+    over keys k, v [nkv, n, d] (GQA: head h reads KV head h // (nh / nkv)),
+    fp64: the decode attention the reference's frt_fa_decode / frt_fa_combine
+    compute (src/fr_win_flint_sm120.cu:2411-2846)."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    nh, nkv = q.shape[0], k.shape[0]
+    out = np.empty_like(q)
+    for h in range(nh):
+        g = h // (nh // nkv)
+        s = k[g] @ q[h]
+        p = np.exp(s - s.max())
+        out[h] = (p @ v[g]) / p.sum()
+    return out
+
+
+def nvfp4_rows(blocks, rows):
+    """Dequantized rows of an NVFP4 matrix (ggml values), f32 [len(rows), K]."""
+    b = np.asarray(blocks, np.uint8)
+    return np.stack([nvfp4_dequant(b[r]) for r in rows])
