@@ -687,6 +687,24 @@ def run_profile_case(args):
             torch.cuda.synchronize()
         print(f"profile case done: {args.steps} GEMMs, M={M}, status {frb200.device_status()}")
         return
+    if args.case == "attn":
+        # decode attention (configs[4] shapes): --tokens sequences, keys
+        # 0..1023 of a 2048-row f16 cache per layer, 4 layers rotating
+        T, nh, nkv, d, ctx = args.tokens, 32, 4, 128, 2048
+        g = torch.Generator(device=dev)
+        g.manual_seed(1)
+        caches = [(torch.randn((T, nkv, ctx, d), generator=g, device=dev).half(),
+                   torch.randn((T, nkv, ctx, d), generator=g, device=dev).half()) for _ in range(4)]
+        q = torch.randn((T, nh, d), generator=g, device=dev) / d ** 0.5
+        out = torch.empty((T, nh * d), dtype=torch.float32, device=dev)
+        pos = torch.tensor([1023], dtype=torch.int32, device=dev)
+        for i in range(args.steps):
+            kc, vc = caches[i % 4]
+            frb200.call("fr_attn_decode_f16", frb200._ptr(q), frb200._ptr(kc), frb200._ptr(vc), frb200._ptr(pos),
+                        frb200._ptr(out), T, nh, nkv, d, ctx, frb200._stream())
+            torch.cuda.synchronize()
+        print(f"profile case done: {args.steps} attention launches, T={T}, status {frb200.device_status()}")
+        return
     if args.case == "moe":
         msets = _moe_sets(frb200, torch, dev, 0, 1, 2)
         if args.layout == "tiled":
@@ -738,7 +756,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step of --profile-case")
     ap.add_argument("--matvec", type=int, default=None, help="force the matvec kernel (1 dp4a, 2 tc-f16, 3 tc-fp4)")
     ap.add_argument("--layout", choices=["ggml", "tiled"], default="ggml", help="weight layout of --profile-case")
-    ap.add_argument("--case", choices=["ffn", "moe", "gemm"], default="ffn", help="workload of --profile-case")
+    ap.add_argument("--case", choices=["ffn", "moe", "gemm", "attn"], default="ffn", help="workload of --profile-case")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)

@@ -95,6 +95,10 @@ struct GvParams {
     // the epilogue runs; null = parity 0)
     const unsigned int *epoch;
     int64_t par_bytes;
+    // q8 input in a double-buffered exchange buffer: q8 + (q8_epoch[0] & 1) *
+    // q8_par (null = q8 as given)
+    const unsigned int *q8_epoch;
+    int64_t q8_par;
 };
 
 // Bounded wait of one lane for flags[r] to reach seen + expect (counters only
@@ -168,6 +172,8 @@ __device__ __forceinline__ void gv_stage_act(const GvParams &p, int4 *act_q, flo
         }
     } else {
         // q8_1 input: every consumer thread moves 4-byte words of the blocks
+        // (from the step-parity half of an exchange buffer when q8_epoch is set)
+        const uint8_t *q8 = p.q8 + (p.q8_epoch ? static_cast<int64_t>(*p.q8_epoch & 1u) * p.q8_par : 0);
         const int tid = warp * 32 + lane;
         const int total = p.nt * nc * 9;
         for (int base = tid; base < total; base += CW * 32 * BATCH) {
@@ -179,7 +185,7 @@ __device__ __forceinline__ void gv_stage_act(const GvParams &p, int4 *act_q, flo
                 if (wi < total) {
                     const int c = wi / 9, k = wi % 9;
                     const int t = c / nc, ch = c % nc;
-                    w[u] = *reinterpret_cast<const uint32_t *>(p.q8 + ((p.t0 + t) * p.ldq + ch) * Q8_BYTES + 4 * k);
+                    w[u] = *reinterpret_cast<const uint32_t *>(q8 + ((p.t0 + t) * p.ldq + ch) * Q8_BYTES + 4 * k);
                 }
             }
 #pragma unroll
@@ -497,13 +503,51 @@ __global__ void __launch_bounds__(256) k_tp_push(uint8_t *const *peer_base, int 
     fr_pdl_trigger();
 }
 
+// Row-sharded tensor parallelism: quantize this rank's GLU columns [T, cols]
+// (f32, row stride ldg) to q8_1 and store the blocks into every rank's copy
+// of the full q8_1 GLU (at byte offset dst_off + (epoch[0] & 1) * par_bytes,
+// rows ldq blocks apart, this rank's blocks from block col0 / 32 on), then
+// count the CTA into every rank's flag[rank] at flag_off.  q8_1 blocks are
+// local to 32 values and shard boundaries are multiples of 64, so the blocks
+// are the ones one GPU quantizing the whole GLU makes.  One warp per block.
+__global__ void __launch_bounds__(256) k_q8_push(const float *__restrict__ glu, int64_t ldg, int T, int cols,
+                                                 int col0, uint8_t *const *peer_base, int npeers, int rank,
+                                                 int64_t dst_off, int64_t par_bytes, const unsigned int *epoch,
+                                                 int64_t ldq, int64_t flag_off) {
+    fr_pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int nc = cols / Q8_ELEMS;
+    const int64_t off = dst_off + static_cast<int64_t>(*epoch & 1u) * par_bytes;
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); c < static_cast<int64_t>(T) * nc;
+         c += static_cast<int64_t>(gridDim.x) * 8) {
+        const int t = static_cast<int>(c / nc), ch = static_cast<int>(c % nc);
+        const q8_lane r = q8_1_chunk(glu[t * ldg + static_cast<int64_t>(ch) * Q8_ELEMS + lane]);
+        const __half2 ds = __halves2half2(__float2half_rn(r.d), __float2half_rn(r.sum));
+        const int64_t boff = off + (t * ldq + col0 / Q8_ELEMS + ch) * Q8_BYTES;
+        for (int q = 0; q < npeers; ++q) {
+            uint8_t *blk = peer_base[q] + boff;
+            blk[4 + lane] = static_cast<uint8_t>(r.q);
+            if (lane == 0) *reinterpret_cast<__half2 *>(blk) = ds;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < npeers; ++q)
+            atomicAdd_system(reinterpret_cast<unsigned int *>(peer_base[q] + flag_off) + rank, 1u);
+    }
+    fr_pdl_trigger();
+}
+
 // Tensor-parallel completion wait and reduction: in every CTA, lane r waits
 // until rank r's flag counter reached this CTA's consumed count plus `expect`
 // (the producer kernels' CTA count) and records the new count in the CTA's
 // own row of `seen` (seen[blockIdx.x * 32 + r]; counters only grow, so
 // CUDA-graph replays need no reset).  Then the CTA sums its slice of the
 // ranks' partial outputs in rank order (identical on every rank), adds the
-// residual and writes `out`.  The wait is bounded (status bit 0, site 30).
+// residual and writes `out` (nsum slots are summed: nranks for the partial
+// sums of the n_ff-sharded form, 1 for an output the ranks assembled by
+// columns).  The wait is bounded (status bit 0, site 30).
 //
 // Step parity (epoch non-null): the partial outputs are double-buffered.
 // epoch[blockIdx.x] counts this CTA's completed steps; a step reads the half
@@ -521,7 +565,7 @@ __global__ void __launch_bounds__(256) k_tp_push(uint8_t *const *peer_base, int 
 __global__ void __launch_bounds__(256) k_tp_reduce(const unsigned int *flags, unsigned int *seen, int nranks,
                                                    unsigned int expect, const float *parts, int64_t n,
                                                    const float *resid, int64_t ldr, int64_t width, float *out,
-                                                   int64_t ldo, unsigned int *epoch, int64_t par_floats) {
+                                                   int64_t ldo, unsigned int *epoch, int64_t par_floats, int nsum) {
     fr_pdl_trigger();
     fr_pdl_wait();
     const unsigned int e = epoch ? epoch[blockIdx.x] : 0u;
@@ -533,7 +577,7 @@ __global__ void __launch_bounds__(256) k_tp_reduce(const unsigned int *flags, un
     const int64_t lo = blockIdx.x * per, hi = min(n, lo + per);
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         float v = parts[i];
-        for (int r = 1; r < nranks; ++r) v += parts[r * n + i];
+        for (int r = 1; r < nsum; ++r) v += parts[r * n + i];
         const int64_t t = i / width, c = i % width;
         if (resid) v += resid[t * ldr + c];
         out[t * ldo + c] = v;

@@ -2127,7 +2127,7 @@ static int ep_moe_impl(const float *x, const float *w_r, const void *wg_local, c
                     reinterpret_cast<unsigned int *>(base + L.seen_d), nranks, static_cast<unsigned>(EP_CTAS),
                     static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<const float *>(nullptr),
                     static_cast<int64_t>(0), static_cast<int64_t>(1), static_cast<float *>(nullptr),
-                    static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr), static_cast<int64_t>(0));
+                    static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr), static_cast<int64_t>(0), 1);
     if (rc != FR_OK) return rc;
     // this rank's experts over everything it received (empty slots skipped)
     if (tiled)
@@ -2148,7 +2148,7 @@ static int ep_moe_impl(const float *x, const float *w_r, const void *wg_local, c
                     reinterpret_cast<unsigned int *>(base + L.seen_r), nranks, static_cast<unsigned>(EP_CTAS),
                     static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<const float *>(nullptr),
                     static_cast<int64_t>(0), static_cast<int64_t>(1), static_cast<float *>(nullptr),
-                    static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr), static_cast<int64_t>(0));
+                    static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr), static_cast<int64_t>(0), 1);
     if (rc != FR_OK) return rc;
     return launch_pdl(k_moe_combine, dim3((n_embd + 255) / 256, T), dim3(256), 0, stream,
                       reinterpret_cast<const float *>(base + L.back), static_cast<const float *>(wts), resid, out,
@@ -2337,7 +2337,7 @@ static int tp_ffn_impl(const float *x, const void *wg_shard, const void *wu_shar
     // Always TP_WAIT_CTAS CTAs: each keeps its own consumed count.
     return launch_pdl(k_tp_reduce, dim3(TP_WAIT_CTAS), dim3(256), 0, stream, flags, seen, nranks, expect, parts,
                       n_out, resid, static_cast<int64_t>(n_embd), static_cast<int64_t>(n_embd), out,
-                      static_cast<int64_t>(n_embd), epoch, L.half / 4);
+                      static_cast<int64_t>(n_embd), epoch, L.half / 4, nranks);
 }
 
 } // namespace frb
@@ -2358,7 +2358,7 @@ int fr_tp_wait(void *local_base, int64_t buffer_bytes, int n_embd, int nranks, u
                       static_cast<const float *>(nullptr), static_cast<int64_t>(0),
                       static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<int64_t>(1),
                       static_cast<float *>(nullptr), static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr),
-                      static_cast<int64_t>(0));
+                      static_cast<int64_t>(0), 1);
 }
 
 int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard, const float *sg,
@@ -2368,6 +2368,139 @@ int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, 
     if (fault_hit("fr_tp_ffn_nvfp4")) return FR_EINJECTED;
     return tp_ffn_impl(x, wg_shard, wu_shard, wd_shard, sg, su, sd, resid, out, T, n_embd, n_ff, nranks, rank,
                        peer_base, local_base, buffer_bytes, false, stream);
+}
+
+} // extern "C"
+
+namespace frb {
+// Row-sharded tensor-parallel FFN buffer: [flags of the GLU exchange 32]
+// [flags of the output exchange 32] u32, per-CTA consumed counts of both
+// [TP_WAIT_CTAS][32] and step counts [TP_WAIT_CTAS], then two parity halves,
+// each [T_cap][n_ff / 32] q8_1 blocks of the GLU followed (256-aligned) by
+// [T_cap][n_embd] f32 of the output; capacity from the buffer's size.
+struct TpRowsLayout {
+    int64_t flags_g, flags_o, seen_g, seen_o, epoch, part, q8, out, half, total, t_cap;
+};
+static int64_t tpr_hdr() {
+    return (4LL * 64 + 2 * 4LL * 32 * TP_WAIT_CTAS + 4LL * TP_WAIT_CTAS + 255) / 256 * 256;
+}
+static int64_t tpr_half(int64_t t_cap, int n_embd, int n_ff) {
+    const int64_t q8 = (t_cap * (n_ff / 32) * Q8_BYTES + 255) / 256 * 256;
+    return q8 + t_cap * n_embd * 4;
+}
+static TpRowsLayout tpr_layout_cap(int64_t t_cap, int n_embd, int n_ff) {
+    TpRowsLayout l{};
+    l.flags_g = 0;
+    l.flags_o = 4LL * 32;
+    l.seen_g = 4LL * 64;
+    l.seen_o = l.seen_g + 4LL * 32 * TP_WAIT_CTAS;
+    l.epoch = l.seen_o + 4LL * 32 * TP_WAIT_CTAS;
+    l.part = tpr_hdr();
+    l.t_cap = t_cap;
+    l.half = tpr_half(t_cap, n_embd, n_ff);
+    l.q8 = 0;
+    l.out = (t_cap * (n_ff / 32) * Q8_BYTES + 255) / 256 * 256;
+    l.total = l.part + 2 * l.half;
+    return l;
+}
+static TpRowsLayout tpr_layout_buf(int64_t bytes, int n_embd, int n_ff) {
+    int64_t t = 0;
+    while (t < (1 << 16) && tpr_layout_cap(t + 1, n_embd, n_ff).total <= bytes) ++t;
+    return tpr_layout_cap(t, n_embd, n_ff);
+}
+} // namespace frb
+
+extern "C" {
+
+int64_t fr_tp_rows_buffer_bytes(int T, int n_embd, int n_ff, int nranks) {
+    if (T <= 0 || n_embd <= 0 || n_ff <= 0 || nranks <= 0) return -1;
+    return tpr_layout_cap(T, n_embd, n_ff).total;
+}
+
+int fr_tp_ffn_rows(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard, const float *sg,
+                   const float *su, const float *sd, const float *resid, float *out, int T, int n_embd, int n_ff,
+                   int nranks, int rank, void *const *peer_base, void *local_base, int64_t buffer_bytes,
+                   cudaStream_t stream) {
+    if (fault_hit("fr_tp_ffn_rows")) return FR_EINJECTED;
+    if (!x || !wg_shard || !wu_shard || !wd_shard || !out || !peer_base || !local_base) return FR_EINVAL;
+    if (T <= 0 || nranks <= 0 || nranks > 32 || rank < 0 || rank >= nranks) return FR_EINVAL;
+    if (n_embd % 64 != 0 || n_ff % 64 != 0 || n_ff % (64 * nranks) != 0 || n_embd % nranks != 0) return FR_EINVAL;
+    const TpRowsLayout L = tpr_layout_buf(buffer_bytes, n_embd, n_ff);
+    if (T > L.t_cap) return FR_EINVAL;
+    uint8_t *base = static_cast<uint8_t *>(local_base);
+    uint8_t *const *pb = reinterpret_cast<uint8_t *const *>(peer_base);
+    unsigned int *epoch = reinterpret_cast<unsigned int *>(base + L.epoch);
+    const int F_p = n_ff / nranks, E_p = n_embd / nranks;
+    const int64_t ld_gu = static_cast<int64_t>(n_embd) / 64 * NV_BYTES;
+    const int64_t ld_d = static_cast<int64_t>(n_ff) / 64 * NV_BYTES;
+    void *q8x = nullptr, *glu_p = nullptr;
+    int rc = workspace_get(WS_Q8, static_cast<size_t>(T) * (n_embd / 32) * Q8_BYTES, stream, &q8x);
+    if (rc != FR_OK) return rc;
+    rc = workspace_get(WS_GLU, static_cast<size_t>(T) * F_p * sizeof(float), stream, &glu_p);
+    if (rc != FR_OK) return rc;
+    float *glu = static_cast<float *>(glu_p);
+    // q8_1(x) on every rank (identical bits), then this rank's GLU columns
+    rc = quantize_launch(x, n_embd, q8x, n_embd / 32, T, n_embd, stream);
+    if (rc != FR_OK) return rc;
+    GvParams p{};
+    p.w0 = static_cast<const uint8_t *>(wg_shard);
+    p.w1 = static_cast<const uint8_t *>(wu_shard);
+    p.w_ld = ld_gu;
+    p.q8 = static_cast<const uint8_t *>(q8x);
+    p.ldq = n_embd / 32;
+    p.s0 = sg;
+    p.s1 = su;
+    p.y = glu;
+    p.ldy = F_p;
+    p.N = F_p;
+    p.K = n_embd;
+    rc = gemv_run(p, T, true, stream);
+    if (rc != FR_OK) return rc;
+    // all-gather of the GLU as q8_1 blocks: every rank's blocks into every rank
+    constexpr int PUSH_CTAS = 64;
+    rc = launch_pdl(k_q8_push, dim3(PUSH_CTAS), dim3(256), 0, stream, static_cast<const float *>(glu),
+                    static_cast<int64_t>(F_p), T, F_p, rank * F_p, pb, nranks, rank, L.part + L.q8, L.half,
+                    static_cast<const unsigned int *>(epoch), static_cast<int64_t>(n_ff / 32), L.flags_g);
+    if (rc != FR_OK) return rc;
+    rc = launch_pdl(k_tp_reduce, dim3(TP_WAIT_CTAS), dim3(256), 0, stream,
+                    reinterpret_cast<const unsigned int *>(base + L.flags_g),
+                    reinterpret_cast<unsigned int *>(base + L.seen_g), nranks, static_cast<unsigned>(PUSH_CTAS),
+                    static_cast<const float *>(nullptr), static_cast<int64_t>(0), static_cast<const float *>(nullptr),
+                    static_cast<int64_t>(0), static_cast<int64_t>(1), static_cast<float *>(nullptr),
+                    static_cast<int64_t>(0), static_cast<unsigned int *>(nullptr), static_cast<int64_t>(0), 1);
+    if (rc != FR_OK) return rc;
+    // this rank's output rows over the whole GLU, stored into column block
+    // rank * E_p of every rank's output (the output all-gather)
+    GvParams q{};
+    q.w0 = static_cast<const uint8_t *>(wd_shard);
+    q.w_ld = ld_d;
+    q.q8 = base + L.part + L.q8;
+    q.q8_epoch = epoch;
+    q.q8_par = L.half;
+    q.ldq = n_ff / 32;
+    q.s0 = sd;
+    q.y = nullptr;
+    q.ldy = n_embd;
+    q.N = E_p;
+    q.K = n_ff;
+    q.peer_base = pb;
+    q.npeers = nranks;
+    q.rank = rank;
+    q.peer_off = L.part + L.out;
+    q.flag_off = L.flags_o;
+    q.col_off = static_cast<int64_t>(rank) * E_p;
+    q.epoch = epoch;
+    q.par_bytes = L.half;
+    rc = gemv_run(q, T, false, stream);
+    if (rc != FR_OK) return rc;
+    const unsigned expect = gemv_ctas(E_p, n_ff, ld_d, T, false);
+    // wait for every rank's column block, add the residual, advance the parity
+    return launch_pdl(k_tp_reduce, dim3(TP_WAIT_CTAS), dim3(256), 0, stream,
+                      reinterpret_cast<const unsigned int *>(base + L.flags_o),
+                      reinterpret_cast<unsigned int *>(base + L.seen_o), nranks, expect,
+                      reinterpret_cast<const float *>(base + L.part + L.out), static_cast<int64_t>(T) * n_embd,
+                      resid, static_cast<int64_t>(n_embd), static_cast<int64_t>(n_embd), out,
+                      static_cast<int64_t>(n_embd), epoch, L.half / 4, 1);
 }
 
 int fr_tp_ffn_tiled(const float *x, const void *wg_t, const void *wu_t, const void *wd_t, const float *sg,

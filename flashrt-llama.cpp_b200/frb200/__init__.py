@@ -67,6 +67,9 @@ SIGNATURES = {
                                 C.c_float, _vp, _vp, _vp, _vp, _vp]),
     "fr_tp_buffer_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "fr_tp_wait": (_i32, [_vp, _i64, _i32, _i32, C.c_uint32, _vp]),
+    "fr_tp_rows_buffer_bytes": (_i64, [_i32, _i32, _i32, _i32]),
+    "fr_tp_ffn_rows": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
+                              _i64, _vp]),
     "fr_tp_ffn_nvfp4": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                _i64, _vp]),
     "fr_tp_ffn_tiled": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp,

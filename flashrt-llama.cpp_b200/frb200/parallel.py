@@ -181,6 +181,38 @@ class TpFfn(_PeerBuffer):
         return out
 
 
+class TpFfnRows(_PeerBuffer):
+    """Tensor-parallel dense FFN row-sharded over the ranks (fr_tp_ffn_rows):
+    gate/up rows and down rows sharded, the q8_1 GLU and the output
+    all-gathered by NVLink peer stores with bounded waits; bit-identical to
+    the single-GPU dp4a FFN.  Weights: `row_shards` of the full matrices."""
+
+    def __init__(self, max_tokens, n_embd, n_ff, group=None):
+        world = dist.get_world_size(group)
+        super().__init__(lib().fr_tp_rows_buffer_bytes(max_tokens, n_embd, n_ff, world), group)
+        self.n_embd, self.n_ff, self.max_tokens = n_embd, n_ff, max_tokens
+
+    def __call__(self, x, wg_shard, wu_shard, wd_shard, sg=None, su=None, sd=None, resid=None, out=None,
+                 stream=None):
+        import torch
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > buffer capacity {self.max_tokens}")
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
+        call("fr_tp_ffn_rows", _ptr(x), _ptr(wg_shard), _ptr(wu_shard), _ptr(wd_shard), _ptr(sg), _ptr(su),
+             _ptr(sd), _ptr(resid), _ptr(out), T, self.n_embd, self.n_ff, self.world, self.rank,
+             _ptr(self.peer_ptrs), C.c_void_p(self.local), self.nbytes, _stream(stream))
+        return out
+
+
+def row_shards(wg, wu, wd, n_embd, n_ff, rank, world):
+    """This rank's rows of the gate/up [n_ff, .] and down [n_embd, .] matrices."""
+    f0, f1 = shard_range(n_ff, rank, world)
+    e0, e1 = shard_range(n_embd, rank, world)
+    return wg[f0:f1].contiguous(), wu[f0:f1].contiguous(), wd[e0:e1].contiguous()
+
+
 class EpMoe(_PeerBuffer):
     """Expert-parallel MoE layer over NVLink peer stores (fr_ep_moe_nvfp4):
     this rank's E/P experts, its own tokens; routed rows go to the expert

@@ -313,6 +313,26 @@ int fr_tp_ffn_nvfp4(const float *x, const void *wg_shard, const void *wu_shard, 
                     int T, int n_embd, int n_ff, int nranks, int rank,
                     void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream);
 
+/* The dense FFN row-sharded over P ranks -- the partitioning BASELINE's
+ * north star names: rank r holds gate/up rows [r F_p, (r+1) F_p) (F_p = n_ff
+ * / P) and down rows [r E_p, (r+1) E_p) (E_p = n_embd / P, each row over the
+ * whole n_ff).  q8_1(x) is computed on every rank; each rank's GLU columns
+ * are quantized to q8_1 and stored into every rank's copy of the full q8_1
+ * GLU over NVLink (the all-gather of the GLU, 3.6x smaller than f32 and
+ * exact: q8_1 blocks never straddle a shard); a bounded wait; each rank's
+ * output rows go into column block r of every rank's output (the output
+ * all-gather); a second bounded wait adds the residual.  Every output value
+ * is one row's dot product on one GPU, so the result equals one GPU's dp4a
+ * FFN bit for bit.  The exchange buffers are double-buffered by step parity
+ * as for fr_tp_ffn_nvfp4; a buffer of fr_tp_rows_buffer_bytes(T_max, ...)
+ * bytes per rank, zeroed once; all ranks call with the same T <= T_max.
+ * n_ff % (64 P) == 0, n_embd % 64 == 0, n_embd % P == 0. */
+int64_t fr_tp_rows_buffer_bytes(int T, int n_embd, int n_ff, int nranks);
+int fr_tp_ffn_rows(const float *x, const void *wg_shard, const void *wu_shard, const void *wd_shard,
+                   const float *sg, const float *su, const float *sd, const float *resid, float *out,
+                   int T, int n_embd, int n_ff, int nranks, int rank,
+                   void *const *peer_base, void *local_base, int64_t buffer_bytes, cudaStream_t stream);
+
 /* ------------------------------------------------------ (e) expert parallel
  * One rank's step of the MoE layer with E/P experts per rank (rank r owns
  * experts [r*E/P, (r+1)*E/P); wg/wu/wd_local hold their rows) and its own T

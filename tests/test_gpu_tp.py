@@ -144,6 +144,30 @@ def _worker(rank, world, port, q):
                 if not torch.equal(ys[i], yr[i]):
                     bad.append(f"chained {name} step {i}: differs from the synchronised step by "
                                f"{float((ys[i] - yr[i]).abs().max()):.3e}")
+        # the row-sharded form (north-star partitioning): equal to the
+        # single-GPU dp4a FFN bit for bit, chained steps included
+        frb200.set_matvec_path(1)
+        tpr = P.TpFfnRows(8, ne, nf)
+        tps.append(tpr)
+        rsh = P.row_shards(wg, wu, wd, ne, nf, rank, world)
+        yrow = [torch.empty((T, ne), dtype=torch.float32, device=dev) for T in (1, 3, 8, 2, 8, 5)]
+        xrow = [t(frb200.synth_normal(300 + i, y.shape[0] * ne).reshape(y.shape[0], ne)) for i, y in enumerate(yrow)]
+        rrow = [t(frb200.synth_normal(320 + i, y.shape[0] * ne).reshape(y.shape[0], ne)) for i, y in enumerate(yrow)]
+        torch.cuda.synchronize()
+        dist.barrier()
+        with torch.cuda.stream(s):
+            for i, (x, r, y) in enumerate(zip(xrow, rrow, yrow)):
+                if rank == world - 1 and i % 2 == 1:
+                    torch.cuda._sleep(2_000_000)
+                tpr(x, *rsh, resid=r, out=y, stream=s, **(dict(sg=sc[0:1], su=sc[1:2], sd=sc[2:3]) if i == 4 else {}))
+        s.synchronize()
+        for i, (x, r, y) in enumerate(zip(xrow, rrow, yrow)):
+            kw = dict(sg=sc[0:1], su=sc[1:2], sd=sc[2:3]) if i == 4 else {}
+            ref = frb200.ffn(x, wg, wu, wd, ne, nf, resid=r, **kw)
+            torch.cuda.synchronize()
+            sums.append(float(y.double().sum()))
+            if not torch.equal(y, ref):
+                bad.append(f"rows-sharded step {i}: differs from one GPU by {float((y - ref).abs().max()):.3e}")
         frb200.set_matvec_path(0)
         q.put((rank, bad, frb200.device_status(), sums))
     except Exception as e:  # noqa: BLE001 - report to the parent instead of hanging it
