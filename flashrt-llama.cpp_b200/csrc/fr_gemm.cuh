@@ -14,12 +14,14 @@
 //   * tile 128 x 256 (one block-scaled MMA of N = 256 per 64-value K block:
 //     half the MMA issues and a third less operand traffic per FLOP than a
 //     128 x 128 tile), K stage 256 values, 4-stage TMA ring of 54 KB stages;
-//   * persistent: one CTA per SM, the (tile, K stage) units divided evenly
-//     over the CTAs (stream-K), so every SM gets the same work whatever the
-//     tile count; a tile split between CTAs is finished by the last of them
-//     to arrive, which adds the partial accumulators in CTA order
-//     (deterministic) -- each CTA owns two partial slots (its first and last
-//     segment), so the workspace is fixed by the grid, not by the problem;
+//   * schedule: with at least as many tiles as SMs, one CTA per SM takes whole
+//     tiles c, c + grid, ... (no partial sum is ever written); with fewer,
+//     every tile is split into S = SMs / tiles equal K ranges on S CTAs, and
+//     the last of them to arrive adds the S partials in K-range order
+//     (deterministic), each CTA owning one partial slot.  (A stream-K
+//     division of the units over the SMs was measured and dropped: the
+//     partial traffic at the end of the kernel cost 15-20 us on configs[3]'s
+//     shapes);
 //   * warp roles: warpgroup 0 = warp 0 TMA producer, warp 1 MMA issuer (and
 //     TMEM owner), warps 2-3 idle; warpgroups 1-2 = epilogue warps 4..11
 //     (lane quadrant = warp % 4, 128-column half = (warp - 4) / 4), which
@@ -29,7 +31,10 @@
 //     8 x 32 x 232 = 64,512 = 384 threads x 168 at launch (ptxas -v);
 //   * scale factors: per stage one 512-byte atom per 64-value K block for A
 //     and two for B (rows 0..127 and 128..255 of the tile), tcgen05.cp'd into
-//     TMEM columns of that stage (SFA: 4 columns, SFB: 8 columns per block);
+//     TMEM columns of that stage (SFA: 4 columns, SFB: 8 columns per block) by
+//     two copier threads (warps 2 and 3, alternate stages), which hand the
+//     stage to the MMA thread through an mbarrier: twelve copies cost an
+//     issuing thread more than the stage's four MMAs;
 //   * every wait is bounded (status word, sites 40..45) and a CTA that gave up
 //     waits for its own copies in flight before it exits.
 #pragma once
@@ -63,22 +68,37 @@ struct PGemmArgs {
     int M, N, K;                 // N = rows of B (the SwiGLU output has N/2 columns)
     int nkt;                     // K stages of 256
     int n_m, n_n;                // tiles along M and N
-    int64_t units;               // tiles x nkt
+    int tiles;
+    int split;                   // 0: whole tiles (CTA c takes tiles c, c + grid, ...);
+                                 // S > 0: grid = tiles * S, CTA c takes K range c % S of tile c / S
     float alpha;
-    float *part;                 // [grid][2][128][256] partial accumulators
+    float *part;                 // [grid][128 x 256] partial accumulators (split mode)
     unsigned int *counter;       // [tiles], zero on entry, reset by the last arrival
 };
 
-// units [u0(c), u0(c+1)) belong to CTA c
-__device__ __forceinline__ int64_t p_u0(int64_t c, int64_t U, int64_t G) { return c * U / G; }
-
-// the CTA whose unit range holds unit u
-__device__ __forceinline__ int p_owner(int64_t u, int64_t U, int64_t G) {
-    int64_t c = (u * G) / U;
-    while (c + 1 < G && p_u0(c + 1, U, G) <= u) ++c;
-    while (c > 0 && p_u0(c, U, G) > u) --c;
-    return static_cast<int>(c);
-}
+// The (tile, K range) segments of one CTA, in order.  Whole tiles when there
+// are at least as many tiles as CTAs (no partial ever written); otherwise
+// every tile split into S equal K ranges on S consecutive CTAs.
+struct PSegIter {
+    int c, G, nkt, tiles, S, i;
+    __device__ __forceinline__ bool next(int &t, int &kt0, int &kt1) {
+        if (S == 0) {
+            t = c + i * G;
+            if (t >= tiles) return false;
+            kt0 = 0;
+            kt1 = nkt;
+            ++i;
+            return true;
+        }
+        if (i > 0) return false;
+        ++i;
+        t = c / S;
+        const int s = c % S;
+        kt0 = static_cast<int>(static_cast<int64_t>(s) * nkt / S);
+        kt1 = static_cast<int>(static_cast<int64_t>(s + 1) * nkt / S);
+        return t < tiles && kt1 > kt0;
+    }
+};
 
 // tile t -> (m block, n block): consecutive tiles share their B tile, so the
 // CTAs working on them at the same time read it from HBM once
@@ -173,15 +193,14 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE);
     uint64_t *empty = full + P_STAGES;
-    uint64_t *acc_full = empty + P_STAGES;
+    uint64_t *sf_ready = empty + P_STAGES;              // the stage's scale factors are in TMEM
+    uint64_t *acc_full = sf_ready + P_STAGES;
     uint64_t *acc_empty = acc_full + 1;
     uint64_t *epi_done = acc_empty + 1;                // every epilogue warp is past its last TMEM read
     uint32_t *tmem_s = reinterpret_cast<uint32_t *>(epi_done + 1);
     volatile int *bcast = reinterpret_cast<volatile int *>(tmem_s + 1);     // [4]: last arrival, lo, hi, abort
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t U = g.units, G = gridDim.x;
-    const int64_t u_begin = p_u0(blockIdx.x, U, G), u_end = p_u0(blockIdx.x + 1, U, G);
     const int nkt = g.nkt;
     const int kb_total = g.K >> 6;
     const int n_rb_b = (g.N + 127) >> 7;
@@ -190,6 +209,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
         for (int s = 0; s < P_STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&sf_ready[s], 1);
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, P_EPI_WARPS);
@@ -214,10 +234,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
             // ---------------- producer: A / B tiles by TMA, scale atoms by bulk copies
             int64_t it = 0;
             bool ok = true;
-            for (int64_t u = u_begin; u < u_end && ok;) {
-                const int t = static_cast<int>(u / nkt);
-                const int kt0 = static_cast<int>(u % nkt);
-                const int kt1 = static_cast<int>(min(static_cast<int64_t>(nkt), kt0 + (u_end - u)));
+            PSegIter sg{static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), nkt, g.tiles, g.split, 0};
+            int t, kt0, kt1;
+            while (ok && sg.next(t, kt0, kt1)) {
                 int mb, nb;
                 p_tile_mn(g, t, mb, nb);
                 const uint8_t *sfa_blk = g.sfa + static_cast<int64_t>(mb) * kb_total * 512;
@@ -241,7 +260,6 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
                     bulk_g2s(sf + P_SFA_BYTES, sfb0 + static_cast<int64_t>(4 * kt) * 512, kbs * 512, &full[s]);
                     bulk_g2s(sf + P_SFA_BYTES + 2048, sfb1 + static_cast<int64_t>(4 * kt) * 512, kbs * 512, &full[s]);
                 }
-                u += kt1 - kt0;
             }
             // nothing of this CTA's may still be landing when it exits: wait
             // (bounded) for the last stages issued
@@ -255,16 +273,18 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
             int64_t it = 0;
             int seg = 0;
             bool ok = true;
-            for (int64_t u = u_begin; u < u_end; ++seg) {
-                const int kt0 = static_cast<int>(u % nkt);
-                const int kt1 = static_cast<int>(min(static_cast<int64_t>(nkt), kt0 + (u_end - u)));
+            PSegIter sg{static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), nkt, g.tiles, g.split, 0};
+            int t, kt0, kt1;
+            for (; sg.next(t, kt0, kt1); ++seg) {
                 if (seg > 0 && ok) {
                     ok = mbar_wait(acc_empty, static_cast<uint32_t>(seg - 1) & 1u, 42);
                     tc_fence_after();
                 }
                 for (int kt = kt0; kt < kt1 && ok; ++kt, ++it) {
                     const int s = static_cast<int>(it % P_STAGES);
-                    if (!mbar_wait(&full[s], static_cast<uint32_t>(it / P_STAGES) & 1u, 43)) {
+                    // the stage's operands landed and a copier thread put
+                    // its scale factors into TMEM
+                    if (!mbar_wait(&sf_ready[s], static_cast<uint32_t>(it / P_STAGES) & 1u, 43)) {
                         ok = false;
                         break;
                     }
@@ -272,14 +292,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
                     const int kbs = min(4, kb_total - 4 * kt);
                     uint8_t *st = smem + s * P_STAGE;
                     const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + P_A_BYTES);
-                    const uint32_t sfa_addr = smem_u32(st + P_A_BYTES + P_B_BYTES);
-                    const uint32_t sfb_addr = sfa_addr + P_SFA_BYTES;
                     const uint32_t t_sfa = tbase + 256 + static_cast<uint32_t>(s) * 48, t_sfb = t_sfa + 16;
-                    for (int j = 0; j < kbs; ++j) {
-                        tc_cp_sf(t_sfa + 4 * j, sdesc_plain(sfa_addr + 512 * j, 128));
-                        tc_cp_sf(t_sfb + 8 * j, sdesc_plain(sfb_addr + 512 * j, 128));
-                        tc_cp_sf(t_sfb + 8 * j + 4, sdesc_plain(sfb_addr + 2048 + 512 * j, 128));
-                    }
                     for (int j = 0; j < kbs; ++j)
                         tc_mma_nvf4(tbase, sdesc_sw128(a_addr + 32 * j), sdesc_sw128(b_addr + 32 * j), idesc,
                                     t_sfa + 4 * j, t_sfb + 8 * j, (kt > kt0 || j > 0) ? 1u : 0u);
@@ -288,7 +301,41 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
                 // always signal the segment, so the epilogue never waits on a
                 // producer or issuer that gave up (the status word says so)
                 tc_commit(acc_full);
-                u += kt1 - kt0;
+            }
+        }
+    } else if (warp == 2 || warp == 3) {
+        if (lane == 0) {
+            // ---------------- scale-factor copiers: each tcgen05.cp costs its
+            // issuing thread ~45 ns, twelve per stage -- more than the
+            // stage's four MMAs -- so two threads copy alternate stages'
+            // atoms into that stage's TMEM columns while the MMA thread
+            // issues, and signal it through sf_ready
+            const int cid = warp - 2;
+            int64_t it = 0;
+            bool ok = true;
+            PSegIter sg{static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), nkt, g.tiles, g.split, 0};
+            int t, kt0, kt1;
+            while (ok && sg.next(t, kt0, kt1)) {
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    if ((it & 1) != cid) continue;
+                    const int s = static_cast<int>(it % P_STAGES);
+                    if (!mbar_wait(&full[s], static_cast<uint32_t>(it / P_STAGES) & 1u, 46)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int kbs = min(4, kb_total - 4 * kt);
+                    uint8_t *st = smem + s * P_STAGE;
+                    const uint32_t sfa_addr = smem_u32(st + P_A_BYTES + P_B_BYTES);
+                    const uint32_t sfb_addr = sfa_addr + P_SFA_BYTES;
+                    const uint32_t t_sfa = tbase + 256 + static_cast<uint32_t>(s) * 48, t_sfb = t_sfa + 16;
+                    for (int j = 0; j < kbs; ++j) {
+                        tc_cp_sf(t_sfa + 4 * j, sdesc_plain(sfa_addr + 512 * j, 128));
+                        tc_cp_sf(t_sfb + 8 * j, sdesc_plain(sfb_addr + 512 * j, 128));
+                        tc_cp_sf(t_sfb + 8 * j + 4, sdesc_plain(sfb_addr + 2048 + 512 * j, 128));
+                    }
+                    tc_commit(&sf_ready[s]);
+                }
             }
         }
     } else if (warp >= 4) {
@@ -300,10 +347,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
         float *stg = reinterpret_cast<float *>(smem + P_STAGES * P_STAGE + 256) + (warp - 4) * P_STG_FLOATS;
         const bool leader = threadIdx.x == 128;
         int seg = 0;
-        for (int64_t u = u_begin; u < u_end; ++seg) {
-            const int t = static_cast<int>(u / nkt);
-            const int kt0 = static_cast<int>(u % nkt);
-            const int kt1 = static_cast<int>(min(static_cast<int64_t>(nkt), kt0 + (u_end - u)));
+        PSegIter sg{static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), nkt, g.tiles, g.split, 0};
+        int t, kt0, kt1;
+        for (; sg.next(t, kt0, kt1); ++seg) {
             int mb, nb;
             p_tile_mn(g, t, mb, nb);
             const int n0 = nb * P_BN;
@@ -332,7 +378,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
                 // CTA's partial in its slot (0: first segment, 1: last one),
                 // laid out [warp block][column / 4][row][4] so that the
                 // warp's stores (and the merging loads) are 512-byte lines
-                float *slot = g.part + (static_cast<int64_t>(blockIdx.x) * 2 + (u == u_begin ? 0 : 1)) * P_SLOT_FLOATS;
+                float *slot = g.part + static_cast<int64_t>(blockIdx.x) * P_SLOT_FLOATS;
                 float4 *blk = reinterpret_cast<float4 *>(slot + wb * (32 * P_CW)) + lane;
 #pragma unroll
                 for (int i = 0; i < P_CW / 4; ++i)
@@ -340,8 +386,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
                 fence_acq_rel_gpu();
                 named_bar(1, P_EPI_WARPS * 32);
                 if (leader) {
-                    const int c_lo = p_owner(static_cast<int64_t>(t) * nkt, U, G);
-                    const int c_hi = p_owner(static_cast<int64_t>(t) * nkt + nkt - 1, U, G);
+                    const int c_lo = t * g.split, c_hi = t * g.split + g.split - 1;
                     const unsigned prev = atomicAdd(&g.counter[t], 1u);
                     const bool last = prev == static_cast<unsigned>(c_hi - c_lo);
                     if (last) g.counter[t] = 0u;            // every contributor has arrived: ready for the next call
@@ -367,9 +412,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
 #pragma unroll
                             for (int j = 0; j < 2; ++j) {
                                 const int c = min(c0 + j, c_hi);           // a spare slot re-reads the last
-                                const int sl = (p_u0(c, U, G) / nkt == t) ? 0 : 1;
                                 const float4 *src = reinterpret_cast<const float4 *>(
-                                                        g.part + (static_cast<int64_t>(c) * 2 + sl) * P_SLOT_FLOATS +
+                                                        g.part + static_cast<int64_t>(c) * P_SLOT_FLOATS +
                                                         wb * (32 * P_CW)) + (ch / 4) * 32 + lane;
 #pragma unroll
                                 for (int i = 0; i < 8; ++i) w[j][i] = __ldcg(src + i * 32);
@@ -393,7 +437,6 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
                     }
                 }
             }
-            u += kt1 - kt0;
         }
         tc_fence_before();
         __syncwarp();

@@ -220,20 +220,29 @@ static GvPlan gv_plan(int N, int K, int64_t w_ld, int T, bool dual) {
         nt = nt / 2;
     pl.TT = pow2_tokens(nt);
     const size_t act = gv_act_bytes(nt, K);
+    const int sms = std::max(1, di.sms);
+    pl.rows_per_cta = (N + sms - 1) / sms;
+    pl.grid = (N + pl.rows_per_cta - 1) / pl.rows_per_cta;
+    // the largest stage (<= 80 KB, two fit) that still gives the CTA at least
+    // two stages, so its first rows are decoded while the rest arrive
     pl.R2 = 1;
     if (pl.TT <= 2) {
         for (int r2 : {4, 2}) {
             const long st = static_cast<long>(CW) * gpw * r2 * row_bytes;
-            if (st <= 80 * 1024 && 2 * st + 2048 + static_cast<long>(act) <= smem_cap) { pl.R2 = r2; break; }
+            if (st <= 80 * 1024 && 2 * st + 2048 + static_cast<long>(act) <= smem_cap &&
+                pl.rows_per_cta >= 2 * CW * gpw * r2) {
+                pl.R2 = r2;
+                break;
+            }
         }
     }
     pl.SR = CW * gpw * pl.R2;
     pl.slot_bytes = static_cast<int>((pl.SR * row_bytes + 15) / 16 * 16);
     const long budget = smem_cap - 2048 - static_cast<long>(act);
-    pl.n_slots = static_cast<int>(std::max(1L, std::min(8L, budget / pl.slot_bytes)));
-    const int sms = std::max(1, di.sms);
-    pl.rows_per_cta = (N + sms - 1) / sms;
-    pl.grid = (N + pl.rows_per_cta - 1) / pl.rows_per_cta;
+    // no more ring slots than the CTA has stages: a small matvec then leaves
+    // shared memory for the next launch's CTAs to start streaming early
+    const long n_st = (pl.rows_per_cta + pl.SR - 1) / pl.SR;
+    pl.n_slots = static_cast<int>(std::max(1L, std::min(std::min(8L, n_st), budget / pl.slot_bytes)));
     pl.smem = 2048 + static_cast<size_t>(pl.n_slots) * pl.slot_bytes + act;
     return pl;
 }
@@ -992,9 +1001,10 @@ static int make_map_sw128(CUtensorMap *map, const void *base, int64_t rows, int6
     return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
 }
 
-// The persistent stream-K GEMM (fr_gemm.cuh): grid = one CTA per SM (or one
-// per unit when there are fewer), the partial slots [grid][2][128 x 256] f32
-// and the per-tile arrival counters in grow-only workspaces.
+// The persistent W4A4 GEMM (fr_gemm.cuh): whole 128x256 tiles on one CTA per
+// SM when the tiles fill the SMs, else every tile split into S equal K ranges
+// (grid = tiles x S), partial slots [grid][128 x 256] f32 and per-tile arrival
+// counters in grow-only workspaces.
 static int gemm_p_run(int epi, const void *A_packed, const void *SFA, const void *B_packed, const void *SFB, float *D,
                       int M, int N, int K, float alpha, cudaStream_t stream) {
     if (!A_packed || !SFA || !B_packed || !SFB || !D || M <= 0 || N <= 0 || K <= 0) return FR_EINVAL;
@@ -1018,12 +1028,23 @@ static int gemm_p_run(int epi, const void *A_packed, const void *SFA, const void
     g.n_n = (N + P_BN - 1) / P_BN;
     const int64_t tiles = static_cast<int64_t>(g.n_m) * g.n_n;
     if (tiles > (1 << 24)) return FR_EINVAL;
-    g.units = tiles * g.nkt;
+    g.tiles = static_cast<int>(tiles);
     g.alpha = alpha;
-    const int grid = static_cast<int>(std::min<int64_t>(di.sms, g.units));
+    // whole tiles when they fill the SMs, else an even K split of every tile
+    int grid;
+    if (tiles >= di.sms) {
+        g.split = 0;
+        grid = di.sms;
+    } else {
+        g.split = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(di.sms / tiles, g.nkt)));
+        grid = static_cast<int>(tiles * g.split);
+    }
     void *part = nullptr, *cnt = nullptr;
-    int rc = workspace_get(WS_GPART, static_cast<size_t>(grid) * 2 * P_SLOT_FLOATS * sizeof(float), stream, &part);
-    if (rc != FR_OK) return rc;
+    int rc = FR_OK;
+    if (g.split > 1) {
+        rc = workspace_get(WS_GPART, static_cast<size_t>(grid) * P_SLOT_FLOATS * sizeof(float), stream, &part);
+        if (rc != FR_OK) return rc;
+    }
     rc = workspace_get_zeroed(WS_GCNT, static_cast<size_t>(tiles) * sizeof(unsigned int), stream, &cnt);
     if (rc != FR_OK) return rc;
     g.part = static_cast<float *>(part);
