@@ -16,9 +16,11 @@
 //     128 x 128 tile), K stage 256 values, 4-stage TMA ring of 54 KB stages;
 //   * schedule: with at least as many tiles as SMs, one CTA per SM takes whole
 //     tiles c, c + grid, ... (no partial sum is ever written); with fewer,
-//     every tile is split into S = SMs / tiles equal K ranges on S CTAs, and
-//     the last of them to arrive adds the S partials in K-range order
-//     (deterministic), each CTA owning one partial slot.  (A stream-K
+//     every tile is split into S = SMs / tiles equal K ranges on S CTAs: for
+//     S = 2 the two CTAs exchange halves (each finishes 64 rows, bounded
+//     wait on its partner's flag, site 47), for S > 2 the last to arrive
+//     adds the S partials in K-range order (deterministic); each CTA owns one
+//     partial slot.  (A stream-K
 //     division of the units over the SMs was measured and dropped: the
 //     partial traffic at the end of the kernel cost 15-20 us on configs[3]'s
 //     shapes);
@@ -73,7 +75,7 @@ struct PGemmArgs {
                                  // S > 0: grid = tiles * S, CTA c takes K range c % S of tile c / S
     float alpha;
     float *part;                 // [grid][128 x 256] partial accumulators (split mode)
-    unsigned int *counter;       // [tiles], zero on entry, reset by the last arrival
+    unsigned int *counter;       // [2 * tiles], zero on entry, reset by the last arrival / the finisher
 };
 
 // The (tile, K range) segments of one CTA, in order.  Whole tiles when there
@@ -373,6 +375,60 @@ __global__ void __launch_bounds__(P_THREADS, 1) k_gemm_p(const __grid_constant__
             const float *v = reinterpret_cast<const float *>(r);
             if (kt0 == 0 && kt1 == nkt) {
                 p_store_rows<EPI, P_CW>(g, mb * P_BM + 32 * q, n0, cw0, v, stg, lane);
+            } else if (g.split == 2) {
+                // two CTAs share the tile (K ranges 0 and 1): CTA s finishes
+                // rows [64 s, 64 s + 64) (lane quadrants 2s, 2s+1) and hands
+                // its other rows to its partner through its slot, so each
+                // moves half a tile each way instead of one CTA merging all
+                const int sh = static_cast<int>(blockIdx.x) & 1;
+                const bool mine = (q >> 1) == sh;
+                if (!mine) {
+                    float4 *blk = reinterpret_cast<float4 *>(g.part + static_cast<int64_t>(blockIdx.x) * P_SLOT_FLOATS +
+                                                             wb * (32 * P_CW)) + lane;
+#pragma unroll
+                    for (int i = 0; i < P_CW / 4; ++i)
+                        blk[i * 32] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    fence_acq_rel_gpu();
+                }
+                named_bar(1, P_EPI_WARPS * 32);
+                if (leader) {
+                    __threadfence();
+                    atomicAdd(&g.counter[2 * t + (1 - sh)], 1u);           // the partner's half is out
+                    unsigned int *f = &g.counter[2 * t + sh];
+                    const uint64_t t0 = fr_now_ns();
+                    int got = 0;
+                    for (;;) {
+                        unsigned int fv;
+                        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(fv) : "l"(f) : "memory");
+                        if (fv != 0u) { got = 1; break; }
+                        if (fr_now_ns() - t0 > g_fr_wait_ns) {
+                            fr_flag(FR_ST_TIMEOUT | (47u << FR_ST_SITE_SHIFT));
+                            break;
+                        }
+                    }
+                    if (got) *f = 0u;                       // nobody else touches it before the next launch
+                    bcast[0] = got;
+                }
+                named_bar(1, P_EPI_WARPS * 32);
+                if (mine && bcast[0]) {
+                    fence_acq_rel_gpu();
+                    const float4 *src = reinterpret_cast<const float4 *>(
+                                            g.part + static_cast<int64_t>(blockIdx.x ^ 1u) * P_SLOT_FLOATS +
+                                            wb * (32 * P_CW)) + lane;
+#pragma unroll
+                    for (int ch = 0; ch < P_CW; ch += 32) {
+                        float acc[32];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 w = __ldcg(src + (ch / 4 + i) * 32);
+                            acc[4 * i] = v[ch + 4 * i] + w.x;          // two terms: the order is immaterial
+                            acc[4 * i + 1] = v[ch + 4 * i + 1] + w.y;
+                            acc[4 * i + 2] = v[ch + 4 * i + 2] + w.z;
+                            acc[4 * i + 3] = v[ch + 4 * i + 3] + w.w;
+                        }
+                        p_store_rows<EPI, 32>(g, mb * P_BM + 32 * q, n0, cw0 + ch, acc, stg, lane);
+                    }
+                }
             } else {
                 // part of a tile shared with neighbouring CTAs: publish this
                 // CTA's partial in its slot (0: first segment, 1: last one),

@@ -1045,7 +1045,7 @@ static int gemm_p_run(int epi, const void *A_packed, const void *SFA, const void
         rc = workspace_get(WS_GPART, static_cast<size_t>(grid) * P_SLOT_FLOATS * sizeof(float), stream, &part);
         if (rc != FR_OK) return rc;
     }
-    rc = workspace_get_zeroed(WS_GCNT, static_cast<size_t>(tiles) * sizeof(unsigned int), stream, &cnt);
+    rc = workspace_get_zeroed(WS_GCNT, static_cast<size_t>(2 * tiles) * sizeof(unsigned int), stream, &cnt);
     if (rc != FR_OK) return rc;
     g.part = static_cast<float *>(part);
     g.counter = static_cast<unsigned int *>(cnt);
