@@ -12,6 +12,7 @@
 #include "fr_moe.cuh"
 #include "fr_w4a4.cuh"
 #include "fr_gemm.cuh"
+#include "fr_gemm2.cuh"
 #include "fr_attn.cuh"
 #include "fr_tcgemv.cuh"
 #include "fr_fp4mv.cuh"
@@ -1001,6 +1002,82 @@ static int make_map_sw128(CUtensorMap *map, const void *base, int64_t rows, int6
     return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
 }
 
+// Scale atoms of 128-row blocks ([rows / 128][K / 64] atoms of 512 B) as a
+// 2D u32 tensor, one box = four consecutive atoms (one K stage of a block)
+static int make_map_sf(CUtensorMap *map, const void *base, int64_t row_blocks, int64_t kb_total) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return FR_ENODEVICE;
+    cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(row_blocks * kb_total)};
+    cuuint64_t strides[1] = {512};
+    cuuint32_t box[2] = {128, 4};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
+}
+
+// f32 output [rows, cols] (row stride ld floats), 32 x 32 boxes, 128-byte swizzle
+static int make_map_out(CUtensorMap *map, float *base, int64_t rows, int64_t cols, int64_t ld) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return FR_ENODEVICE;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FR_OK : FR_EINVAL;
+}
+
+// The SM-pair GEMM (fr_gemm2.cuh): 256 x 256 tiles, one cluster of two CTAs
+// per SM pair, static round-robin over the tiles.
+static int gemm_c2_run(int epi, const void *A_packed, const void *SFA, const void *B_packed, const void *SFB, float *D,
+                       int M, int N, int K, float alpha, cudaStream_t stream) {
+    const DevInfo &di = dev_info();
+    C2Args g{};
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.nkt = K / 256;
+    g.kb_total = K / 64;
+    g.n_m2 = (M + 255) / 256;
+    g.n_n2 = (N + 255) / 256;
+    g.tiles = g.n_m2 * g.n_n2;
+    g.alpha = alpha;
+    CUtensorMap ma, mb, msa, msb, md;
+    int rc = make_map_sw128(&ma, A_packed, M, K / 2, 128);
+    if (rc == FR_OK) rc = make_map_sw128(&mb, B_packed, N, K / 2, 128);
+    if (rc == FR_OK) rc = make_map_sf(&msa, SFA, (M + 127) / 128, g.kb_total);
+    if (rc == FR_OK) rc = make_map_sf(&msb, SFB, (N + 127) / 128, g.kb_total);
+    const int nout = epi == P_SWIGLU ? N / 2 : N;
+    if (rc == FR_OK) rc = make_map_out(&md, D, M, nout, nout);
+    if (rc != FR_OK) return rc;
+    const int ncl = std::max(1, std::min(g.tiles, di.sms / 2));
+    auto kern = epi == P_SWIGLU ? k_gemm_c2<P_SWIGLU> : k_gemm_c2<P_PLAIN>;
+    static bool done[2][64] = {};
+    rc = allow_max_smem(kern, done[epi == P_SWIGLU ? 1 : 0]);
+    if (rc != FR_OK) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * ncl);
+    cfg.blockDim = dim3(P_THREADS);
+    cfg.dynamicSmemBytes = C2_SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, msa, msb, md, g);
+    if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cuda_rc(e);
+}
+
 // The persistent W4A4 GEMM (fr_gemm.cuh): whole 128x256 tiles on one CTA per
 // SM when the tiles fill the SMs, else every tile split into S equal K ranges
 // (grid = tiles x S), partial slots [grid][128 x 256] f32 and per-tile arrival
@@ -1015,6 +1092,17 @@ static int gemm_p_run(int epi, const void *A_packed, const void *SFA, const void
         return FR_EINVAL;
     const DevInfo &di = dev_info();
     if (di.cc_major != 10) return FR_ENODEVICE;
+    // SM pairs when the 256 x 256 tiles nearly fill them (FR_GEMM_PAIR=0
+    // keeps the one-SM kernel): whole K stages, output rows 16-byte aligned
+    {
+        static const char *pv = getenv("FR_GEMM_PAIR");
+        const bool pair_ok = !(pv && *pv == '0');
+        const int64_t tiles2 = static_cast<int64_t>((M + 255) / 256) * ((N + 255) / 256);
+        const int nout = epi == P_SWIGLU ? N / 2 : N;
+        if (pair_ok && M >= 256 && K % 256 == 0 && nout % 4 == 0 && tiles2 >= (di.sms / 2) * 7 / 8 &&
+            tiles2 < (1 << 24))
+            return gemm_c2_run(epi, A_packed, SFA, B_packed, SFB, D, M, N, K, alpha, stream);
+    }
     PGemmArgs g{};
     g.sfa = static_cast<const uint8_t *>(SFA);
     g.sfb = static_cast<const uint8_t *>(SFB);
@@ -1309,11 +1397,15 @@ static int fp4t_launch(FtArgs a, int grid, cudaStream_t stream) {
     if (rc != FR_OK) return rc;
     // about 110 KB of weights in flight per SM (measured best for one pass
     // over a matrix: more only lengthens the memory queues); each ring stage
-    // also holds its activation columns; TMEM's 256 scale columns bound the
-    // ring, whose depth is a multiple of the issue groups
-    const int extra = 2048;                                  // scale atom, factors, barriers
-    const int cap = dev_info().smem_optin - 1024 - extra;
-    const int per = S::WST + S::BST;
+    // also holds its activation columns, unless the kernel builds them (a.x
+    // set: then a fixed area holds every slot's columns and x values);
+    // TMEM's 256 scale columns bound the ring, whose depth is a multiple of
+    // the issue groups
+    const bool build = a.x != nullptr;
+    const int fixed = build ? a.n_slots * (S::BST + NT * 1024 * a.T) : 0;
+    const int extra = 2048 + (build ? 8 * a.n_slots : 0);   // scale atom, factors, barriers, scratch
+    const int cap = dev_info().smem_optin - 1024 - extra - fixed;
+    const int per = S::WST + (build ? 0 : S::BST);
     const int nw_tmem = (256 - 4 * S::NISS) / (16 * S::NI);
     // the down projection (one matrix) follows the activation kernel of the
     // GLU: a deeper ring prefetches more of its weights meanwhile
@@ -1329,8 +1421,8 @@ static int fp4t_launch(FtArgs a, int grid, cudaStream_t stream) {
     nw -= nw % S::P;
     if (nw < 2 || nw * per > cap) return FR_EINVAL;
     a.n_w = nw;
-    a.n_b = nw;
-    const size_t smem = 1024 + static_cast<size_t>(nw) * per + extra;
+    a.n_b = build ? 0 : nw;
+    const size_t smem = 1024 + static_cast<size_t>(nw) * per + fixed + extra;
     return launch_pdl(kern, dim3(grid), dim3(S::THREADS), smem, stream, a);
 }
 
@@ -1413,6 +1505,27 @@ static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const
         if (tp->ctas_out) *tp->ctas_out = static_cast<unsigned>(G) * static_cast<unsigned>((T + TW - 1) / TW);
     }
     const int nq = K / Q8_ELEMS;
+    // T <= 2 from f32 rows, FR_FP4T_BUILD=1: the matvec builds its
+    // activation columns itself (no k_act_fp4 launch); the slots are the
+    // K-stage groups of the most units a CTA holds.  Off by default: the five
+    // builder warps measured ~1.8 us per slot, slower than the weight stream
+    // they feed, so the separate kernel is faster end to end.
+    static const char *bv = getenv("FR_FP4T_BUILD");
+    const bool build_ok = bv && *bv == '1';
+    if (build_ok && x != nullptr && q8 == nullptr && T <= 2 && NCOL == 16 &&
+        (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0) {
+        const int slots = std::min((U + G - 1) / G, nsr);
+        if (slots * (nt * NCOL * 128 + nt * 1024 * T) <= 64 * 1024) {
+            a.T = T;
+            a.t0 = 0;
+            a.x = x;
+            a.ldx = ldx;
+            a.amax_in = amax_in;
+            a.n_amax = nq;
+            a.n_slots = slots;
+            return fp4t_launch2<16>(a, G, dual, nt, stream);
+        }
+    }
     for (int t0 = 0; t0 < T; t0 += TW) {
         const int tw = std::min(TW, T - t0);
         a.T = tw;

@@ -135,6 +135,40 @@ def test_gemm_rejects_bad_shapes(fr, dev):
     assert L.fr_gemm_f32out(p, p, p, p, p, 128, 128, 96, 1.0, False, fr._stream()) == -1    # K % 64
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 16400, 512), (1000, 16384, 256), (256, 16384, 4096)])
+def test_gemm_pair_tiles(fr, O, dev, M, N, K):
+    """Shapes that take the SM-pair kernel (256 x 256 tiles on clusters of
+    two CTAs, tcgen05 cta_group::2): rows and columns past the last full tile
+    (M = 300, N = 16400), several tiles per cluster (M = 1000), one row of
+    tiles (M = 256); sampled rows against the fp64 products."""
+    _gemm_case(fr, O, dev, M, N, K, row_sample=96)
+    assert fr.device_status() == 0
+
+
+def test_gemm_pair_tiles_deterministic_and_graph_replay(fr, dev):
+    """The SM-pair kernel gives the same bits eager and replayed from a CUDA
+    graph (static tile order, no cross-CTA reduction)."""
+    import torch
+    M, N, K = 512, 14336, 4096
+    A, SFA = fr.quantize_act_f32(_t(fr.synth_normal(0x5EED4A00, M * K).reshape(M, K), dev))
+    B, SFB = fr.repack_weight(_t(fr.synth_nvfp4(0x5EED4A01, N, K), dev), N, K)
+    d0 = fr.gemm_f32out(A, SFA, B, SFB, M, N, K)
+    s = torch.cuda.Stream(dev)
+    out = torch.empty_like(d0)
+    with torch.cuda.stream(s):
+        fr.gemm_f32out(A, SFA, B, SFB, M, N, K, out=out, stream=s)
+    s.synchronize()
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph, stream=s):
+        fr.gemm_f32out(A, SFA, B, SFB, M, N, K, out=out, stream=s)
+    for _ in range(3):
+        out.zero_()
+        gph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, d0)
+    assert fr.device_status() == 0
+
+
 @pytest.mark.parametrize("M,n_ff,K", [(512, 14336, 4096), (100, 768, 2048), (7, 208, 320)])
 def test_gemm_swiglu_fused_epilogue(fr, O, dev, M, n_ff, K):
     """The prefill FFN's gate/up GEMM with the SwiGLU in its epilogue
