@@ -1034,9 +1034,10 @@ static int make_map_out(CUtensorMap *map, float *base, int64_t rows, int64_t col
 // The SM-pair GEMM (fr_gemm2.cuh): 256 x 256 tiles, one cluster of two CTAs
 // per SM pair, static round-robin over the tiles.
 static int gemm_c2_run(int epi, const void *A_packed, const void *SFA, const void *B_packed, const void *SFB, float *D,
-                       int M, int N, int K, float alpha, cudaStream_t stream) {
+                       int M, int N, int K, float alpha, int split, cudaStream_t stream) {
     const DevInfo &di = dev_info();
     C2Args g{};
+    g.split = split;
     g.M = M;
     g.N = N;
     g.K = K;
@@ -1054,7 +1055,18 @@ static int gemm_c2_run(int epi, const void *A_packed, const void *SFA, const voi
     const int nout = epi == P_SWIGLU ? N / 2 : N;
     if (rc == FR_OK) rc = make_map_out(&md, D, M, nout, nout);
     if (rc != FR_OK) return rc;
-    const int ncl = std::max(1, std::min(g.tiles, di.sms / 2));
+    if (split == 2) {
+        // hand-off halves and their flags (zero between launches)
+        void *part = nullptr, *cnt = nullptr;
+        rc = workspace_get(WS_GPART, static_cast<size_t>(g.tiles) * 16 * 32 * 128 * sizeof(float), stream, &part);
+        if (rc != FR_OK) return rc;
+        rc = workspace_get_zeroed(WS_GCNT, static_cast<size_t>(g.tiles) * 16 * sizeof(unsigned int), stream, &cnt);
+        if (rc != FR_OK) return rc;
+        g.part = static_cast<float *>(part);
+        g.counter = static_cast<unsigned int *>(cnt);
+    }
+    // split 2: one unit per cluster, so the two halves of a tile run together
+    const int ncl = std::max(1, std::min(g.tiles * split, di.sms / 2));
     auto kern = epi == P_SWIGLU ? k_gemm_c2<P_SWIGLU> : k_gemm_c2<P_PLAIN>;
     static bool done[2][64] = {};
     rc = allow_max_smem(kern, done[epi == P_SWIGLU ? 1 : 0]);
@@ -1092,16 +1104,22 @@ static int gemm_p_run(int epi, const void *A_packed, const void *SFA, const void
         return FR_EINVAL;
     const DevInfo &di = dev_info();
     if (di.cc_major != 10) return FR_ENODEVICE;
-    // SM pairs when the 256 x 256 tiles nearly fill them (FR_GEMM_PAIR=0
-    // keeps the one-SM kernel): whole K stages, output rows 16-byte aligned
+    // SM pairs (FR_GEMM_PAIR=0 keeps the one-SM kernel; whole K stages,
+    // output rows 16-byte aligned): whole tiles when the 256 x 256 tiles
+    // nearly fill the pairs, two K halves per tile when half as many tiles
+    // do (both halves of every tile then run at once)
     {
         static const char *pv = getenv("FR_GEMM_PAIR");
         const bool pair_ok = !(pv && *pv == '0');
         const int64_t tiles2 = static_cast<int64_t>((M + 255) / 256) * ((N + 255) / 256);
         const int nout = epi == P_SWIGLU ? N / 2 : N;
-        if (pair_ok && M >= 256 && K % 256 == 0 && nout % 4 == 0 && tiles2 >= (di.sms / 2) * 7 / 8 &&
-            tiles2 < (1 << 24))
-            return gemm_c2_run(epi, A_packed, SFA, B_packed, SFB, D, M, N, K, alpha, stream);
+        const int pairs = di.sms / 2;
+        if (pair_ok && M >= 256 && K % 256 == 0 && nout % 4 == 0 && tiles2 < (1 << 24)) {
+            if (tiles2 >= pairs * 7 / 8)
+                return gemm_c2_run(epi, A_packed, SFA, B_packed, SFB, D, M, N, K, alpha, 1, stream);
+            if (2 * tiles2 <= pairs && 2 * tiles2 >= pairs * 5 / 8 && K >= 512)
+                return gemm_c2_run(epi, A_packed, SFA, B_packed, SFB, D, M, N, K, alpha, 2, stream);
+        }
     }
     PGemmArgs g{};
     g.sfa = static_cast<const uint8_t *>(SFA);

@@ -135,12 +135,15 @@ def test_gemm_rejects_bad_shapes(fr, dev):
     assert L.fr_gemm_f32out(p, p, p, p, p, 128, 128, 96, 1.0, False, fr._stream()) == -1    # K % 64
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 16400, 512), (1000, 16384, 256), (256, 16384, 4096)])
+@pytest.mark.parametrize("M,N,K", [(300, 16400, 512), (1000, 16384, 256), (256, 16384, 4096), (512, 4096, 14336),
+                                   (300, 4096, 1024)])
 def test_gemm_pair_tiles(fr, O, dev, M, N, K):
     """Shapes that take the SM-pair kernel (256 x 256 tiles on clusters of
     two CTAs, tcgen05 cta_group::2): rows and columns past the last full tile
     (M = 300, N = 16400), several tiles per cluster (M = 1000), one row of
-    tiles (M = 256); sampled rows against the fp64 products."""
+    tiles (M = 256), and two K halves per tile handed over between clusters
+    (N = 4096: 32 tiles on 74 SM pairs); sampled rows against the fp64
+    products."""
     _gemm_case(fr, O, dev, M, N, K, row_sample=96)
     assert fr.device_status() == 0
 
