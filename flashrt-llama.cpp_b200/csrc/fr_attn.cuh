@@ -186,6 +186,16 @@ __global__ void k_pos_advance(int32_t *pos_p) {
     if (threadIdx.x == 0) *pos_p += 1;
 }
 
+// fr_copy_pinned: 16-byte copy, grid-stride, after the previous kernel of
+// the stream (it may still read the destination), ahead of the next one
+__global__ void __launch_bounds__(256) k_copy16(const uint4 *__restrict__ src, uint4 *__restrict__ dst, int64_t n) {
+    fr_pdl_wait();
+    fr_pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * 256)
+        dst[i] = src[i];
+}
+
 // ------------------------------------------------------ GQA decode attention
 // One CTA per (split of AT_CH keys, KV head g, sequence t): the KV head's
 // keys [s * 128, s * 128 + 128) of sequence t against its 8 query heads,

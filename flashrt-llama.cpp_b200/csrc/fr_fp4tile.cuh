@@ -93,19 +93,8 @@ struct FtArgs {
     const unsigned int *epoch;   // step parity of the receiving slots (as GvParams::epoch)
     int64_t par_bytes;
     unsigned int *counter;       // [row blocks][4 quadrants], zero on entry, reset by the last arrival
-    int n_w, n_b;                // ring depth (stages of weights + activation columns); n_b = n_w,
-                                 // or 0 when the kernel builds the columns itself (x below)
+    int n_w, n_b;                // ring depth (stages of weights + activation columns); n_b = n_w
     int amax_ld;
-    // in-kernel activation columns (T <= 2, NCOL = 16): with x set, bimg and
-    // gtab are unused; the CTA copies the x values of its K stages into
-    // shared memory and builds their digit columns there.  amax_in
-    // (nullable): per token the maxima of x's 32-value groups ([T][n_amax]),
-    // else the row is scanned.  n_slots: K-stage groups a CTA holds at most.
-    const float *x;
-    int64_t ldx;
-    const float *amax_in;
-    int n_amax;
-    int n_slots;
 };
 
 // A pipeline stage is two 18 KB weight tiles -- the gate and up tiles of one
@@ -131,11 +120,8 @@ struct FtShape {
     static constexpr int P = 2 * NI * NCOL <= 256 ? 2 : 1;         // issue groups
     static constexpr int NISS = P * NI;                            // issuer threads = accumulators
     // weight producer, issuers (warps 1, 2, then 8, 9), four epilogue warps
-    // (3..6), activation producer (7), then four more column-building warps
-    // (WB..WB+3; with warp 7 the builders of the in-kernel form)
-    static constexpr int WB = 8 + (NISS > 2 ? NISS - 2 : 0);
-    static constexpr int NBW = 5;
-    static constexpr int THREADS = 32 * (WB + NBW - 1);
+    // (3..6), activation producer (7)
+    static constexpr int THREADS = 32 * (8 + (NISS > 2 ? NISS - 2 : 0));
 };
 
 // first unit of CTA c when U units go to G CTAs, and the CTA owning unit u
@@ -178,174 +164,6 @@ __device__ __forceinline__ void ft_sum_parts(F part, int n, int T, int erow, flo
     }
 }
 
-// The eight digit planes of one q8_1 block (32 values, lane = value) as
-// 32-bit words: W holds this lane's digit nibbles (plane p at bits 4p).  Byte
-// b of plane p's 16-byte unit packs values b and b + 8 of its sub-block
-// (ggml's order, as fp4_digits_store); lane L writes bytes 4(L&3)..+3 of
-// plane L>>2, so the warp stores 128 bytes in one conflict-free instruction
-// (eight rows, each in its own 16-byte swizzle position).
-__device__ __forceinline__ void fp4_words_store(uint32_t W, uint8_t *tile, int n0, int c) {
-    const int lane = threadIdx.x & 31;
-    const uint32_t hiW = __shfl_xor_sync(0xffffffffu, W, 8);
-    // valid on lanes j < 8 of each half: even planes' bytes, odd planes' bytes
-    const uint32_t E = (W & 0x0F0F0F0Fu) | ((hiW & 0x0F0F0F0Fu) << 4);
-    const uint32_t O = ((W >> 4) & 0x0F0F0F0Fu) | (hiW & 0xF0F0F0F0u);
-    const int p = lane >> 2, qd = lane & 3;
-    const int src = 4 * (qd & 1) + 16 * (qd >> 1);
-    uint32_t v[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t e = __shfl_sync(0xffffffffu, E, src + i);
-        const uint32_t o = __shfl_sync(0xffffffffu, O, src + i);
-        v[i] = (p & 1) ? o : e;
-    }
-    const uint32_t k = static_cast<uint32_t>(p >> 1);
-    const uint32_t sel = k | ((k + 4u) << 4);
-    const uint32_t word = __byte_perm(__byte_perm(v[0], v[1], sel), __byte_perm(v[2], v[3], sel), 0x5410);
-    const int n = n0 + p;
-    *reinterpret_cast<uint32_t *>(tile + n * 128 + ((c ^ (n & 7)) << 4) + 4 * qd) = word;
-}
-
-// The activation columns of this CTA's K stages, built in shared memory by
-// five warps (bw = 0..4) instead of by a separate kernel (T <= 2).  Slot j
-// holds the K-stage group (u_lo + j) mod nsr, the group of the CTA's unit j
-// (and of every unit j + m nsr): its NT column tiles and, per token, its
-// NT x 256 x values.  The arithmetic is act_fp4_row's, value for value:
-// the token's reference exponent from the row's largest |x| (or from the
-// producer's 32-value-group maxima), q8_1 per 32 values, the eight balanced
-// base-9 digits as E2M1 codes in the 128-byte-swizzled K-major tiles.
-// The x values (and the row scan) arrive by plain vector loads, all in
-// flight at once; each warp then builds up to four q8_1 blocks together,
-// and every slot is released to the MMA issuers as soon as it is built.
-template <int NCOL, int NT>
-__device__ __forceinline__ void ft_build_columns(const FtArgs &g, int bw, int u_lo, int n_st, int nsr, uint8_t *act,
-                                                 float *xbuf, float *gtab, int *scr, uint64_t *gready,
-                                                 uint64_t *act_ready) {
-    constexpr int NBW = 5, NTH = NBW * 32;
-    constexpr int SV = NT * 256;                      // x values of one slot per token
-    constexpr int B_BYTES = NCOL * 128;
-    constexpr int LD = 8;                             // float4 loads in flight per thread and batch
-    const int lane = threadIdx.x & 31;
-    const int bt = bw * 32 + lane;
-    const int T = g.T;
-    const int nsl = min(n_st, nsr);
-    const int xt = g.n_slots * SV;                    // floats per token in xbuf
-    const int ga = u_lo % nsr;
-    const int n1 = min(nsl, nsr - ga);                // slots before the wrap at the row's end
-    fr_pdl_wait();
-    // 1. the slots' x values into xbuf (slot order) and each token's largest
-    // |x| (from the row, or from the producer's group maxima)
-    const int span4 = nsl * SV / 4;                   // float4 per token
-    const int K4 = g.K / 4;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        float am = 0.0f;
-        if (t < T) {
-            const float4 *r4 = reinterpret_cast<const float4 *>(g.x + static_cast<int64_t>(t) * g.ldx);
-            float4 *dst = reinterpret_cast<float4 *>(xbuf + t * xt);
-            for (int k0 = 0; k0 < span4; k0 += LD * NTH) {
-                float4 v[LD];
-#pragma unroll
-                for (int u = 0; u < LD; ++u) {
-                    const int k = k0 + u * NTH + bt;
-                    // slot-order index k -> row position (one wrap at most)
-                    const int sl = k / (SV / 4);
-                    const int src = (sl < n1 ? (ga + sl) : (sl - n1)) * (SV / 4) + k % (SV / 4);
-                    v[u] = k < span4 ? r4[src] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                }
-#pragma unroll
-                for (int u = 0; u < LD; ++u) {
-                    const int k = k0 + u * NTH + bt;
-                    if (k < span4) dst[k] = v[u];
-                }
-            }
-            if (g.amax_in != nullptr) {
-                const float *ai = g.amax_in + static_cast<int64_t>(t) * g.n_amax;
-                for (int i0 = 0; i0 < g.n_amax; i0 += LD * NTH) {
-                    float v[LD];
-#pragma unroll
-                    for (int u = 0; u < LD; ++u) {
-                        const int i = i0 + u * NTH + bt;
-                        v[u] = i < g.n_amax ? ai[i] : 0.0f;
-                    }
-#pragma unroll
-                    for (int u = 0; u < LD; ++u) am = fmaxf(am, v[u]);
-                }
-            } else {
-                for (int k0 = 0; k0 < K4; k0 += LD * NTH) {
-                    float4 v[LD];
-#pragma unroll
-                    for (int u = 0; u < LD; ++u) {
-                        const int k = k0 + u * NTH + bt;
-                        v[u] = k < K4 ? r4[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    }
-#pragma unroll
-                    for (int u = 0; u < LD; ++u)
-                        am = fmaxf(am, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
-                }
-            }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-        if (lane == 0) scr[t * NBW + bw] = __float_as_int(am);
-    }
-    named_bar(2, NTH);                                // xbuf and the maxima are complete
-    int e0v[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        float am = __int_as_float(scr[t * NBW]);
-#pragma unroll
-        for (int w = 1; w < NBW; ++w) am = fmaxf(am, __int_as_float(scr[t * NBW + w]));
-        const int emax = fp4_row_emax(am);
-        e0v[t] = emax > -1000 ? emax - FM_SPAN : 0;
-    }
-    if (bt < (NCOL / FM_DIGITS) * FM_GSTRIDE) {
-        const int t = bt / FM_GSTRIDE, p = bt % FM_GSTRIDE;
-        float v = 1.0f;
-        for (int i = 0; i < p; ++i) v *= 9.0f;
-        gtab[bt] = t < T ? ldexpf(v, (t == 0 ? e0v[0] : e0v[1]) + 1) : 0.0f;
-    }
-    // 2. the slots, in the order the issuers use them; the q8_1 blocks of
-    // all slots are dealt round-robin over the five warps, four at a time
-    const int NB = NT * 8 * T;                        // q8_1 blocks per slot
-    for (int j = 0; j < nsl; ++j) {
-        const int b0 = ((bw - (j * NB) % NBW) % NBW + NBW) % NBW;
-        for (int b = b0; b < NB; b += 4 * NBW) {
-            float xv[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int bb = b + k * NBW;
-                const int t = bb / (NT * 8), c8 = bb % (NT * 8);
-                xv[k] = bb < NB ? xbuf[t * xt + j * SV + c8 * 32 + lane] : 0.0f;
-            }
-            uint32_t W[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int bb = b + k * NBW;
-                const q8_lane r = q8_1_chunk(xv[k]);
-                uint32_t nib[FM_DIGITS];
-                fp4_digits(r.q, __float2half_rn(r.d), bb / (NT * 8) == 0 ? e0v[0] : e0v[1], nib);
-                uint32_t w = 0;
-#pragma unroll
-                for (int p = 0; p < FM_DIGITS; ++p) w |= nib[p] << (4 * p);
-                W[k] = w;
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int bb = b + k * NBW;
-                if (bb < NB) {
-                    const int t = bb / (NT * 8), c8 = bb % (NT * 8);
-                    fp4_words_store(W[k], act + (j * NT + (c8 >> 3)) * B_BYTES, FM_DIGITS * t, c8 & 7);
-                }
-            }
-        }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&act_ready[j]);
-        if (j == 0 && bt == 0) mbar_arrive(gready);   // gtab was written before the first slot
-    }
-}
-
 template <int NCOL, int EPI, int NT>
 __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(const FtArgs g) {
     using S = FtShape<NCOL, EPI, NT>;
@@ -358,22 +176,15 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int NW = g.n_w;                                   // ring stages (weights + activation columns)
-    const bool build = g.x != nullptr;                      // columns built here (T <= 2, NCOL = 16)
-    const int NSL = build ? g.n_slots : 0;
     uint8_t *w_ring = smem;
     uint8_t *b_ring = w_ring + static_cast<size_t>(NW) * S::WST;
-    uint8_t *act = b_ring + static_cast<size_t>(g.n_b) * S::BST;        // [NSL][NT] column tiles (built)
-    float *xbuf = reinterpret_cast<float *>(act + static_cast<size_t>(NSL) * S::BST);  // [T][NSL * NT * 256]
-    uint8_t *sfb_const = reinterpret_cast<uint8_t *>(xbuf + static_cast<size_t>(NSL) * NT * 256 * (build ? g.T : 0));
+    uint8_t *sfb_const = b_ring + static_cast<size_t>(NW) * S::BST;   // 512 B: the activation scale atom
     float *gtab = reinterpret_cast<float *>(sfb_const + 512);             // [TMAX][8] column factors
     uint64_t *full = reinterpret_cast<uint64_t *>(gtab + TMAX * FM_GSTRIDE);
     uint64_t *empty = full + NW;
     uint64_t *accfull = empty + NW;
     uint64_t *accempty = accfull + 1;
-    uint64_t *gready = accempty + 1;                         // column factors written (built form)
-    uint64_t *act_ready = gready + 1;                        // [NSL] column tiles built
-    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(act_ready + NSL);
-    int *bscr = reinterpret_cast<int *>(tmem_s + 1);         // [2][5] builder scratch
+    uint32_t *tmem_s = reinterpret_cast<uint32_t *>(accempty + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, U = g.n_units;
@@ -384,13 +195,11 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NW; ++s) {
-            mbar_init(&full[s], build ? 1 : 2);              // weight (and activation) producers
+            mbar_init(&full[s], 2);                          // weight and activation producers
             mbar_init(&empty[s], NI);                        // the owning group's issuers
         }
         mbar_init(accfull, NISS);                            // every issuer, once per segment
         mbar_init(accempty, 4);
-        mbar_init(gready, 1);
-        for (int j = 0; j < NSL; ++j) mbar_init(&act_ready[j], S::NBW);
         fence_mbar_init();
     }
     if (warp == 3) {
@@ -422,12 +231,6 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
                 if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &full[s]);
             }
         }
-    } else if (build && (warp == 7 || warp >= S::WB)) {
-        // ---------------- column builders (five warps; the host selects
-        // this form only for NCOL = 16)
-        if constexpr (NCOL == 16)
-            ft_build_columns<NCOL, NT>(g, warp == 7 ? 0 : warp - S::WB + 1, u_lo, n_st, nsr, act, xbuf, gtab, bscr,
-                                       gready, act_ready);
     } else if (warp == 7) {
         // ---------------- activation producer (after the PDL wait)
         if (lane == 0) {
@@ -441,7 +244,7 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
                          S::BST, &full[s]);
             }
         }
-    } else if (warp == 1 || warp == 2 || (warp >= 8 && warp < S::WB)) {
+    } else if (warp == 1 || warp == 2 || warp >= 8) {
         // ---------------- MMA issuers: thread (group p, tile k) issues tile k
         // of the stages i with i % P == p into accumulator p * NI + k
         const int ii = warp <= 2 ? warp - 1 : warp - 6;
@@ -467,12 +270,9 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
                 if (i % P == p) {
                     const int sw = i % NW;
                     if (!mbar_wait(&full[sw], (i / NW) & 1, 53)) break;
-                    // built columns: unit i's K-stage group sits in slot i mod nsr
-                    if (build && !mbar_wait(&act_ready[i % nsr], 0, 54)) break;
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + k * FT_TILE;
-                    const uint32_t b_addr = (build ? smem_u32(act + static_cast<size_t>(i % nsr) * S::BST)
-                                                   : smem_u32(b_ring + static_cast<size_t>(sw) * S::BST)) +
+                    const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sw) * S::BST) +
                                             (NT == 2 ? k : 0) * S::B_BYTES;
                     const uint32_t t_sfa = tbase + 256 + (sw * NI + k) * 16;
 #pragma unroll
@@ -498,11 +298,7 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
         const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
         const int erow = 32 * q + lane;
         fr_pdl_wait();
-        if (build) {
-            mbar_wait(gready, 0, 57);                     // the builders wrote gtab
-        } else if (at < TMAX * FM_GSTRIDE) {
-            gtab[at] = at / FM_GSTRIDE < T ? g.gtab[at] : 0.0f;
-        }
+        if (at < TMAX * FM_GSTRIDE) gtab[at] = at / FM_GSTRIDE < T ? g.gtab[at] : 0.0f;
         named_bar(1, 128);
         const float sc0 = g.s0 ? *g.s0 : 1.0f;
         const float sc1 = (DUAL && g.s1) ? *g.s1 : 1.0f;

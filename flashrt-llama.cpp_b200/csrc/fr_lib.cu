@@ -1415,15 +1415,11 @@ static int fp4t_launch(FtArgs a, int grid, cudaStream_t stream) {
     if (rc != FR_OK) return rc;
     // about 110 KB of weights in flight per SM (measured best for one pass
     // over a matrix: more only lengthens the memory queues); each ring stage
-    // also holds its activation columns, unless the kernel builds them (a.x
-    // set: then a fixed area holds every slot's columns and x values);
-    // TMEM's 256 scale columns bound the ring, whose depth is a multiple of
-    // the issue groups
-    const bool build = a.x != nullptr;
-    const int fixed = build ? a.n_slots * (S::BST + NT * 1024 * a.T) : 0;
-    const int extra = 2048 + (build ? 8 * a.n_slots : 0);   // scale atom, factors, barriers, scratch
-    const int cap = dev_info().smem_optin - 1024 - extra - fixed;
-    const int per = S::WST + (build ? 0 : S::BST);
+    // also holds its activation columns; TMEM's 256 scale columns bound the
+    // ring, whose depth is a multiple of the issue groups
+    const int extra = 2048;                                  // scale atom, factors, barriers
+    const int cap = dev_info().smem_optin - 1024 - extra;
+    const int per = S::WST + S::BST;
     const int nw_tmem = (256 - 4 * S::NISS) / (16 * S::NI);
     // the down projection (one matrix) follows the activation kernel of the
     // GLU: a deeper ring prefetches more of its weights meanwhile
@@ -1439,8 +1435,8 @@ static int fp4t_launch(FtArgs a, int grid, cudaStream_t stream) {
     nw -= nw % S::P;
     if (nw < 2 || nw * per > cap) return FR_EINVAL;
     a.n_w = nw;
-    a.n_b = build ? 0 : nw;
-    const size_t smem = 1024 + static_cast<size_t>(nw) * per + fixed + extra;
+    a.n_b = nw;
+    const size_t smem = 1024 + static_cast<size_t>(nw) * per + extra;
     return launch_pdl(kern, dim3(grid), dim3(S::THREADS), smem, stream, a);
 }
 
@@ -1523,27 +1519,6 @@ static int fp4t_matvec(const uint8_t *w0, const uint8_t *w1, int N, int K, const
         if (tp->ctas_out) *tp->ctas_out = static_cast<unsigned>(G) * static_cast<unsigned>((T + TW - 1) / TW);
     }
     const int nq = K / Q8_ELEMS;
-    // T <= 2 from f32 rows, FR_FP4T_BUILD=1: the matvec builds its
-    // activation columns itself (no k_act_fp4 launch); the slots are the
-    // K-stage groups of the most units a CTA holds.  Off by default: the five
-    // builder warps measured ~1.8 us per slot, slower than the weight stream
-    // they feed, so the separate kernel is faster end to end.
-    static const char *bv = getenv("FR_FP4T_BUILD");
-    const bool build_ok = bv && *bv == '1';
-    if (build_ok && x != nullptr && q8 == nullptr && T <= 2 && NCOL == 16 &&
-        (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0) {
-        const int slots = std::min((U + G - 1) / G, nsr);
-        if (slots * (nt * NCOL * 128 + nt * 1024 * T) <= 64 * 1024) {
-            a.T = T;
-            a.t0 = 0;
-            a.x = x;
-            a.ldx = ldx;
-            a.amax_in = amax_in;
-            a.n_amax = nq;
-            a.n_slots = slots;
-            return fp4t_launch2<16>(a, G, dual, nt, stream);
-        }
-    }
     for (int t0 = 0; t0 < T; t0 += TW) {
         const int tw = std::min(TW, T - t0);
         a.T = tw;
@@ -2801,6 +2776,37 @@ int fr_argmax_f32(const float *logits, int T, int V, int32_t *tok, cudaStream_t 
 int fr_pos_advance(int32_t *pos, cudaStream_t stream) {
     if (!pos) return FR_EINVAL;
     return launch_pdl(k_pos_advance, dim3(1), dim3(32), 0, stream, pos);
+}
+
+int fr_copy_pinned(void *dst, const void *src, int64_t bytes, cudaStream_t stream) {
+    if (fault_hit("fr_copy_pinned")) return FR_EINJECTED;
+    if (!dst || !src || bytes < 0 || bytes % 16 != 0) return FR_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) || (reinterpret_cast<uintptr_t>(src) & 15)) return FR_EINVAL;
+    if (bytes == 0) return FR_OK;
+    // the device-side address of each side (host memory must be mapped)
+    auto dev_addr = [](const void *p, void **out) -> bool {
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+            *out = const_cast<void *>(p);
+            return true;
+        }
+        if (a.type == cudaMemoryTypeHost && a.devicePointer != nullptr) {
+            *out = a.devicePointer;
+            return true;
+        }
+        return false;
+    };
+    void *d = nullptr, *sp = nullptr;
+    if (!dev_addr(dst, &d) || !dev_addr(src, &sp)) return FR_EINVAL;
+    const int64_t n16 = bytes / 16;
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((n16 + threads - 1) / threads, 4LL * dev_info().sms);
+    return launch_pdl(k_copy16, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, stream,
+                      static_cast<const uint4 *>(sp), static_cast<uint4 *>(d), n16);
 }
 
 } // extern "C"

@@ -104,6 +104,7 @@ SIGNATURES = {
     "fr_embed_nvfp4": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _vp]),
     "fr_argmax_f32": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "fr_pos_advance": (_i32, [_vp, _vp]),
+    "fr_copy_pinned": (_i32, [_vp, _vp, _i64, _vp]),
     "fr_synth_nvfp4_device": (_i32, [C.c_uint64, _i64, _i64, C.c_double, _vp, _vp]),
     "fr_synth_nvfp4": (None, [C.c_uint64, _i64, _i64, C.c_double, _vp]),
     "fr_synth_normal": (None, [C.c_uint64, _i64, C.c_double, C.c_double, _vp]),
@@ -400,6 +401,16 @@ def moe_combine(part, wts, n_embd, resid=None, out=None, stream=None):
         out = torch.empty((T, n_embd), dtype=torch.float32, device=part.device)
     call("fr_moe_combine", _ptr(part), _ptr(wts), _ptr(resid), _ptr(out), T, n_used, n_embd, _stream(stream))
     return out
+
+
+def copy_pinned(dst, src, stream=None):
+    """dst <- src (same byte size; device memory and/or page-locked host
+    memory) by SM loads and stores inside the stream's PDL chain."""
+    n = src.numel() * src.element_size()
+    if dst.numel() * dst.element_size() != n:
+        raise ValueError("copy_pinned: sizes differ")
+    call("fr_copy_pinned", _ptr(dst), _ptr(src), n, _stream(stream))
+    return dst
 
 
 def sf_bytes(rows: int, K: int) -> int:

@@ -446,6 +446,20 @@ int fr_pos_advance(int32_t *pos, cudaStream_t stream);
 int fr_synth_nvfp4_device(uint64_t seed, int64_t rows, int64_t K, double scale_sigma, void *out,
                           cudaStream_t stream);
 
+/* ------------------------------------------------------ host transfers
+ * fr_copy_pinned: copies `bytes` between device memory and page-locked host
+ * memory (either side may be host; cudaHostAlloc / pin_memory buffers) with
+ * SM loads and stores over PCIe inside the stream's PDL chain, instead of a
+ * copy-engine memcpy, whose fixed latency dominates the few KB a decode step
+ * moves and which breaks the chain of programmatic launches around it.  It
+ * waits for the previous kernel of the stream to finish before it writes.
+ * Host pointers must be mapped (cudaHostGetDevicePointer succeeds: true of
+ * every page-locked allocation on a unified-address system); both addresses
+ * and `bytes` 16-byte aligned.  FR_EINVAL otherwise.  Not a reference
+ * interface: the ggml backend's tensor_set/get do the same transfers with
+ * cudaMemcpyAsync. */
+int fr_copy_pinned(void *dst, const void *src, int64_t bytes, cudaStream_t stream);
+
 /* ------------------------------------------------------ synthetic inputs
  * Host-side, deterministic (splitmix64 + Box-Muller in double) generator of
  * the benchmark inputs: NVFP4 rows with E2M1 codes uniform over 0..15 and
