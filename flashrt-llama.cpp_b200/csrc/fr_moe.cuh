@@ -55,17 +55,20 @@ __device__ __forceinline__ void router_tile(const float *__restrict__ x, int64_t
             for (int u = 0; u < 4; ++u)
                 acc[r][u] += wv[r].x * xv[u].x + wv[r].y * xv[u].y + wv[r].z * xv[u].z + wv[r].w * xv[u].w;
     }
+    // warp sums of the tile's real tokens only (T = 1: 4 of the 16)
+    const int nu = min(4, T - t0);
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
+            if (u >= nu) continue;
             float v = acc[r][u];
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
             if (lane == 0) red[warp][r * 4 + u] = v;
         }
     __syncthreads();
-    if (tid < 16) {
+    if (tid < 16 && (tid & 3) < nu) {
         const int r = tid >> 2, u = tid & 3;
         float v = red[0][tid];
 #pragma unroll
@@ -303,17 +306,22 @@ __global__ void __launch_bounds__(256) k_route(const RouteArgs a) {
                    a.ids + static_cast<int64_t>(t) * a.n_used, a.wts + static_cast<int64_t>(t) * a.n_used);
     __threadfence();
     __syncthreads();
-    if (tid == 0) {
+    if (n_tc > 1) {
+        // the permute needs every chunk's ids: the last chunk does it
+        if (tid == 0) {
+            a.cnt[tc] = 0;
+            s_last = atomicAdd(&a.cnt[n_tc], 1u) == static_cast<unsigned>(n_tc - 1);
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+    } else if (tid == 0) {
         a.cnt[tc] = 0;
-        s_last = atomicAdd(&a.cnt[n_tc], 1u) == static_cast<unsigned>(n_tc - 1);
     }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
     const int32_t *ids = a.ids;
     group_slots_warp([&](int s) { return __ldcg(ids + s); }, a.T * a.n_used, a.E, a.eoff, a.slots, a.act, sm_route,
                      sm_route + 8 * MOE_MAX_E);
-    if (tid == 0) a.cnt[n_tc] = 0;
+    if (tid == 0 && n_tc > 1) a.cnt[n_tc] = 0;
 }
 
 // permute for caller-given ids [T, n_used] (row stride ids_ld); out-of-range
