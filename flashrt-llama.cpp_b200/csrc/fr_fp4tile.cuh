@@ -164,6 +164,36 @@ __device__ __forceinline__ void ft_sum_parts(F part, int n, int T, int erow, flo
     }
 }
 
+// a[t] (and b[t]) += the partial slices k = 1..n-1 of this thread's row, in
+// k order (the owner's own slice 0 is already in a / b); the loads of
+// several slices are issued together
+template <int TMAX, bool DUAL, typename F>
+__device__ __forceinline__ void ft_add_parts(F part, int n, int T, int erow, float (&a)[TMAX], float (&b)[TMAX]) {
+    constexpr int CH = 32 / (TMAX * (DUAL ? 2 : 1)) > 0 ? 32 / (TMAX * (DUAL ? 2 : 1)) : 1;
+    for (int k0 = 1; k0 < n; k0 += CH) {
+        float va[CH][TMAX], vb[CH][TMAX];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const float *pc = part(min(k0 + c, n - 1));
+#pragma unroll
+            for (int t = 0; t < TMAX; ++t) {
+                va[c][t] = t < T ? __ldcg(pc + t * 128 + erow) : 0.0f;
+                vb[c][t] = (DUAL && t < T) ? __ldcg(pc + TMAX * 128 + t * 128 + erow) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            if (k0 + c < n) {
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) {
+                    a[t] += va[c][t];
+                    if (DUAL) b[t] += vb[c][t];
+                }
+            }
+        }
+    }
+}
+
 template <int NCOL, int EPI, int NT>
 __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(const FtArgs g) {
     using S = FtShape<NCOL, EPI, NT>;
@@ -387,29 +417,59 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
 #pragma unroll
                 for (int t = 0; t < TMAX; ++t) publish(rb, t, finish(rb, t, acc0[t], acc1[t]));
             } else {
+                // a row block shared with neighbouring CTAs.  Its owner is the
+                // CTA holding its first unit, for which it is the last
+                // segment; the others hold its later units at the start of
+                // their ranges (or all of their range), so their parts are
+                // usually in before the owner's.  They publish; the owner
+                // waits (bounded) for them and adds them after its own, in CTA
+                // order -- the sum the last-arriver form made, without the
+                // owner's own store, fence and atomic on the critical path.
                 const int c_first = ft_owner(rb * nsr, U, G);
                 const int nparts = ft_owner((rb + 1) * nsr - 1, U, G) - c_first + 1;
                 const int slot = static_cast<int>(blockIdx.x) - c_first;
-                float *pp = g.part + ((static_cast<int64_t>(rb) * g.maxp + slot) * 2) * TMAX * 128;
+                unsigned int *cnt = &g.counter[rb * 4 + q];
+                if (slot > 0) {
+                    float *pp = g.part + ((static_cast<int64_t>(rb) * g.maxp + slot) * 2) * TMAX * 128;
 #pragma unroll
-                for (int t = 0; t < TMAX; ++t) {
-                    pp[t * 128 + erow] = acc0[t];
-                    if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
-                }
-                fence_acq_rel_gpu();
-                __syncwarp();
-                unsigned prev = 0;
-                if (lane == 0) prev = atomicAdd(&g.counter[rb * 4 + q], 1u);
-                prev = __shfl_sync(0xffffffffu, prev, 0);
-                if (prev == static_cast<unsigned>(nparts - 1)) {
+                    for (int t = 0; t < TMAX; ++t) {
+                        pp[t * 128 + erow] = acc0[t];
+                        if (DUAL) pp[TMAX * 128 + t * 128 + erow] = acc1[t];
+                    }
                     fence_acq_rel_gpu();
-                    const float *pb = g.part + (static_cast<int64_t>(rb) * g.maxp * 2) * TMAX * 128;
-                    float s0[TMAX], s1[TMAX];
-                    ft_sum_parts<TMAX, DUAL>([&](int k2) { return pb + (k2 * 2) * TMAX * 128; }, nparts, T, erow,
-                                             s0, s1);
+                    __syncwarp();
+                    if (lane == 0) atomicAdd(cnt, 1u);
+                } else {
+                    int got = 1;
+                    if (lane == 0) {
+                        const uint64_t t0w = fr_now_ns();
+                        for (;;) {
+                            unsigned int fv;
+                            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(fv) : "l"(cnt) : "memory");
+                            if (fv >= static_cast<unsigned>(nparts - 1)) break;
+                            if (fr_now_ns() - t0w > g_fr_wait_ns) {
+                                fr_flag(FR_ST_TIMEOUT | (58u << FR_ST_SITE_SHIFT));
+                                got = 0;
+                                break;
+                            }
+                        }
+                        if (got) *cnt = 0u;                  // nobody touches it again before the next launch
+                    }
+                    got = __shfl_sync(0xffffffffu, got, 0);
+                    if (got) {
+                        fence_acq_rel_gpu();
+                        const float *pb = g.part + (static_cast<int64_t>(rb) * g.maxp * 2) * TMAX * 128;
+                        float s0[TMAX], s1[TMAX];
 #pragma unroll
-                    for (int t = 0; t < TMAX; ++t) publish(rb, t, finish(rb, t, s0[t], s1[t]));
-                    if (lane == 0) g.counter[rb * 4 + q] = 0;
+                        for (int t = 0; t < TMAX; ++t) {
+                            s0[t] = 0.0f + acc0[t];
+                            s1[t] = 0.0f + acc1[t];
+                        }
+                        ft_add_parts<TMAX, DUAL>([&](int k2) { return pb + (k2 * 2) * TMAX * 128; }, nparts, T, erow,
+                                                 s0, s1);
+#pragma unroll
+                        for (int t = 0; t < TMAX; ++t) publish(rb, t, finish(rb, t, s0[t], s1[t]));
+                    }
                 }
             }
             s0u = s1u;
