@@ -690,6 +690,21 @@ def run_profile_case(args):
             torch.cuda.synchronize()
         print(f"profile case done: {args.steps} GEMMs, M={M}, status {frb200.device_status()}")
         return
+    if args.case == "decoder":
+        # a 4-layer configs[4] decoder (--layout for the dense and expert
+        # weights), 8 prompt tokens then --steps decode steps, eager
+        from frb200.decoder import Config, MoeDecoder
+        T = args.tokens
+        cfg = Config(n_layers=4, ctx=2048)
+        dec = MoeDecoder(cfg, T, dense=args.layout, experts=args.layout, device=dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(0x5EED7100 + T)
+        dec.set_prompt(torch.randint(0, cfg.vocab, (T, 8), generator=g, device=dev, dtype=torch.int32))
+        for i in range(8 + args.steps):
+            dec.step()
+            torch.cuda.synchronize()
+        print(f"profile case done: {8 + args.steps} decoder steps, T={T}, 4 layers, status {frb200.device_status()}")
+        return
     if args.case == "attn":
         # decode attention (configs[4] shapes): --tokens sequences, keys
         # 0..1023 of a 2048-row f16 cache per layer, 4 layers rotating
@@ -759,7 +774,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step of --profile-case")
     ap.add_argument("--matvec", type=int, default=None, help="force the matvec kernel (1 dp4a, 2 tc-f16, 3 tc-fp4)")
     ap.add_argument("--layout", choices=["ggml", "tiled"], default="ggml", help="weight layout of --profile-case")
-    ap.add_argument("--case", choices=["ffn", "moe", "gemm", "attn"], default="ffn", help="workload of --profile-case")
+    ap.add_argument("--case", choices=["ffn", "moe", "gemm", "attn", "decoder"], default="ffn",
+                    help="workload of --profile-case")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)

@@ -28,29 +28,58 @@ constexpr int AT_CH = 128;         // keys per CTA (one split)
 constexpr int AT_THREADS = 128;
 
 // ------------------------------------------------------------------ RMSNorm
-// y = x / sqrt(mean(x^2) + eps) * w (w nullable = 1); one CTA per row.
+// y = x / sqrt(mean(x^2) + eps) * w (w nullable = 1); one CTA per row.  Each
+// thread loads all of its values (and weights) at once -- a decode step runs
+// two of these per layer at T = 1, where latency is all there is.
+constexpr int RN_MAXV = 8;           // float4 per thread: the vector path covers H <= 8192
 __global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w,
                                                  float *__restrict__ y, int H, float eps) {
     fr_pdl_wait();
     fr_pdl_trigger();
     const float *xr = x + static_cast<int64_t>(blockIdx.x) * H;
+    float *yr = y + static_cast<int64_t>(blockIdx.x) * H;
+    const bool vec = (H & 3) == 0 && H <= 4 * 256 * RN_MAXV && (reinterpret_cast<uintptr_t>(xr) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(yr) & 15) == 0 && (w == nullptr || (reinterpret_cast<uintptr_t>(w) & 15) == 0);
+    const int H4 = H >> 2;
+    float4 v[RN_MAXV], wv[RN_MAXV];
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    if (vec) {
+#pragma unroll
+        for (int u = 0; u < RN_MAXV; ++u) {
+            const int k = threadIdx.x + u * 256;
+            v[u] = k < H4 ? reinterpret_cast<const float4 *>(xr)[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            wv[u] = (w != nullptr && k < H4) ? reinterpret_cast<const float4 *>(w)[k] : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        }
+#pragma unroll
+        for (int u = 0; u < RN_MAXV; ++u)
+            ss = fmaf(v[u].w, v[u].w, fmaf(v[u].z, v[u].z, fmaf(v[u].y, v[u].y, fmaf(v[u].x, v[u].x, ss))));
+    } else {
+        for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    }
     __shared__ float red[32];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (threadIdx.x == 0) red[0] = v;
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (threadIdx.x == 0) red[0] = t;
     }
     __syncthreads();
     const float scale = rsqrtf(red[0] / static_cast<float>(H) + eps);
-    float *yr = y + static_cast<int64_t>(blockIdx.x) * H;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) yr[i] = w ? xr[i] * scale * w[i] : xr[i] * scale;
+    if (vec) {
+#pragma unroll
+        for (int u = 0; u < RN_MAXV; ++u) {
+            const int k = threadIdx.x + u * 256;
+            if (k < H4)
+                reinterpret_cast<float4 *>(yr)[k] = make_float4(v[u].x * scale * wv[u].x, v[u].y * scale * wv[u].y,
+                                                                v[u].z * scale * wv[u].z, v[u].w * scale * wv[u].w);
+        }
+    } else {
+        for (int i = threadIdx.x; i < H; i += blockDim.x) yr[i] = w ? xr[i] * scale * w[i] : xr[i] * scale;
+    }
 }
 
 // ------------------------------------------------------------ RoPE + KV append
@@ -59,7 +88,9 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, co
 // theta in f32 -- the arithmetic of ggml's rope_neox as the reference's QKV
 // post restates it (src/fr_qkv_post.cu:71-131, no YaRN correction, freq_scale
 // and attn_factor 1); q rows scaled by qscale; K and V rows of the step stored
-// as f16 at row *pos of the layer's cache.  grid (T).
+// as f16 at row *pos of the layer's cache.  grid (T, ceil((nh + nkv) / 4)),
+// 256 threads: thread = one rotated pair of one of the CTA's four heads (its
+// loads, power and cos / sin issued at once), plus a slice of the V row.
 __global__ void __launch_bounds__(256) k_rope_kv(const float *__restrict__ qkv, const int32_t *__restrict__ pos_p,
                                                  float *__restrict__ q_r, __half *__restrict__ kc,
                                                  __half *__restrict__ vc, int nh, int nkv, int ctx, float base,
@@ -71,13 +102,17 @@ __global__ void __launch_bounds__(256) k_rope_kv(const float *__restrict__ qkv, 
     const int half = AT_D / 2;
     const int width = (nh + 2 * nkv) * AT_D;
     const float *row = qkv + static_cast<int64_t>(t) * width;
-    // rotated pairs of the q and k heads
-    const float theta_scale = powf(base, -2.0f / static_cast<float>(AT_D));
-    for (int i = threadIdx.x; i < (nh + nkv) * half; i += blockDim.x) {
-        const int hd = i / half, j = i % half;
+    const int hd = blockIdx.y * 4 + (threadIdx.x >> 6), j = threadIdx.x & 63;
+    // this CTA's slice of the V row (loaded with the pair)
+    const int nv = nkv * AT_D, per_v = (nv + gridDim.y - 1) / gridDim.y;
+    const int vi = blockIdx.y * per_v + threadIdx.x;
+    const bool has_v = threadIdx.x < per_v && vi < nv;
+    const float vv = has_v ? row[(nh + nkv) * AT_D + vi] : 0.0f;
+    if (hd < nh + nkv) {
+        const float a = row[hd * AT_D + j], b = row[hd * AT_D + j + half];
+        const float theta_scale = powf(base, -2.0f / static_cast<float>(AT_D));
         const float theta = static_cast<float>(pos) * powf(theta_scale, static_cast<float>(j));
         const float cs = cosf(theta), sn = sinf(theta);
-        const float a = row[hd * AT_D + j], b = row[hd * AT_D + j + half];
         const float ra = a * cs - b * sn, rb = a * sn + b * cs;
         if (hd < nh) {
             float *qo = q_r + (static_cast<int64_t>(t) * nh + hd) * AT_D;
@@ -90,11 +125,9 @@ __global__ void __launch_bounds__(256) k_rope_kv(const float *__restrict__ qkv, 
             ko[j + half] = __float2half_rn(rb);
         }
     }
-    // V rows copied as f16
-    for (int i = threadIdx.x; i < nkv * AT_D; i += blockDim.x) {
-        const int g = i / AT_D, c = i % AT_D;
-        vc[((static_cast<int64_t>(t) * nkv + g) * ctx + pos) * AT_D + c] =
-            __float2half_rn(row[(nh + nkv) * AT_D + i]);
+    if (has_v) {
+        const int g = vi / AT_D, c = vi % AT_D;
+        vc[((static_cast<int64_t>(t) * nkv + g) * ctx + pos) * AT_D + c] = __float2half_rn(vv);
     }
 }
 
@@ -144,38 +177,61 @@ __global__ void __launch_bounds__(256) k_embed_nvfp4(const uint8_t *__restrict__
 
 // ------------------------------------------------------------------- arg-max
 // tok[t] = argmax_v logits[t, v] (ties: the lowest index; NaN never wins).
-// One CTA per row.
-__global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ logits, int V, int32_t *__restrict__ tok) {
+// grid (AM_SLICES, T): each CTA scans a contiguous slice with its loads in
+// flight together and leaves (max, index); the last CTA of the row (arrival
+// counter) reduces the slices.  The (value, index) order with ties to the
+// lower index is a total order, so the reduction order does not matter.
+constexpr int AM_SLICES = 64;
+__device__ __forceinline__ void am_take(float &best, int &bi, float ob, int oi) {
+    if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+}
+__global__ void __launch_bounds__(256) k_argmax(const float *__restrict__ logits, int V, int32_t *__restrict__ tok,
+                                                float *__restrict__ part_v, int *__restrict__ part_i,
+                                                unsigned int *__restrict__ cnt) {
     fr_pdl_wait();
     fr_pdl_trigger();
-    const float *r = logits + static_cast<int64_t>(blockIdx.x) * V;
+    const int t = blockIdx.y, sl = blockIdx.x, ns = gridDim.x;
+    const float *r = logits + static_cast<int64_t>(t) * V;
+    const int per = (V + ns - 1) / ns;
+    const int v0 = sl * per, v1 = min(V, v0 + per);
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        const float f = r[v];
-        if (f > best) { best = f; bi = v; }      // v ascending per thread: the first max is kept
+    for (int b = v0 + threadIdx.x; b < v1; b += 8 * 256) {
+        float f[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) f[u] = (b + u * 256 < v1) ? r[b + u * 256] : -INFINITY;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) am_take(best, bi, f[u], b + u * 256);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-    }
-    __shared__ float sb[32];
-    __shared__ int si[32];
+    for (int o = 16; o > 0; o >>= 1)
+        am_take(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    __shared__ float sb[8];
+    __shared__ int si[8];
+    __shared__ int s_last;
     if ((threadIdx.x & 31) == 0) { sb[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
     __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) am_take(sb[0], si[0], sb[w], si[w]);
+        part_v[t * ns + sl] = sb[0];
+        part_i[t * ns + sl] = si[0];
+        __threadfence();
+        s_last = atomicAdd(&cnt[t], 1u) == static_cast<unsigned>(ns - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
     if (threadIdx.x < 32) {
-        const bool in = threadIdx.x < (blockDim.x >> 5);
-        best = in ? sb[threadIdx.x] : -INFINITY;
-        bi = in ? si[threadIdx.x] : 0x7fffffff;
+        __threadfence();
+        best = -INFINITY;
+        bi = 0x7fffffff;
+        for (int k = threadIdx.x; k < ns; k += 32) am_take(best, bi, __ldcg(part_v + t * ns + k), __ldcg(part_i + t * ns + k));
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        for (int o = 16; o > 0; o >>= 1)
+            am_take(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+        if (threadIdx.x == 0) {
+            tok[t] = bi == 0x7fffffff ? 0 : bi;
+            cnt[t] = 0u;
         }
-        if (threadIdx.x == 0) tok[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
     }
 }
 

@@ -2725,7 +2725,8 @@ int fr_rope_kv_f16(const float *qkv, const int32_t *pos, float *q_r, void *kcach
     if (fault_hit("fr_rope_kv_f16")) return FR_EINJECTED;
     if (!qkv || !pos || !q_r || !kcache || !vcache || T <= 0 || nh <= 0 || nkv <= 0 || ctx <= 0) return FR_EINVAL;
     if (head_dim != AT_D) return FR_EINVAL;
-    return launch_pdl(k_rope_kv, dim3(T), dim3(256), 0, stream, qkv, pos, q_r, static_cast<__half *>(kcache),
+    return launch_pdl(k_rope_kv, dim3(T, (nh + nkv + 3) / 4), dim3(256), 0, stream, qkv, pos, q_r,
+                      static_cast<__half *>(kcache),
                       static_cast<__half *>(vcache), nh, nkv, ctx, rope_base, 1.0f / sqrtf(static_cast<float>(AT_D)));
 }
 
@@ -2769,8 +2770,17 @@ int fr_embed_nvfp4(const void *table, int vocab, int H, const int32_t *prompt, i
 
 int fr_argmax_f32(const float *logits, int T, int V, int32_t *tok, cudaStream_t stream) {
     if (fault_hit("fr_argmax_f32")) return FR_EINJECTED;
-    if (!logits || !tok || T <= 0 || V <= 0) return FR_EINVAL;
-    return launch_pdl(k_argmax, dim3(T), dim3(1024), 0, stream, logits, V, tok);
+    if (!logits || !tok || T <= 0 || V <= 0 || T > 65535) return FR_EINVAL;
+    // per-slice maxima and the rows' arrival counters (zero between calls)
+    void *part = nullptr, *cnt = nullptr;
+    int rc = workspace_get(WS_ARGMAX, static_cast<size_t>(T) * AM_SLICES * 8, stream, &part);
+    if (rc != FR_OK) return rc;
+    rc = workspace_get_zeroed(WS_AMCNT, static_cast<size_t>(T) * sizeof(unsigned int), stream, &cnt);
+    if (rc != FR_OK) return rc;
+    float *pv = static_cast<float *>(part);
+    int *pi = reinterpret_cast<int *>(pv + static_cast<size_t>(T) * AM_SLICES);
+    return launch_pdl(k_argmax, dim3(AM_SLICES, T), dim3(256), 0, stream, logits, V, tok, pv, pi,
+                      static_cast<unsigned int *>(cnt));
 }
 
 int fr_pos_advance(int32_t *pos, cudaStream_t stream) {

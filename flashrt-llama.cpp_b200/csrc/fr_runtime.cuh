@@ -87,7 +87,8 @@ int workspace_get(int purpose, size_t bytes, cudaStream_t stream, void **out);
 
 enum WsPurpose : int { WS_Q8 = 0, WS_GLU = 1, WS_GLUQ8 = 2, WS_MOE = 3, WS_ACT = 4, WS_TGPART = 5, WS_ACT2 = 6,
                        WS_FP4 = 7, WS_FE = 8, WS_ROUTE = 9, WS_AMAX = 10,
-                       WS_MOECNT = 11, WS_GPART = 12, WS_GCNT = 13, WS_ATPART = 14, WS_ATCNT = 15, WS_COUNT = 16 };
+                       WS_MOECNT = 11, WS_GPART = 12, WS_GCNT = 13, WS_ATPART = 14, WS_ATCNT = 15, WS_ARGMAX = 16, WS_AMCNT = 17,
+                       WS_COUNT = 18 };
 
 // Same, but the buffer is zero-filled whenever it is (re)allocated (for
 // counters that kernels keep at zero between calls).
