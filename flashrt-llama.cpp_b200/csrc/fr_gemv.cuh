@@ -299,8 +299,11 @@ __device__ __forceinline__ void gv_block_reg(const uint32_t *blk, const ActBlk<T
 // [(w*(32/LG) + g) * R2, +R2) with lane group g), so each ring slot is waited
 // on by every warp in phase order and freed by eight arrivals.  Stages are
 // 16-74 KB: large enough that one bulk copy per operand keeps HBM busy.
+// One-row-group, one-token forms (small matvecs: the decode step's QKV / O,
+// configs[0]) are compiled for two CTAs per SM, so the next launch's CTAs can
+// start streaming their weights while this one's finish.
 template <int LG, int TT, int EPI, int R2, int CW>
-__global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(const GvParams p) {
+__global__ void __launch_bounds__((CW + 1) * 32, (TT == 1 && R2 == 1) ? 2 : 1) k_gemv(const GvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NS = p.n_slots;
