@@ -473,21 +473,43 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
     }
     __syncthreads();
     if (*flag) {
+        // merge: every split's (m, l) into shared memory with all loads in
+        // flight, the per-head weights exp(m_s - max) once, then each thread
+        // (= head dimension) its outputs with its split loads issued together
         __threadfence();
         const int ns = min(splits, (n + AT_CH - 1) / AT_CH);
         const float *base = a.part + (static_cast<int64_t>(t) * a.nkv + g) * splits * AT_PART;
+        float *ml = reinterpret_cast<float *>(Vt);        // [split][16]: m[8], l[8]; then w [split][8]
+        float *wts = ml + 16 * ns;
+        for (int i = tid; i < 16 * ns; i += AT_THREADS) ml[i] = __ldcg(base + (i >> 4) * AT_PART + (i & 15));
+        __syncthreads();
+        if (tid < AT_G) {
+            float mx = -INFINITY;
+            for (int s2 = 0; s2 < ns; ++s2) mx = fmaxf(mx, ml[s2 * 16 + tid]);
+            float lsum = 0.0f;
+            for (int s2 = 0; s2 < ns; ++s2) {
+                const float w = expf(ml[s2 * 16 + tid] - mx);
+                wts[s2 * 8 + tid] = w;
+                lsum = fmaf(w, ml[s2 * 16 + 8 + tid], lsum);
+            }
+            red[tid] = lsum;                           // (the softmax's scratch is free by now)
+        }
+        __syncthreads();
         const int d = tid;
+        constexpr int MS = 16;                         // splits whose loads go out together
 #pragma unroll 1
         for (int h = 0; h < AT_G; ++h) {
-            float mx = -INFINITY;
-            for (int s2 = 0; s2 < ns; ++s2) mx = fmaxf(mx, __ldcg(base + s2 * AT_PART + h));
-            float lsum = 0.0f, o = 0.0f;
-            for (int s2 = 0; s2 < ns; ++s2) {
-                const float w = expf(__ldcg(base + s2 * AT_PART + h) - mx);
-                lsum = fmaf(w, __ldcg(base + s2 * AT_PART + 8 + h), lsum);
-                o = fmaf(w, __ldcg(base + s2 * AT_PART + 16 + h * AT_D + d), o);
+            float o = 0.0f;
+            for (int s0 = 0; s0 < ns; s0 += MS) {
+                float v[MS];
+#pragma unroll
+                for (int u = 0; u < MS; ++u)
+                    v[u] = s0 + u < ns ? __ldcg(base + (s0 + u) * AT_PART + 16 + h * AT_D + d) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < MS; ++u)
+                    if (s0 + u < ns) o = fmaf(wts[(s0 + u) * 8 + h], v[u], o);
             }
-            a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h) * AT_D + d] = o / lsum;
+            a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h) * AT_D + d] = o / red[h];
         }
     }
     fr_pdl_trigger();
