@@ -496,20 +496,28 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
         }
         __syncthreads();
         const int d = tid;
-        constexpr int MS = 16;                         // splits whose loads go out together
+        constexpr int MS = 16, MH = 4;                 // splits x heads whose loads go out together
 #pragma unroll 1
-        for (int h = 0; h < AT_G; ++h) {
-            float o = 0.0f;
+        for (int h0 = 0; h0 < AT_G; h0 += MH) {
+            float o[MH];
+#pragma unroll
+            for (int hh = 0; hh < MH; ++hh) o[hh] = 0.0f;
             for (int s0 = 0; s0 < ns; s0 += MS) {
-                float v[MS];
+                float v[MH][MS];
 #pragma unroll
-                for (int u = 0; u < MS; ++u)
-                    v[u] = s0 + u < ns ? __ldcg(base + (s0 + u) * AT_PART + 16 + h * AT_D + d) : 0.0f;
+                for (int hh = 0; hh < MH; ++hh)
 #pragma unroll
-                for (int u = 0; u < MS; ++u)
-                    if (s0 + u < ns) o = fmaf(wts[(s0 + u) * 8 + h], v[u], o);
+                    for (int u = 0; u < MS; ++u)
+                        v[hh][u] = s0 + u < ns ? __ldcg(base + (s0 + u) * AT_PART + 16 + (h0 + hh) * AT_D + d) : 0.0f;
+#pragma unroll
+                for (int hh = 0; hh < MH; ++hh)
+#pragma unroll
+                    for (int u = 0; u < MS; ++u)
+                        if (s0 + u < ns) o[hh] = fmaf(wts[(s0 + u) * 8 + h0 + hh], v[hh][u], o[hh]);
             }
-            a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h) * AT_D + d] = o / red[h];
+#pragma unroll
+            for (int hh = 0; hh < MH; ++hh)
+                a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h0 + hh) * AT_D + d] = o[hh] / red[h0 + hh];
         }
     }
     fr_pdl_trigger();
