@@ -692,11 +692,13 @@ def run_profile_case(args):
         return
     if args.case == "decoder":
         # a 4-layer configs[4] decoder (--layout for the dense and expert
-        # weights), 8 prompt tokens then --steps decode steps, eager
+        # weights; mixed = the batch-64 bench's ggml dense, tiled experts),
+        # 8 prompt tokens then --steps decode steps, eager
         from frb200.decoder import Config, MoeDecoder
         T = args.tokens
         cfg = Config(n_layers=4, ctx=2048)
-        dec = MoeDecoder(cfg, T, dense=args.layout, experts=args.layout, device=dev)
+        dense, experts = ("ggml", "tiled") if args.layout == "mixed" else (args.layout, args.layout)
+        dec = MoeDecoder(cfg, T, dense=dense, experts=experts, device=dev)
         g = torch.Generator(device=dev)
         g.manual_seed(0x5EED7100 + T)
         dec.set_prompt(torch.randint(0, cfg.vocab, (T, 8), generator=g, device=dev, dtype=torch.int32))
@@ -773,7 +775,8 @@ def main():
                     help="run a short fixed kernel sequence for profiler captures (no benchmark line)")
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step of --profile-case")
     ap.add_argument("--matvec", type=int, default=None, help="force the matvec kernel (1 dp4a, 2 tc-f16, 3 tc-fp4)")
-    ap.add_argument("--layout", choices=["ggml", "tiled"], default="ggml", help="weight layout of --profile-case")
+    ap.add_argument("--layout", choices=["ggml", "tiled", "mixed"], default="ggml",
+                    help="weight layout of --profile-case (mixed: decoder dense ggml, experts tiled)")
     ap.add_argument("--case", choices=["ffn", "moe", "gemm", "attn", "decoder"], default="ffn",
                     help="workload of --profile-case")
     args = ap.parse_args()

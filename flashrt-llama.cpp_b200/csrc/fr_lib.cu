@@ -1303,6 +1303,19 @@ static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, 
     const int Kp = (K + 255) / 256 * 256;
     const int n_kt = Kp / 256;
     int ksplit = std::max(1, std::min(n_kt, (128 * G) / std::max(1, N)));
+    // each split's partial is 2 x TW x 128 floats per row tile (twice for
+    // the SwiGLU pair), summed by the tile's last CTA: when a CTA's share of
+    // the weights is under twice that, the hand-off costs more than the SMs
+    // the split adds (T=64: 5120x2048 52.6 -> 20.5 us, 2048x4096 51.8 ->
+    // 32.7 us unsplit; 4096x14336 keeps its split)
+    {
+        const double w_per_cta = static_cast<double>(N) * K * 36.0 / 64.0 / G;
+        const double part_bytes = 2.0 * TW * 128 * 4 * (dual ? 2 : 1);
+        if (w_per_cta < 2.0 * part_bytes) ksplit = 1;
+    }
+    // tuning cap (FR_TC_KSPLIT_MAX)
+    static const char *kv = getenv("FR_TC_KSPLIT_MAX");
+    if (kv && *kv) ksplit = std::max(1, std::min(ksplit, atoi(kv)));
     const int kt_per = (n_kt + ksplit - 1) / ksplit;
     ksplit = (n_kt + kt_per - 1) / kt_per;
     const int R = std::min(128, std::max(1, static_cast<int>((static_cast<int64_t>(N) * ksplit + G - 1) / G)));

@@ -82,6 +82,8 @@ GEMV_CASES = [
     (517, 4096, 4),
     (129, 4096, 8),
     (77, 1024, 13),       # several token windows
+    (5120, 2048, 64),     # configs[4] QKV at batch 64 (the f16 kernel unsplit along K)
+    (2048, 4096, 64),     # configs[4] attention output at batch 64
 ]
 
 
