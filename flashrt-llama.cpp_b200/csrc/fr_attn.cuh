@@ -24,8 +24,8 @@ namespace frb {
 
 constexpr int AT_D = 128;          // head dimension
 constexpr int AT_G = 8;            // query heads per KV head (32 / 4)
-constexpr int AT_CH = 128;         // keys per CTA (one split)
-constexpr int AT_THREADS = 128;
+constexpr int AT_CH = 128;          // keys per chunk
+constexpr int AT_THREADS = 256;    // two head groups of four per key
 
 // ------------------------------------------------------------------ RMSNorm
 // y = x / sqrt(mean(x^2) + eps) * w (w nullable = 1); one CTA per row.  Each
@@ -253,17 +253,22 @@ __global__ void __launch_bounds__(256) k_copy16(const uint4 *__restrict__ src, u
 }
 
 // ------------------------------------------------------ GQA decode attention
-// One CTA per (split of AT_CH keys, KV head g, sequence t): the KV head's
-// keys [s * 128, s * 128 + 128) of sequence t against its 8 query heads,
-// both matmuls on the tensor cores (tcgen05.mma kind::f16, f32 in TMEM):
+// CTA (s, g, t) of a grid (S, nkv, T) handles KV head g of sequence t over the
+// key chunks s, s + S, s + 2S, ... of AT_CH keys below the step's length, both
+// matmuls of a chunk on the tensor cores (tcgen05.mma kind::f16, f32 in TMEM):
 //   S^T [128 keys x 16] = K_chunk [128 x 128] . Q^T   (Q: 8 heads, 8 zero rows)
 //   softmax over the keys (thread = key = TMEM lane), P^T in f16
 //   O^T [128 dims x 16] = V_chunk^T [128 x 128] . P^T (V transposed in shared memory)
-// so K and V are read once per KV head for all 8 heads.  Each split writes
-// (m, l, o) per head; the last CTA of (t, g) to finish merges the splits in
-// split order (deterministic) into out.  K / V chunks arrive by TMA
-// (128-byte swizzle) straight from the cache; rows past the step's keys are
-// masked (the cache is zero-initialised, so they are finite).
+// so K and V are read once per KV head for all 8 heads.  Across its chunks a
+// CTA keeps the running max m, sum l and output o per head (online softmax,
+// o in registers: thread = head dimension x 4 heads); the next chunk's K / V
+// TMA is issued as soon as the current chunk's K and V have been consumed, so
+// it overlaps the softmax and the P.V product.  With S = 1 the CTA writes
+// o / l directly; otherwise each CTA writes (m, l, o) and the last CTA of
+// (t, g) to finish merges the splits in split order (deterministic).  The
+// host picks S so that the grid fills the SMs (S = ctx / AT_CH at T = 1, one
+// CTA per (t, g) at batch 64).  Rows past the step's keys are masked (the
+// cache is zero-initialised, so they are finite).
 struct AtArgs {
     const float *q;              // [T, nh, d], RoPE'd, pre-scaled
     const int32_t *pos;          // keys = *pos + 1
@@ -302,13 +307,18 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
     uint8_t *Vt = Vs + 2 * AT_SLAB;            // 2 slabs: dims x keys [0, 64) and [64, 128)
     uint8_t *Qs = Vt + 2 * AT_SLAB;            // 2 slabs: 16 heads x dims
     uint8_t *Pt = Qs + 2 * AT_QSLAB;           // 2 slabs: 16 heads x keys
-    float *red = reinterpret_cast<float *>(Pt + 2 * AT_QSLAB);     // [4 warps][8] x 2, then M[8], L[8]
+    float *red = reinterpret_cast<float *>(Pt + 2 * AT_QSLAB);     // [4][8] maxima, [4][8] sums, M, L, alpha
     uint64_t *bars = reinterpret_cast<uint64_t *>(red + 96);       // tma, mma
     uint32_t *tmem_s = reinterpret_cast<uint32_t *>(bars + 2);
     int *flag = reinterpret_cast<int *>(tmem_s + 1);
+    float *M = red + 64, *L = red + 72, *AL = red + 80;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+    // thread = TMEM lane kd = wq * 32 + lane (a key of the chunk for the
+    // scores, a head dimension for the output) x heads [4 hg, 4 hg + 4)
+    const int wq = warp & 3, hg = warp >> 2;
+    const int kd = wq * 32 + lane;
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -323,20 +333,22 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
     const uint32_t tm = *tmem_s;
     fr_pdl_wait();                                     // q, the cache rows and pos come from earlier kernels
     const int n = *a.pos + 1;
-    const int k0 = s * AT_CH;
+    const int nch = (n + AT_CH - 1) / AT_CH;           // chunks holding the step's keys
     const int splits = gridDim.x;
+    const int row_base = (t * a.nkv + g) * a.ctx;
     float *part = a.part + ((static_cast<int64_t>(t) * a.nkv + g) * splits + s) * AT_PART;
-    bool ok = true;
-    if (k0 < n) {
-        const int nk = min(AT_CH, n - k0);
+    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    bool ok = true, tma_pending = false;
+    uint32_t ph0 = 0, ph1 = 0;
+    if (s < nch) {
         if (tid == 0) {
-            const int row0 = (t * a.nkv + g) * a.ctx + k0;
             mbar_expect_tx(&bars[0], 4 * AT_SLAB);
-            tma_load_2d(Ks, &tmK, 0, row0, &bars[0]);
-            tma_load_2d(Ks + AT_SLAB, &tmK, 64, row0, &bars[0]);
-            tma_load_2d(Vs, &tmV, 0, row0, &bars[0]);
-            tma_load_2d(Vs + AT_SLAB, &tmV, 64, row0, &bars[0]);
+            tma_load_2d(Ks, &tmK, 0, row_base + s * AT_CH, &bars[0]);
+            tma_load_2d(Ks + AT_SLAB, &tmK, 64, row_base + s * AT_CH, &bars[0]);
+            tma_load_2d(Vs, &tmV, 0, row_base + s * AT_CH, &bars[0]);
+            tma_load_2d(Vs + AT_SLAB, &tmV, 64, row_base + s * AT_CH, &bars[0]);
         }
+        tma_pending = true;
         // Q tile (f16, 128-byte swizzled K-major): 16 rows x 16 chunks of 8 dims; rows 8..15 zero
         for (int i = tid; i < 16 * 16; i += AT_THREADS) {
             const int h = i >> 4, c = i & 15;
@@ -358,169 +370,222 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
             *reinterpret_cast<uint4 *>(Pt + (c >> 3) * AT_QSLAB + h * 128 + (((c & 7) ^ (h & 7)) << 4)) =
                 make_uint4(0u, 0u, 0u, 0u);
         }
+        if (tid < AT_G) {
+            M[tid] = -INFINITY;
+            L[tid] = 0.0f;
+        }
         fence_proxy_async();
         __syncthreads();
-        ok = mbar_wait(&bars[0], 0, 50);
-        if (tid == 0 && ok) {
-            tc_fence_after();
-            const uint32_t idesc = idesc_f16_f32acc(128, 16);
-            for (int j = 0; j < 8; ++j) {
-                const int sl = j >> 2, ko = (j & 3) * 32;
-                tc_mma_f16_ss(tm, sdesc_sw128(smem_u32(Ks + sl * AT_SLAB) + ko),
-                              sdesc_sw128(smem_u32(Qs + sl * AT_QSLAB) + ko), idesc, j > 0 ? 1u : 0u);
-            }
-            tc_commit(&bars[1]);
-        }
-        if (ok) {
-            // V [keys x dims] -> V^T [dims x keys], 8x8 blocks of halves
-            for (int blk = tid; blk < 256; blk += AT_THREADS) {
-                const int kg = blk >> 4, dg = blk & 15;
-                uint32_t in[8][4];
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const int key = 8 * kg + r;
-                    const uint4 w = *reinterpret_cast<const uint4 *>(Vs + (dg >> 3) * AT_SLAB + key * 128 +
-                                                                      (((dg & 7) ^ (key & 7)) << 4));
-                    in[r][0] = w.x; in[r][1] = w.y; in[r][2] = w.z; in[r][3] = w.w;
-                }
-#pragma unroll
-                for (int d = 0; d < 8; ++d) {
-                    uint32_t o[4];
-#pragma unroll
-                    for (int r2 = 0; r2 < 4; ++r2) {
-                        const uint32_t lo = (in[2 * r2][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
-                        const uint32_t hi = (in[2 * r2 + 1][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
-                        o[r2] = lo | (hi << 16);
-                    }
-                    const int dim = 8 * dg + d;
-                    *reinterpret_cast<uint4 *>(Vt + (kg >> 3) * AT_SLAB + dim * 128 + (((kg & 7) ^ (dim & 7)) << 4)) =
-                        make_uint4(o[0], o[1], o[2], o[3]);
-                }
-            }
-            ok = mbar_wait(&bars[1], 0, 51);
-        }
-        tc_fence_after();
-        // scores: thread = key = TMEM lane
-        const int key = warp * 32 + lane;
-        float sv[AT_G];
-        {
-            uint32_t r[16];
-            tmem_ld16(tm + (static_cast<uint32_t>(warp * 32) << 16), r);
-#pragma unroll
-            for (int h = 0; h < AT_G; ++h) sv[h] = (ok && key < nk) ? __uint_as_float(r[h]) : -INFINITY;
-        }
-        float *M = red + 64, *L = red + 72;
-#pragma unroll
-        for (int h = 0; h < AT_G; ++h) {
-            float m = sv[h];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) red[warp * 8 + h] = m;
-        }
-        __syncthreads();
-        if (tid < AT_G) M[tid] = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
-        __syncthreads();
-#pragma unroll
-        for (int h = 0; h < AT_G; ++h) {
-            const float mh = M[h];
-            const __half p16 = __float2half_rn(key < nk && mh > -INFINITY ? expf(sv[h] - mh) : 0.0f);
-            float l = __half2float(p16);               // the sum of the probabilities the MMA multiplies
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            if (lane == 0) red[32 + warp * 8 + h] = l;
-            const int kk = key & 63;
-            *reinterpret_cast<__half *>(Pt + (key >> 6) * AT_QSLAB + h * 128 + (((kk >> 3) ^ (h & 7)) << 4) +
-                                        (kk & 7) * 2) = p16;
-        }
-        fence_proxy_async();
-        tc_fence_before();
-        __syncthreads();
-        if (tid < AT_G) L[tid] = (red[32 + tid] + red[40 + tid]) + (red[48 + tid] + red[56 + tid]);
-        if (tid == 0 && ok) {
-            tc_fence_after();
-            const uint32_t idesc = idesc_f16_f32acc(128, 16);
-            for (int j = 0; j < 8; ++j) {
-                const int sl = j >> 2, ko = (j & 3) * 32;
-                tc_mma_f16_ss(tm + 16, sdesc_sw128(smem_u32(Vt + sl * AT_SLAB) + ko),
-                              sdesc_sw128(smem_u32(Pt + sl * AT_QSLAB) + ko), idesc, j > 0 ? 1u : 0u);
-            }
-            tc_commit(&bars[1]);
-        }
-        if (ok) ok = mbar_wait(&bars[1], 1, 52);
-        tc_fence_after();
-        {
-            uint32_t r[16];
-            tmem_ld16(tm + (static_cast<uint32_t>(warp * 32) << 16) + 16, r);
-            const int d = warp * 32 + lane;             // thread = head dimension = TMEM lane
-#pragma unroll
-            for (int h = 0; h < AT_G; ++h) part[16 + h * AT_D + d] = ok ? __uint_as_float(r[h]) : 0.0f;
-        }
-        __syncthreads();
-        if (tid < AT_G) {
-            part[tid] = M[tid];
-            part[8 + tid] = L[tid];
-        }
-    }
-    // the last CTA of (t, g) merges the splits
-    __threadfence();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-        unsigned int *c = a.counter + t * a.nkv + g;
-        const unsigned prev = atomicAdd(c, 1u);
-        *flag = prev == static_cast<unsigned>(splits - 1);
-        if (*flag) *c = 0u;
-    }
-    __syncthreads();
-    if (*flag) {
-        // merge: every split's (m, l) into shared memory with all loads in
-        // flight, the per-head weights exp(m_s - max) once, then each thread
-        // (= head dimension) its outputs with its split loads issued together
-        __threadfence();
-        const int ns = min(splits, (n + AT_CH - 1) / AT_CH);
-        const float *base = a.part + (static_cast<int64_t>(t) * a.nkv + g) * splits * AT_PART;
-        float *ml = reinterpret_cast<float *>(Vt);        // [split][16]: m[8], l[8]; then w [split][8]
-        float *wts = ml + 16 * ns;
-        for (int i = tid; i < 16 * ns; i += AT_THREADS) ml[i] = __ldcg(base + (i >> 4) * AT_PART + (i & 15));
-        __syncthreads();
-        if (tid < AT_G) {
-            float mx = -INFINITY;
-            for (int s2 = 0; s2 < ns; ++s2) mx = fmaxf(mx, ml[s2 * 16 + tid]);
-            float lsum = 0.0f;
-            for (int s2 = 0; s2 < ns; ++s2) {
-                const float w = expf(ml[s2 * 16 + tid] - mx);
-                wts[s2 * 8 + tid] = w;
-                lsum = fmaf(w, ml[s2 * 16 + 8 + tid], lsum);
-            }
-            red[tid] = lsum;                           // (the softmax's scratch is free by now)
-        }
-        __syncthreads();
-        const int d = tid;
-        constexpr int MS = 16, MH = 4;                 // splits x heads whose loads go out together
 #pragma unroll 1
-        for (int h0 = 0; h0 < AT_G; h0 += MH) {
-            float o[MH];
+        for (int c = s; c < nch && ok; c += splits) {
+            const int nk = min(AT_CH, n - c * AT_CH);
+            ok = mbar_wait(&bars[0], ph0, 50);
+            if (ok) {
+                ph0 ^= 1u;
+                tma_pending = false;
+            }
+            if (tid == 0 && ok) {
+                tc_fence_after();
+                const uint32_t idesc = idesc_f16_f32acc(128, 16);
+                for (int j = 0; j < 8; ++j) {
+                    const int sl = j >> 2, ko = (j & 3) * 32;
+                    tc_mma_f16_ss(tm, sdesc_sw128(smem_u32(Ks + sl * AT_SLAB) + ko),
+                                  sdesc_sw128(smem_u32(Qs + sl * AT_QSLAB) + ko), idesc, j > 0 ? 1u : 0u);
+                }
+                tc_commit(&bars[1]);
+            }
+            if (ok) {
+                // V [keys x dims] -> V^T [dims x keys], 8x8 blocks of halves
+                for (int blk = tid; blk < 256; blk += AT_THREADS) {
+                    const int kg = blk >> 4, dg = blk & 15;
+                    uint32_t in[8][4];
 #pragma unroll
-            for (int hh = 0; hh < MH; ++hh) o[hh] = 0.0f;
-            for (int s0 = 0; s0 < ns; s0 += MS) {
-                float v[MH][MS];
+                    for (int r = 0; r < 8; ++r) {
+                        const int key = 8 * kg + r;
+                        const uint4 w = *reinterpret_cast<const uint4 *>(Vs + (dg >> 3) * AT_SLAB + key * 128 +
+                                                                          (((dg & 7) ^ (key & 7)) << 4));
+                        in[r][0] = w.x; in[r][1] = w.y; in[r][2] = w.z; in[r][3] = w.w;
+                    }
 #pragma unroll
-                for (int hh = 0; hh < MH; ++hh)
+                    for (int d = 0; d < 8; ++d) {
+                        uint32_t ov[4];
 #pragma unroll
-                    for (int u = 0; u < MS; ++u)
-                        v[hh][u] = s0 + u < ns ? __ldcg(base + (s0 + u) * AT_PART + 16 + (h0 + hh) * AT_D + d) : 0.0f;
+                        for (int r2 = 0; r2 < 4; ++r2) {
+                            const uint32_t lo = (in[2 * r2][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
+                            const uint32_t hi = (in[2 * r2 + 1][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
+                            ov[r2] = lo | (hi << 16);
+                        }
+                        const int dim = 8 * dg + d;
+                        *reinterpret_cast<uint4 *>(Vt + (kg >> 3) * AT_SLAB + dim * 128 +
+                                                   (((kg & 7) ^ (dim & 7)) << 4)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+                    }
+                }
+                ok = mbar_wait(&bars[1], ph1, 51);
+            }
+            ph1 ^= 1u;
+            // V^T stores before the P.V product, V reads before the next chunk's TMA
+            fence_proxy_async();
+            tc_fence_after();
+            float sv[4];
+            {
+                uint32_t r[16];
+                tmem_ld16(tm + (static_cast<uint32_t>(wq * 32) << 16), r);
 #pragma unroll
-                for (int hh = 0; hh < MH; ++hh)
-#pragma unroll
-                    for (int u = 0; u < MS; ++u)
-                        if (s0 + u < ns) o[hh] = fmaf(wts[(s0 + u) * 8 + h0 + hh], v[hh][u], o[hh]);
+                for (int h4 = 0; h4 < 4; ++h4)
+                    sv[h4] = (ok && kd < nk) ? __uint_as_float(r[4 * hg + h4]) : -INFINITY;
             }
 #pragma unroll
-            for (int hh = 0; hh < MH; ++hh)
-                a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h0 + hh) * AT_D + d] = o[hh] / red[h0 + hh];
+            for (int h4 = 0; h4 < 4; ++h4) {
+                float m = sv[h4];
+#pragma unroll
+                for (int sh = 16; sh > 0; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
+                if (lane == 0) red[wq * 8 + 4 * hg + h4] = m;
+            }
+            tc_fence_before();
+            ok = __syncthreads_and(ok) != 0;
+            // K and V of this chunk are consumed: the next chunk's copies go out now
+            if (ok && c + splits < nch) {
+                if (tid == 0) {
+                    const int row = row_base + (c + splits) * AT_CH;
+                    mbar_expect_tx(&bars[0], 4 * AT_SLAB);
+                    tma_load_2d(Ks, &tmK, 0, row, &bars[0]);
+                    tma_load_2d(Ks + AT_SLAB, &tmK, 64, row, &bars[0]);
+                    tma_load_2d(Vs, &tmV, 0, row, &bars[0]);
+                    tma_load_2d(Vs + AT_SLAB, &tmV, 64, row, &bars[0]);
+                }
+                tma_pending = true;
+            }
+            if (tid < AT_G) {
+                const float mc = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
+                const float mo = M[tid], mn = fmaxf(mo, mc);
+                AL[tid] = mo > -INFINITY ? expf(mo - mn) : 0.0f;     // rescale of what came before
+                M[tid] = mn;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int h4 = 0; h4 < 4; ++h4) {
+                const int h = 4 * hg + h4;
+                const float mh = M[h];
+                const __half p16 = __float2half_rn(kd < nk && mh > -INFINITY ? expf(sv[h4] - mh) : 0.0f);
+                float l = __half2float(p16);           // the sum of the probabilities the MMA multiplies
+#pragma unroll
+                for (int sh = 16; sh > 0; sh >>= 1) l += __shfl_xor_sync(0xffffffffu, l, sh);
+                if (lane == 0) red[32 + wq * 8 + h] = l;
+                const int kk = kd & 63;
+                *reinterpret_cast<__half *>(Pt + (kd >> 6) * AT_QSLAB + h * 128 + (((kk >> 3) ^ (h & 7)) << 4) +
+                                            (kk & 7) * 2) = p16;
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncthreads();
+            if (tid < AT_G)
+                L[tid] = fmaf(L[tid], AL[tid], (red[32 + tid] + red[40 + tid]) + (red[48 + tid] + red[56 + tid]));
+            if (tid == 0 && ok) {
+                tc_fence_after();
+                const uint32_t idesc = idesc_f16_f32acc(128, 16);
+                for (int j = 0; j < 8; ++j) {
+                    const int sl = j >> 2, ko = (j & 3) * 32;
+                    tc_mma_f16_ss(tm + 16, sdesc_sw128(smem_u32(Vt + sl * AT_SLAB) + ko),
+                                  sdesc_sw128(smem_u32(Pt + sl * AT_QSLAB) + ko), idesc, j > 0 ? 1u : 0u);
+                }
+                tc_commit(&bars[1]);
+            }
+            if (ok) ok = mbar_wait(&bars[1], ph1, 52);
+            ph1 ^= 1u;
+            tc_fence_after();
+            {
+                uint32_t r[16];
+                tmem_ld16(tm + (static_cast<uint32_t>(wq * 32) << 16) + 16, r);
+#pragma unroll
+                for (int h4 = 0; h4 < 4; ++h4)
+                    o[h4] = fmaf(o[h4], AL[4 * hg + h4], ok ? __uint_as_float(r[4 * hg + h4]) : 0.0f);
+            }
+            tc_fence_before();
+            ok = __syncthreads_and(ok) != 0;
+        }
+        // a copy still in flight after a timed-out wait lands before the CTA leaves
+        if (tma_pending && tid == 0) mbar_wait(&bars[0], ph0, 53);
+        __syncthreads();
+        if (splits == 1) {
+#pragma unroll
+            for (int h4 = 0; h4 < 4; ++h4) {
+                const int h = 4 * hg + h4;
+                a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h) * AT_D + kd] = ok ? o[h4] / L[h] : 0.0f;
+            }
+        } else {
+#pragma unroll
+            for (int h4 = 0; h4 < 4; ++h4) part[16 + (4 * hg + h4) * AT_D + kd] = ok ? o[h4] : 0.0f;
+            if (tid < AT_G) {
+                part[tid] = M[tid];
+                part[8 + tid] = L[tid];
+            }
+        }
+    }
+    if (splits > 1) {
+        // the last CTA of (t, g) merges the splits
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            unsigned int *cnt = a.counter + t * a.nkv + g;
+            const unsigned prev = atomicAdd(cnt, 1u);
+            *flag = prev == static_cast<unsigned>(splits - 1);
+            if (*flag) *cnt = 0u;
+        }
+        __syncthreads();
+        if (*flag) {
+            // merge: every split's (m, l) into shared memory with all loads in
+            // flight, the per-head weights exp(m_s - max) once, then each thread
+            // (= head dimension) its outputs with its split loads issued together
+            __threadfence();
+            const int ns = min(splits, nch);
+            const float *base = a.part + (static_cast<int64_t>(t) * a.nkv + g) * splits * AT_PART;
+            float *ml = reinterpret_cast<float *>(Vt);        // [split][16]: m[8], l[8]; then w [split][8]
+            float *wts = ml + 16 * ns;
+            for (int i = tid; i < 16 * ns; i += AT_THREADS) ml[i] = __ldcg(base + (i >> 4) * AT_PART + (i & 15));
+            __syncthreads();
+            if (tid < AT_G) {
+                float mx = -INFINITY;
+                for (int s2 = 0; s2 < ns; ++s2) mx = fmaxf(mx, ml[s2 * 16 + tid]);
+                float lsum = 0.0f;
+                for (int s2 = 0; s2 < ns; ++s2) {
+                    const float w = expf(ml[s2 * 16 + tid] - mx);
+                    wts[s2 * 8 + tid] = w;
+                    lsum = fmaf(w, ml[s2 * 16 + 8 + tid], lsum);
+                }
+                red[tid] = lsum;                           // (the softmax's scratch is free by now)
+            }
+            __syncthreads();
+            // thread = head dimension of one of the two head groups
+            const int d = tid & (AT_D - 1);
+            constexpr int MS = 16, MH = 4;                 // splits x heads whose loads go out together
+#pragma unroll 1
+            for (int h0 = (tid >> 7) * MH; h0 < AT_G; h0 += 2 * MH) {
+                float acc[MH];
+#pragma unroll
+                for (int hh = 0; hh < MH; ++hh) acc[hh] = 0.0f;
+                for (int s0 = 0; s0 < ns; s0 += MS) {
+                    float v[MH][MS];
+#pragma unroll
+                    for (int hh = 0; hh < MH; ++hh)
+#pragma unroll
+                        for (int u = 0; u < MS; ++u)
+                            v[hh][u] = s0 + u < ns ? __ldcg(base + (s0 + u) * AT_PART + 16 + (h0 + hh) * AT_D + d)
+                                                   : 0.0f;
+#pragma unroll
+                    for (int hh = 0; hh < MH; ++hh)
+#pragma unroll
+                        for (int u = 0; u < MS; ++u)
+                            if (s0 + u < ns) acc[hh] = fmaf(wts[(s0 + u) * 8 + h0 + hh], v[hh][u], acc[hh]);
+                }
+#pragma unroll
+                for (int hh = 0; hh < MH; ++hh)
+                    a.out[(static_cast<int64_t>(t) * a.nh + g * AT_G + h0 + hh) * AT_D + d] = acc[hh] / red[h0 + hh];
+            }
         }
     }
     fr_pdl_trigger();
+    tc_fence_before();
+    __syncthreads();
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tm, 32);

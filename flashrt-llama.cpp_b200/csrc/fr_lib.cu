@@ -2753,7 +2753,11 @@ int fr_attn_decode_f16(const float *q_r, const void *kcache, const void *vcache,
         return FR_EINVAL;
     const DevInfo &di = dev_info();
     if (di.cc_major != 10) return FR_ENODEVICE;
-    const int splits = ctx / AT_CH;
+    // a sequence's chunks split S ways so that the grid fills the SMs (two
+    // CTAs resident on each); at batch 64 one CTA walks all of its chunks
+    int splits = std::min(ctx / AT_CH, std::max(1, 2 * di.sms / (T * nkv)));
+    static const char *sv = getenv("FR_ATTN_SPLITS");
+    if (sv && *sv) splits = std::max(1, std::min(ctx / AT_CH, atoi(sv)));
     void *part = nullptr, *cnt = nullptr;
     int rc = workspace_get(WS_ATPART, static_cast<size_t>(T) * nkv * splits * AT_PART * sizeof(float), stream, &part);
     if (rc != FR_OK) return rc;

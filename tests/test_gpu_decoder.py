@@ -76,11 +76,19 @@ def test_rope_kv_append(fr, O, dev, pos):
     assert fr.device_status() == 0
 
 
-@pytest.mark.parametrize("n_keys", [1, 2, 127, 128, 129, 300, 1024, 2048])
-def test_attention_decode(fr, O, dev, n_keys):
+# (T, n_keys): the host splits a sequence's key chunks over 2 * SMs / (T * nkv)
+# CTAs (at most ctx / 128), so T = 2 has one chunk per CTA and a split merge,
+# T = 24 walks up to 6 chunks per CTA (online softmax) before the merge, and
+# T = 64 walks all of them in one CTA with no merge
+ATTN_CASES = [(2, n) for n in (1, 2, 127, 128, 129, 300, 1024, 2048)] + \
+             [(24, 1), (24, 385), (24, 2048), (64, 1), (64, 129), (64, 1100), (64, 2048)]
+
+
+@pytest.mark.parametrize("T,n_keys", ATTN_CASES)
+def test_attention_decode(fr, O, dev, T, n_keys):
     import torch
-    T, nh, nkv, d, ctx = 2, 32, 4, 128, 2048
-    rng = np.random.default_rng(n_keys)
+    nh, nkv, d, ctx = 32, 4, 128, 2048
+    rng = np.random.default_rng(n_keys + 7919 * T)
     q = (rng.standard_normal((T, nh, d)) / np.sqrt(d)).astype(np.float32)
     k = rng.standard_normal((T, nkv, ctx, d)).astype(np.float16)
     v = rng.standard_normal((T, nkv, ctx, d)).astype(np.float16)
