@@ -703,6 +703,8 @@ def run_profile_case(args):
         g.manual_seed(0x5EED7100 + T)
         dec.set_prompt(torch.randint(0, cfg.vocab, (T, 8), generator=g, device=dev, dtype=torch.int32))
         for i in range(8 + args.steps):
+            if i == 8 and args.pos > 8:
+                dec.pos.fill_(args.pos)     # decode at --pos (cache rows 8..pos-1 stay zero: finite keys)
             dec.step()
             torch.cuda.synchronize()
         print(f"profile case done: {8 + args.steps} decoder steps, T={T}, 4 layers, status {frb200.device_status()}")
@@ -777,6 +779,8 @@ def main():
     ap.add_argument("--matvec", type=int, default=None, help="force the matvec kernel (1 dp4a, 2 tc-f16, 3 tc-fp4)")
     ap.add_argument("--layout", choices=["ggml", "tiled", "mixed"], default="ggml",
                     help="weight layout of --profile-case (mixed: decoder dense ggml, experts tiled)")
+    ap.add_argument("--pos", type=int, default=0,
+                    help="decoder --profile-case: position of the decode steps after the 8-token prompt")
     ap.add_argument("--case", choices=["ffn", "moe", "gemm", "attn", "decoder"], default="ffn",
                     help="workload of --profile-case")
     args = ap.parse_args()

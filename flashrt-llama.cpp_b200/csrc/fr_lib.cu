@@ -1302,23 +1302,19 @@ static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, 
     const int TW = NP / 2;
     const int Kp = (K + 255) / 256 * 256;
     const int n_kt = Kp / 256;
-    int ksplit = std::max(1, std::min(n_kt, (128 * G) / std::max(1, N)));
-    // each split's partial is 2 x TW x 128 floats per row tile (twice for
-    // the SwiGLU pair), summed by the tile's last CTA: when a CTA's share of
-    // the weights is under twice that, the hand-off costs more than the SMs
-    // the split adds (T=64: 5120x2048 52.6 -> 20.5 us, 2048x4096 51.8 ->
-    // 32.7 us unsplit; 4096x14336 keeps its split)
-    {
-        const double w_per_cta = static_cast<double>(N) * K * 36.0 / 64.0 / G;
-        const double part_bytes = 2.0 * TW * 128 * 4 * (dual ? 2 : 1);
-        if (w_per_cta < 2.0 * part_bytes) ksplit = 1;
-    }
+    // K split so that tiles of (up to) 128 rows fill the SMs: every CTA
+    // re-reads the activation of its K range (2 x T f16 columns, 4 x the
+    // bytes of the NVFP4 weights it decodes at T = 64), so fewer, fuller row
+    // tiles keep that L2 traffic down; the split partials are added by the
+    // last CTA of each (row tile, quadrant, column range)
+    int ksplit = std::max(1, std::min(n_kt, G / ((N + 127) / 128)));
     // tuning cap (FR_TC_KSPLIT_MAX)
     static const char *kv = getenv("FR_TC_KSPLIT_MAX");
     if (kv && *kv) ksplit = std::max(1, std::min(ksplit, atoi(kv)));
     const int kt_per = (n_kt + ksplit - 1) / ksplit;
     ksplit = (n_kt + kt_per - 1) / kt_per;
-    const int R = std::min(128, std::max(1, static_cast<int>((static_cast<int64_t>(N) * ksplit + G - 1) / G)));
+    // rows per tile: the row tiles of one K split take G / ksplit CTAs
+    const int R = std::min(128, std::max(1, (N + G / ksplit - 1) / (G / ksplit)));
     const int n_rt = (N + R - 1) / R;
 
     void *actp = nullptr;
@@ -1327,7 +1323,7 @@ static int tc_matvec(const uint8_t *w0, const uint8_t *w1, int64_t w_ld, int N, 
     // counters live at a fixed place (the first TG_MAX_COUNTERS words, zero
     // after allocation and reset by every last split), partials after them
     constexpr size_t TG_MAX_COUNTERS = 1 << 16;
-    if (static_cast<size_t>(n_rt) * 4 > TG_MAX_COUNTERS) return FR_EINVAL;
+    if (ksplit > 1 && static_cast<size_t>(n_rt) * 16 > TG_MAX_COUNTERS) return FR_EINVAL;
     const size_t part_floats = static_cast<size_t>(n_rt) * ksplit * 2 * TW * 128;
     const size_t part_off = TG_MAX_COUNTERS * 4;
     void *wsp = nullptr;

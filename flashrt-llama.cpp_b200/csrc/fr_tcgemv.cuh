@@ -177,7 +177,7 @@ struct TgArgs {
     float *y;                    // [.., ldy]
     int64_t ldy;
     float *part;                 // split-K partials [n_rt][ksplit][2][NP/2][128]
-    unsigned int *counter;       // [n_rt][4 quadrants], zero on entry, reset by the last split
+    unsigned int *counter;       // [n_rt][4 quadrants][4 column ranges], zero on entry, reset by the last split
     int n_stages;                // shared-memory ring depth
 };
 
@@ -327,11 +327,17 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tcgemv(const __grid_constant_
             __syncwarp();
             if (lane == 0) mbar_arrive(&afull[slot]);
         }
-        // ---------------- epilogue: warps of phase 0, one per quadrant.  Each
-        // warp finishes its own 32 rows; with split-K it publishes its partial
-        // and the last of the K splits (per row tile and quadrant) adds them in
-        // split order -- no CTA-wide barrier, so a timed-out warp cannot hang it.
-        if (ph == 0 && ok && mbar_wait(accfull, 0, 26)) {
+        // ---------------- epilogue: EW warps per quadrant (EW = NP / 16, at
+        // most 4), warp ph for the columns [ph CW, ph CW + CW) (tokens
+        // [ph CW / 2, ...)) of its quadrant's 32 rows.  With split-K it
+        // publishes its partial and the last of the K splits for that
+        // (row tile, quadrant, column range) adds them in split order, its
+        // partial loads batched so their latencies overlap -- no CTA-wide
+        // barrier, so a timed-out warp cannot hang it.
+        constexpr int EW = NP / 16 < 4 ? NP / 16 : 4;
+        constexpr int CW = NP / EW;                          // columns per epilogue warp
+        constexpr int TWW = CW / 2;                          // tokens per epilogue warp
+        if (ph < EW && ok && mbar_wait(accfull, 0, 26)) {
             tc_fence_after();
             fr_pdl_wait();
             const bool split = g.ksplit > 1;
@@ -339,6 +345,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tcgemv(const __grid_constant_
             const bool live = row < g.R && n < g.N;
             const float sc0 = g.s0 ? *g.s0 : 1.0f;
             const float sc1 = (DUAL && g.s1) ? *g.s1 : 1.0f;
+            const int tw0 = ph * TWW;
             float *pp = g.part + ((static_cast<int64_t>(rt) * g.ksplit + ks) * 2) * NT * 128;
             auto finish = [&](int t, float a0, float a1) {
                 if (!live || t >= g.T) return;
@@ -357,14 +364,14 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tcgemv(const __grid_constant_
                 }
                 g.y[tt * g.ldy + n] = v;
             };
-#pragma unroll 1
-            for (int c = 0; c < NP; c += 16) {
+#pragma unroll
+            for (int c = 0; c < CW; c += 16) {
                 uint32_t r0v[16], r1v[16];
-                tmem_ld16(tD + lane_off + c, r0v);
-                if (DUAL) tmem_ld16(tD + NP + lane_off + c, r1v);
+                tmem_ld16(tD + lane_off + ph * CW + c, r0v);
+                if (DUAL) tmem_ld16(tD + NP + lane_off + ph * CW + c, r1v);
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
-                    const int t = c / 2 + u;
+                    const int t = tw0 + c / 2 + u;
                     const float a0 = __uint_as_float(r0v[2 * u]) + __uint_as_float(r0v[2 * u + 1]);
                     const float a1 = DUAL ? __uint_as_float(r1v[2 * u]) + __uint_as_float(r1v[2 * u + 1]) : 0.0f;
                     if (split) {
@@ -378,22 +385,56 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tcgemv(const __grid_constant_
             if (split) {
                 __threadfence();
                 __syncwarp();
+                unsigned int *cnt = &g.counter[(rt * 4 + q) * 4 + ph];
                 unsigned prev = 0;
-                if (lane == 0) prev = atomicAdd(&g.counter[rt * 4 + q], 1u);
+                if (lane == 0) prev = atomicAdd(cnt, 1u);
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 if (prev == static_cast<unsigned>(g.ksplit - 1)) {
                     __threadfence();
-                    const float *pb = g.part + (static_cast<int64_t>(rt) * g.ksplit * 2) * NT * 128;
-#pragma unroll 1
-                    for (int t = 0; t < NT && t < g.T; ++t) {
-                        float a0 = 0.0f, a1 = 0.0f;
-                        for (int k2 = 0; k2 < g.ksplit; ++k2) {
-                            a0 += __ldcg(pb + (k2 * 2) * NT * 128 + t * 128 + row);
-                            if (DUAL) a1 += __ldcg(pb + (k2 * 2 + 1) * NT * 128 + t * 128 + row);
-                        }
-                        finish(t, a0, a1);
+                    const float *pb = g.part + (static_cast<int64_t>(rt) * g.ksplit * 2) * NT * 128 + tw0 * 128 + row;
+                    constexpr int KU = DUAL ? 2 : 4;         // splits whose loads go out together
+                    float acc0[TWW], acc1[TWW];
+#pragma unroll
+                    for (int u = 0; u < TWW; ++u) {
+                        acc0[u] = 0.0f;
+                        acc1[u] = 0.0f;
                     }
-                    if (lane == 0) g.counter[rt * 4 + q] = 0;
+                    int k2 = 0;
+#pragma unroll 1
+                    for (; k2 + KU <= g.ksplit; k2 += KU) {
+                        float v0[KU][TWW], v1[KU][TWW];
+#pragma unroll
+                        for (int j = 0; j < KU; ++j)
+#pragma unroll
+                            for (int u = 0; u < TWW; ++u) {
+                                v0[j][u] = __ldcg(pb + ((k2 + j) * 2) * NT * 128 + u * 128);
+                                if (DUAL) v1[j][u] = __ldcg(pb + ((k2 + j) * 2 + 1) * NT * 128 + u * 128);
+                            }
+#pragma unroll
+                        for (int j = 0; j < KU; ++j)
+#pragma unroll
+                            for (int u = 0; u < TWW; ++u) {
+                                acc0[u] += v0[j][u];
+                                if (DUAL) acc1[u] += v1[j][u];
+                            }
+                    }
+#pragma unroll 1
+                    for (; k2 < g.ksplit; ++k2) {
+                        float v0[TWW], v1[TWW];
+#pragma unroll
+                        for (int u = 0; u < TWW; ++u) {
+                            v0[u] = __ldcg(pb + (k2 * 2) * NT * 128 + u * 128);
+                            if (DUAL) v1[u] = __ldcg(pb + (k2 * 2 + 1) * NT * 128 + u * 128);
+                        }
+#pragma unroll
+                        for (int u = 0; u < TWW; ++u) {
+                            acc0[u] += v0[u];
+                            if (DUAL) acc1[u] += v1[u];
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < TWW; ++u) finish(tw0 + u, acc0[u], acc1[u]);
+                    if (lane == 0) *cnt = 0;
                 }
             }
         }
