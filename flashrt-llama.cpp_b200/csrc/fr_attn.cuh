@@ -258,12 +258,13 @@ __global__ void __launch_bounds__(256) k_copy16(const uint4 *__restrict__ src, u
 // matmuls of a chunk on the tensor cores (tcgen05.mma kind::f16, f32 in TMEM):
 //   S^T [128 keys x 16] = K_chunk [128 x 128] . Q^T   (Q: 8 heads, 8 zero rows)
 //   softmax over the keys (thread = key = TMEM lane), P^T in f16
-//   O^T [128 dims x 16] = V_chunk^T [128 x 128] . P^T (V transposed in shared memory)
+//   O^T [128 dims x 16] = V_chunk^T [128 x 128] . P^T (V read MN-major as the TMA wrote it)
 // so K and V are read once per KV head for all 8 heads.  Across its chunks a
 // CTA keeps the running max m, sum l and output o per head (online softmax,
 // o in registers: thread = head dimension x 4 heads); the next chunk's K / V
 // TMA is issued as soon as the current chunk's K and V have been consumed, so
-// it overlaps the softmax and the P.V product.  With S = 1 the CTA writes
+// it overlaps the softmax and the P.V product (V has two buffers, so the
+// next chunk's V lands while this chunk's P.V product still reads its own).  With S = 1 the CTA writes
 // o / l directly; otherwise each CTA writes (m, l, o) and the last CTA of
 // (t, g) to finish merges the splits in split order (deterministic).  The
 // host picks S so that the grid fills the SMs (S = ctx / AT_CH at T = 1, one
@@ -281,7 +282,7 @@ struct AtArgs {
 constexpr int AT_SLAB = 128 * 128;                 // 128 rows x 128 B
 constexpr int AT_QSLAB = 16 * 128;                 // 16 rows x 128 B
 constexpr int AT_PART = 16 + AT_G * AT_D;
-constexpr size_t AT_SMEM = 1024 + 6 * AT_SLAB + 4 * AT_QSLAB + 512 + 64;
+constexpr size_t AT_SMEM = 1024 + 6 * AT_SLAB + 4 * AT_QSLAB + 512 + 64;   // K, 2 x V, Q, P, scratch
 
 __device__ __forceinline__ void tc_mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                               uint32_t accumulate) {
@@ -303,9 +304,8 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *Ks = smem;                        // 2 slabs: keys x dims [0, 64) and [64, 128)
-    uint8_t *Vs = Ks + 2 * AT_SLAB;            // same for V
-    uint8_t *Vt = Vs + 2 * AT_SLAB;            // 2 slabs: dims x keys [0, 64) and [64, 128)
-    uint8_t *Qs = Vt + 2 * AT_SLAB;            // 2 slabs: 16 heads x dims
+    uint8_t *Vb = Ks + 2 * AT_SLAB;            // 2 buffers of V, each as K
+    uint8_t *Qs = Vb + 4 * AT_SLAB;            // 2 slabs: 16 heads x dims
     uint8_t *Pt = Qs + 2 * AT_QSLAB;           // 2 slabs: 16 heads x keys
     float *red = reinterpret_cast<float *>(Pt + 2 * AT_QSLAB);     // [4][8] maxima, [4][8] sums, M, L, alpha
     uint64_t *bars = reinterpret_cast<uint64_t *>(red + 96);       // tma, mma
@@ -345,8 +345,8 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
             mbar_expect_tx(&bars[0], 4 * AT_SLAB);
             tma_load_2d(Ks, &tmK, 0, row_base + s * AT_CH, &bars[0]);
             tma_load_2d(Ks + AT_SLAB, &tmK, 64, row_base + s * AT_CH, &bars[0]);
-            tma_load_2d(Vs, &tmV, 0, row_base + s * AT_CH, &bars[0]);
-            tma_load_2d(Vs + AT_SLAB, &tmV, 64, row_base + s * AT_CH, &bars[0]);
+            tma_load_2d(Vb, &tmV, 0, row_base + s * AT_CH, &bars[0]);
+            tma_load_2d(Vb + AT_SLAB, &tmV, 64, row_base + s * AT_CH, &bars[0]);
         }
         tma_pending = true;
         // Q tile (f16, 128-byte swizzled K-major): 16 rows x 16 chunks of 8 dims; rows 8..15 zero
@@ -376,9 +376,11 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
         }
         fence_proxy_async();
         __syncthreads();
+        int it = 0;
 #pragma unroll 1
-        for (int c = s; c < nch && ok; c += splits) {
+        for (int c = s; c < nch && ok; c += splits, ++it) {
             const int nk = min(AT_CH, n - c * AT_CH);
+            uint8_t *Vs = Vb + (it & 1) * 2 * AT_SLAB;
             ok = mbar_wait(&bars[0], ph0, 50);
             if (ok) {
                 ph0 ^= 1u;
@@ -395,36 +397,9 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
                 tc_commit(&bars[1]);
             }
             if (ok) {
-                // V [keys x dims] -> V^T [dims x keys], 8x8 blocks of halves
-                for (int blk = tid; blk < 256; blk += AT_THREADS) {
-                    const int kg = blk >> 4, dg = blk & 15;
-                    uint32_t in[8][4];
-#pragma unroll
-                    for (int r = 0; r < 8; ++r) {
-                        const int key = 8 * kg + r;
-                        const uint4 w = *reinterpret_cast<const uint4 *>(Vs + (dg >> 3) * AT_SLAB + key * 128 +
-                                                                          (((dg & 7) ^ (key & 7)) << 4));
-                        in[r][0] = w.x; in[r][1] = w.y; in[r][2] = w.z; in[r][3] = w.w;
-                    }
-#pragma unroll
-                    for (int d = 0; d < 8; ++d) {
-                        uint32_t ov[4];
-#pragma unroll
-                        for (int r2 = 0; r2 < 4; ++r2) {
-                            const uint32_t lo = (in[2 * r2][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
-                            const uint32_t hi = (in[2 * r2 + 1][d >> 1] >> ((d & 1) * 16)) & 0xFFFFu;
-                            ov[r2] = lo | (hi << 16);
-                        }
-                        const int dim = 8 * dg + d;
-                        *reinterpret_cast<uint4 *>(Vt + (kg >> 3) * AT_SLAB + dim * 128 +
-                                                   (((kg & 7) ^ (dim & 7)) << 4)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
-                    }
-                }
                 ok = mbar_wait(&bars[1], ph1, 51);
             }
             ph1 ^= 1u;
-            // V^T stores before the P.V product, V reads before the next chunk's TMA
-            fence_proxy_async();
             tc_fence_after();
             float sv[4];
             {
@@ -443,15 +418,17 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
             }
             tc_fence_before();
             ok = __syncthreads_and(ok) != 0;
-            // K and V of this chunk are consumed: the next chunk's copies go out now
+            // K of this chunk is consumed and the other V buffer's last P.V
+            // product is done: the next chunk's copies go out now
             if (ok && c + splits < nch) {
                 if (tid == 0) {
                     const int row = row_base + (c + splits) * AT_CH;
+                    uint8_t *Vn = Vb + ((it + 1) & 1) * 2 * AT_SLAB;
                     mbar_expect_tx(&bars[0], 4 * AT_SLAB);
                     tma_load_2d(Ks, &tmK, 0, row, &bars[0]);
                     tma_load_2d(Ks + AT_SLAB, &tmK, 64, row, &bars[0]);
-                    tma_load_2d(Vs, &tmV, 0, row, &bars[0]);
-                    tma_load_2d(Vs + AT_SLAB, &tmV, 64, row, &bars[0]);
+                    tma_load_2d(Vn, &tmV, 0, row, &bars[0]);
+                    tma_load_2d(Vn + AT_SLAB, &tmV, 64, row, &bars[0]);
                 }
                 tma_pending = true;
             }
@@ -482,11 +459,12 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
                 L[tid] = fmaf(L[tid], AL[tid], (red[32 + tid] + red[40 + tid]) + (red[48 + tid] + red[56 + tid]));
             if (tid == 0 && ok) {
                 tc_fence_after();
-                const uint32_t idesc = idesc_f16_f32acc(128, 16);
+                // keys [16 j, 16 j + 16) are rows 16 j.. of both V slabs; A (V^T) MN-major
+                const uint32_t idesc_pv = idesc_f16_f32acc(128, 16) | (1u << 15);
                 for (int j = 0; j < 8; ++j) {
                     const int sl = j >> 2, ko = (j & 3) * 32;
-                    tc_mma_f16_ss(tm + 16, sdesc_sw128(smem_u32(Vt + sl * AT_SLAB) + ko),
-                                  sdesc_sw128(smem_u32(Pt + sl * AT_QSLAB) + ko), idesc, j > 0 ? 1u : 0u);
+                    tc_mma_f16_ss(tm + 16, sdesc_sw128_mn(smem_u32(Vs) + j * 16 * 128, AT_SLAB, 1024),
+                                  sdesc_sw128(smem_u32(Pt + sl * AT_QSLAB) + ko), idesc_pv, j > 0 ? 1u : 0u);
                 }
                 tc_commit(&bars[1]);
             }
@@ -539,7 +517,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(const __grid_constan
             __threadfence();
             const int ns = min(splits, nch);
             const float *base = a.part + (static_cast<int64_t>(t) * a.nkv + g) * splits * AT_PART;
-            float *ml = reinterpret_cast<float *>(Vt);        // [split][16]: m[8], l[8]; then w [split][8]
+            float *ml = reinterpret_cast<float *>(Ks);        // [split][16]: m[8], l[8]; then w [split][8]
             float *wts = ml + 16 * ns;
             for (int i = tid; i < 16 * ns; i += AT_THREADS) ml[i] = __ldcg(base + (i >> 4) * AT_PART + (i & 15));
             __syncthreads();

@@ -24,6 +24,14 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
            (2ull << 61);
 }
 
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    // MN-major, 128-byte swizzle: rows of 64 16-bit MN values, one row per K
+    // index; LBO between 64-value MN blocks, SBO between 8-row K groups
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+           (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
 __device__ __forceinline__ uint64_t sdesc_plain(uint32_t saddr, uint32_t sbo_bytes) {
     // no swizzle, K-major core matrices of 8 rows x 16 B, SBO between them
     return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) |
