@@ -342,29 +342,34 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
         int64_t *orow = orow_w + q * 16;
         float *part_cta = g.part + static_cast<int64_t>(blockIdx.x) * 2 * 2 * TMAX * 128;
         int seg = 0;
+        int cur_w = -1, e = 0, sb = 0, nt = 0;
+        float sc0 = 1.0f, sc1 = 1.0f;
         for (int s0u = u_lo; s0u < u_hi; ++seg) {
             const int rbg = s0u / nsr;
             const int s1u = min(u_hi, (rbg + 1) * nsr);
             const int w = rbg / g.n_rb, rb = rbg % g.n_rb;
-            int e, sb, nt;
-            win_at(w, e, sb, nt);
-            // this warp's copy of the window's factors and output rows
-            __syncwarp();
+            if (w != cur_w) {
+                // this warp's copy of the window's factors, output rows and
+                // scales, loaded once per window (its row blocks follow)
+                win_at(w, e, sb, nt);
+                __syncwarp();
 #pragma unroll
-            for (int c = lane; c < TMAX * FM_GSTRIDE; c += 32) {
-                const int t = c / FM_GSTRIDE;
-                float v = 0.0f;
-                if (t < nt) v = g.gtab[static_cast<int64_t>(row_at(w, sb, t)) * FM_GSTRIDE + (c % FM_GSTRIDE)];
-                gt[c] = v;
+                for (int c = lane; c < TMAX * FM_GSTRIDE; c += 32) {
+                    const int t = c / FM_GSTRIDE;
+                    float v = 0.0f;
+                    if (t < nt) v = g.gtab[static_cast<int64_t>(row_at(w, sb, t)) * FM_GSTRIDE + (c % FM_GSTRIDE)];
+                    gt[c] = v;
+                }
+                if (lane < TMAX) {
+                    const int slot = lane < nt ? g.slots[sb + lane] : 0;
+                    orow[lane] = static_cast<int64_t>(slot / g.n_used) * g.ld_tok +
+                                 static_cast<int64_t>(slot % g.n_used) * g.ld_slot;
+                }
+                __syncwarp();
+                sc0 = g.s0 ? g.s0[e] : 1.0f;
+                sc1 = (DUAL && g.s1) ? g.s1[e] : 1.0f;
+                cur_w = w;
             }
-            if (lane < TMAX) {
-                const int slot = lane < nt ? g.slots[sb + lane] : 0;
-                orow[lane] = static_cast<int64_t>(slot / g.n_used) * g.ld_tok +
-                             static_cast<int64_t>(slot % g.n_used) * g.ld_slot;
-            }
-            __syncwarp();
-            const float sc0 = g.s0 ? g.s0[e] : 1.0f;
-            const float sc1 = (DUAL && g.s1) ? g.s1[e] : 1.0f;
             auto finish = [&](int t, float a0, float a1) {
                 const int n = rb * 128 + erow;
                 if (n >= g.N || t >= nt) return;
