@@ -243,11 +243,13 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
         // ---------------- weight producer
         if (lane == 0) {
             int cur_w = -1, e = 0, sb = 0, nt = 0;
+            // unit u = (window u / wpu, row block (u % wpu) / nsr, K stage
+            // u % nsr), ring slot s and its use count, all as counters: a
+            // runtime division per stage is a dependent chain this lone
+            // thread pays
+            int w = u_lo / wpu, rb = (u_lo % wpu) / nsr, kq = u_lo % nsr, s = 0, use = 0;
             for (int i = 0; i < n_st; ++i) {
-                const int s = i % NW;
-                if (i >= NW && !mbar_wait(&empty[s], ((i / NW) - 1) & 1, 60)) break;
-                const int u = u_lo + i;
-                const int w = u / wpu, rb = (u % wpu) / nsr, kq = u % nsr;
+                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, 60)) break;
                 if (w != cur_w) {
                     win_at(w, e, sb, nt);
                     cur_w = w;
@@ -258,6 +260,17 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
                 mbar_expect_tx(&full[s], S::WST);
                 bulk_g2s(st, g.w0 + off, FT_TILE, &full[s]);
                 if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &full[s]);
+                if (++s == NW) {
+                    s = 0;
+                    ++use;
+                }
+                if (++kq == nsr) {
+                    kq = 0;
+                    if (++rb == g.n_rb) {
+                        rb = 0;
+                        ++w;
+                    }
+                }
             }
         }
     } else if (warp == 7) {
@@ -265,10 +278,8 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
         // of the stage; the stage records the MMA width its tokens need
         int cur_w = -1, nt = 0, ncol = 16;
         const uint8_t *src = g.img;
+        int w = u_lo / wpu, rb = (u_lo % wpu) / nsr, kq = u_lo % nsr, s = 0, use = 0;
         for (int i = 0; i < n_st; ++i) {
-            const int s = i % NW;
-            const int u = u_lo + i;
-            const int w = u / wpu, kq = u % nsr;
             if (w != cur_w) {
                 int e, sb;
                 win_at(w, e, sb, nt);
@@ -278,7 +289,7 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
                 cur_w = w;
             }
             bool ok = true;
-            if (lane == 0 && i >= NW) ok = mbar_wait(&empty[s], ((i / NW) - 1) & 1, 61);
+            if (lane == 0 && use > 0) ok = mbar_wait(&empty[s], (use - 1) & 1, 61);
             if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
             uint8_t *st = b_ring + static_cast<size_t>(s) * S::BST;
             if (lane == 0) {
@@ -287,6 +298,17 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
             }
             __syncwarp();
             if (lane < nt) bulk_g2s(st + lane * 1024, src + kq * 1024, 1024, &full[s]);
+            if (++s == NW) {
+                s = 0;
+                ++use;
+            }
+            if (++kq == nsr) {
+                kq = 0;
+                if (++rb == g.n_rb) {
+                    rb = 0;
+                    ++w;
+                }
+            }
         }
     } else if (warp == 1 || warp == 2 || warp >= 8) {
         // ---------------- MMA issuers: thread (group p, matrix m) issues the
@@ -298,10 +320,12 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
             tc_cp_sf(t_sfb, sdesc_plain(smem_u32(sfb_const), 128));
             int seg = 0;
             bool started = false;
+            // K stage within the row block, ring slot and its use count as
+            // counters (no runtime division on this thread's critical path)
+            int kq = u_lo % nsr, sw = 0, use = 0;
             for (int i = 0; i < n_st; ++i) {
-                const int u = u_lo + i;
-                const bool first = i == 0 || u % nsr == 0;
-                const bool last = i == n_st - 1 || (u + 1) % nsr == 0;
+                const bool first = i == 0 || kq == 0;
+                const bool last = i == n_st - 1 || kq == nsr - 1;
                 const int d = seg % D;
                 if (first) {
                     started = false;
@@ -309,8 +333,7 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
                     if (seg >= D && !mbar_wait(&accempty[d], ((seg / D) - 1) & 1, 62)) break;
                 }
                 if (i % P == p) {
-                    const int sw = i % NW;
-                    if (!mbar_wait(&full[sw], (i / NW) & 1, 63)) break;
+                    if (!mbar_wait(&full[sw], use & 1, 63)) break;
                     tc_fence_after();
                     const uint32_t idesc = idesc_nvf4(128, stage_n[sw]);
                     const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + m * FT_TILE;
@@ -330,6 +353,11 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
                 if (last) {
                     tc_commit(&accfull[d]);
                     ++seg;
+                }
+                if (++kq == nsr) kq = 0;
+                if (++sw == NW) {
+                    sw = 0;
+                    ++use;
                 }
             }
         }

@@ -249,29 +249,41 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
     if (warp == 0) {
         // ---------------- weight producer: contiguous tiles, no PDL wait
         if (lane == 0) {
+            // ring slot s and its use count kept as counters: a runtime
+            // division per stage is a dependent chain this lone thread pays
+            int s = 0, use = 0;
             for (int i = 0; i < n_st; ++i) {
-                const int s = i % NW;
-                if (i >= NW && !mbar_wait(&empty[s], ((i / NW) - 1) & 1, 50)) break;
+                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, 50)) break;
                 uint8_t *st = w_ring + static_cast<size_t>(s) * S::WST;
-                const int u = u_lo + i;
-                // first tile of the stage: row block u / nsr, K stage (u % nsr) * NT
-                const int64_t off = (static_cast<int64_t>(u / nsr) * g.n_kq + (u % nsr) * NT) * FT_TILE;
+                // unit u = row block u / nsr, K stage (u % nsr) * NT: tiles
+                // are stored row block by row block, n_kq = nsr * NT per block,
+                // so its first tile is tile u * NT
+                const int64_t off = static_cast<int64_t>(u_lo + i) * NT * FT_TILE;
                 mbar_expect_tx(&full[s], S::WST);
                 bulk_g2s(st, g.w0 + off, NT * FT_TILE, &full[s]);
                 if (DUAL) bulk_g2s(st + FT_TILE, g.w1 + off, FT_TILE, &full[s]);
+                if (++s == NW) {
+                    s = 0;
+                    ++use;
+                }
             }
         }
     } else if (warp == 7) {
         // ---------------- activation producer (after the PDL wait)
         if (lane == 0) {
             fr_pdl_wait();
+            int s = 0, use = 0, kq = u_lo % nsr;
             for (int i = 0; i < n_st; ++i) {
-                const int s = i % NW;
-                if (i >= NW && !mbar_wait(&empty[s], ((i / NW) - 1) & 1, 51)) break;
-                const int kq0 = ((u_lo + i) % nsr) * NT;
+                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, 51)) break;
+                const int kq0 = kq * NT;
                 mbar_expect_tx(&full[s], S::BST);
                 bulk_g2s(b_ring + static_cast<size_t>(s) * S::BST, g.bimg + static_cast<int64_t>(kq0) * S::B_BYTES,
                          S::BST, &full[s]);
+                if (++s == NW) {
+                    s = 0;
+                    ++use;
+                }
+                if (++kq == nsr) kq = 0;
             }
         }
     } else if (warp == 1 || warp == 2 || warp >= 8) {
@@ -288,18 +300,19 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
             tc_cp_sf(t_sfb, sdesc_plain(smem_u32(sfb_const), 128));
             int seg = 0;
             bool started = false;
+            // K stage within the row block, ring slot and its use count as
+            // counters (no runtime division on this thread's critical path)
+            int kq = u_lo % nsr, sw = 0, use = 0;
             for (int i = 0; i < n_st; ++i) {
-                const int u = u_lo + i;
-                const bool first = i == 0 || u % nsr == 0;       // first stage of a row-block segment
-                const bool last = i == n_st - 1 || (u + 1) % nsr == 0;
+                const bool first = i == 0 || kq == 0;             // first stage of a row-block segment
+                const bool last = i == n_st - 1 || kq == nsr - 1;
                 if (first) {
                     started = false;
                     // every issuer waits for each drain, in order
                     if (seg > 0 && !mbar_wait(accempty, (seg - 1) & 1, 52)) break;
                 }
                 if (i % P == p) {
-                    const int sw = i % NW;
-                    if (!mbar_wait(&full[sw], (i / NW) & 1, 53)) break;
+                    if (!mbar_wait(&full[sw], use & 1, 53)) break;
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(w_ring + static_cast<size_t>(sw) * S::WST) + k * FT_TILE;
                     const uint32_t b_addr = smem_u32(b_ring + static_cast<size_t>(sw) * S::BST) +
@@ -318,6 +331,11 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
                 if (last) {
                     tc_commit(accfull);
                     ++seg;
+                }
+                if (++kq == nsr) kq = 0;
+                if (++sw == NW) {
+                    sw = 0;
+                    ++use;
                 }
             }
         }

@@ -244,11 +244,12 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tcgemv(const __grid_constant_
         // ---------------- producer: weights need no PDL wait, the activation does
         if (lane == 0) {
             bool waited_pdl = false;
-            for (int i = 0; i < n_st; ++i) {
-                const int s = i % S;
-                if (i >= S) {
-                    if (!mbar_wait(&wfree[s], ((i / S) - 1) & 1, 20)) break;
-                    if (!mbar_wait(&bfree[s], ((i / S) - 1) & 1, 21)) break;
+            // ring slot s and its use count as counters (no runtime division
+            // on this thread's critical path)
+            for (int i = 0, s = 0, use = 0; i < n_st; ++i, use += (++s == S), s = (s == S) ? 0 : s) {
+                if (use > 0) {
+                    if (!mbar_wait(&wfree[s], (use - 1) & 1, 20)) break;
+                    if (!mbar_wait(&bfree[s], (use - 1) & 1, 21)) break;
                 }
                 uint8_t *st = smem + s * STAGE;
                 const int kt = kt0 + i;
@@ -267,9 +268,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tcgemv(const __grid_constant_
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(128, NP);
             bool ok = true;
-            for (int i = 0; i < n_st && ok; ++i) {
-                const int s = i % S;
-                if (!mbar_wait(&full[s], (i / S) & 1, 22)) { ok = false; break; }
+            for (int i = 0, s = 0, use = 0; i < n_st && ok; ++i, use += (++s == S), s = (s == S) ? 0 : s) {
+                if (!mbar_wait(&full[s], use & 1, 22)) { ok = false; break; }
                 const int kb0 = (kt0 + i) * 4;
                 const uint32_t b_addr = smem_u32(smem + s * STAGE + NM * TG_WBYTES);
                 for (int blk = 0; blk < 4; ++blk) {
@@ -299,9 +299,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tcgemv(const __grid_constant_
         const int row = 32 * q + lane;                       // tile row = TMEM lane
         const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
         bool ok = true;
-        for (int i = 0; i < n_st; ++i) {
-            const int s = i % S;
-            if (!mbar_wait(&full[s], (i / S) & 1, 24)) { ok = false; break; }
+        for (int i = 0, s = 0, su = 0; i < n_st; ++i, su += (++s == S), s = (s == S) ? 0 : s) {
+            if (!mbar_wait(&full[s], su & 1, 24)) { ok = false; break; }
             const bool has_blk = (kt0 + i) * 4 + ph < nkb_total;
             uint32_t w0[9], w1[9];
             if (has_blk) {
