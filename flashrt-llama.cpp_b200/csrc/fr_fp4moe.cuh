@@ -372,10 +372,11 @@ __global__ void __launch_bounds__(FeShape<NCOL, EPI>::THREADS, 1) k_fp4e(const F
         int seg = 0;
         int cur_w = -1, e = 0, sb = 0, nt = 0;
         float sc0 = 1.0f, sc1 = 1.0f;
-        for (int s0u = u_lo; s0u < u_hi; ++seg) {
-            const int rbg = s0u / nsr;
+        // row-block group rbg (window w, row block rb) of each segment kept as
+        // counters: one segment per row block, in order
+        int rbg = u_lo / nsr, w = rbg / g.n_rb, rb = rbg % g.n_rb;
+        for (int s0u = u_lo; s0u < u_hi; ++seg, ++rbg, (++rb == g.n_rb) ? (rb = 0, ++w) : 0) {
             const int s1u = min(u_hi, (rbg + 1) * nsr);
-            const int w = rbg / g.n_rb, rb = rbg % g.n_rb;
             if (w != cur_w) {
                 // this warp's copy of the window's factors, output rows and
                 // scales, loaded once per window (its row blocks follow)

@@ -390,8 +390,8 @@ __global__ void __launch_bounds__(FtShape<NCOL, EPI, NT>::THREADS, 1) k_fp4t(con
         // block adds the partials in CTA order (per quadrant, so a warp that
         // timed out cannot hold the others)
         int seg = 0;
-        for (int s0u = u_lo; s0u < u_hi; ++seg) {
-            const int rb = s0u / nsr;
+        int rb = u_lo / nsr;                               // one segment per row block, in order
+        for (int s0u = u_lo; s0u < u_hi; ++seg, ++rb) {
             const int s1u = min(u_hi, (rb + 1) * nsr);
             if (!mbar_wait(accfull, seg & 1, 55)) break;
             tc_fence_after();

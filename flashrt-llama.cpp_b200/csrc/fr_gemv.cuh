@@ -336,9 +336,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, (TT == 1 && R2 == 1) ? 2 : 1) k
         // ---------------- producer: stream the CTA's weight rows, before the
         // PDL wait (weights do not depend on the previous kernel)
         const int64_t dual_off = static_cast<int64_t>(SR) * p.w_ld;
-        for (int i = 0; i < n_st; ++i) {
-            const int s = i % NS;
-            if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1, 1)) break;
+        // ring slot s and its use count as counters (no runtime division per stage)
+        for (int i = 0, s = 0, use = 0; i < n_st; ++i, use += (++s == NS), s = (s == NS) ? 0 : s) {
+            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, 1)) break;
             const int rows = min(SR, n_rows - i * SR);
             const int64_t off = static_cast<int64_t>(r_begin + i * SR) * p.w_ld;
             uint8_t *dst = ring + static_cast<size_t>(s) * p.slot_bytes;
@@ -374,9 +374,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (TT == 1 && R2 == 1) ? 2 : 1) k
     const int g = lane / LG, j = lane % LG;
     const int rg0 = (warp * GPW + g) * R2;              // first stage row of this lane group
 
-    for (int i = 0; i < n_st; ++i) {
-        const int s = i % NS;
-        if (!mbar_wait(&full[s], (i / NS) & 1, 2)) break;
+    for (int i = 0, s = 0, use = 0; i < n_st; ++i, use += (++s == NS), s = (s == NS) ? 0 : s) {
+        if (!mbar_wait(&full[s], use & 1, 2)) break;
         const int rows = min(SR, n_rows - i * SR);
         const uint8_t *st = ring + static_cast<size_t>(s) * p.slot_bytes;
         float acc0[R2][TT], acc1[R2][TT];
