@@ -426,7 +426,13 @@ int fr_gemm_swiglu_f32out(const void *A_packed, const void *SFA, const void *B_p
  *                      (nh / nkv); tcgen05 tensor cores (f16 operands, f32
  *                      accumulation, probabilities rounded to f16 for the PV
  *                      product); d == 128, nh == 8 nkv, ctx % 128 == 0; the
- *                      caches zero-initialised before first use
+ *                      caches zero-initialised before first use.  Each
+ *                      (sequence, KV head) walks its 128-key chunks over S
+ *                      CTAs, S = min(ctx / 128, 2 x SMs / (T x nkv)) (the
+ *                      FR_ATTN_SPLITS environment variable, read once, sets S
+ *                      for tuning); with S > 1 the last CTA merges the splits
+ *                      in split order, so results are deterministic for a
+ *                      given S
  *   fr_embed_nvfp4     x[t] = NVFP4 row of token prompt[t * prompt_ld + pos]
  *                      while pos < prompt_len, else of gen[t]
  *   fr_argmax_f32      tok[t] = argmax logits[t, :] (ties: lowest index)
