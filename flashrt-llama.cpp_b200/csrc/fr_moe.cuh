@@ -78,10 +78,105 @@ __device__ __forceinline__ void router_tile(const float *__restrict__ x, int64_t
 }
 
 // ------------------------------------------------------------ top-k
-// Softmax top-k of one token by one warp, the reference's algorithm
+// Softmax top-k of a token, the reference's algorithm
 // (src/fr_win_qwen36_sm120.cu:1826-1870): softmax in fp32, n_used rounds of
 // warp argmax (ties -> lower id), weights renormalised by max(sum, clamp).
+// The rounds are restated as ranks: expert e is picked in round r when r
+// probabilities beat it (higher, or equal with a lower id), so every thread
+// of the CTA counts the rank of one (token, expert) pair at once instead of
+// one warp running n_used dependent shuffle butterflies.  The float
+// operations that fix the weights' bits keep the reference's order: the
+// softmax as one warp per token, then each lane adds its own winners in
+// round order and the warp sums those partials with the same butterfly.
+
+// phase 1, one warp per token: probabilities into p[0, E) (NaN -> -FLT_MAX).
 // Logits are read through L2 (other CTAs wrote them).
+__device__ __forceinline__ void topk_softmax(const float *__restrict__ l, int E, float *__restrict__ p) {
+    const int lane = threadIdx.x & 31;
+    const int per = E / 32;
+    float wt[MOE_MAX_E / 32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+        wt[i] = (i < per) ? __ldcg(l + lane + 32 * i) : -INFINITY;
+        mx = fmaxf(mx, wt[i]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+        if (i < per) {
+            wt[i] = expf(wt[i] - mx);
+            sum += wt[i];
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+        if (i < per) {
+            float v = wt[i] * inv;
+            if (isnan(v)) v = -FLT_MAX;
+            p[lane + 32 * i] = v;
+        }
+    }
+}
+
+// phase 2, every thread of the block: rank[u][e] for the nu tokens whose
+// probabilities are p[u][0, E) (rows MOE_MAX_E apart, E a multiple of 32)
+__device__ __forceinline__ void topk_ranks(const float *__restrict__ p, int *__restrict__ rank, int nu, int E) {
+    for (int u = 0; u < nu; ++u) {
+        const float *pu = p + u * MOE_MAX_E;
+        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            const float v = pu[e];
+            int r = 0;
+            for (int j = 0; j < E; j += 4) {
+                const float4 q = *reinterpret_cast<const float4 *>(pu + j);
+                r += (q.x > v || (q.x == v && j < e)) ? 1 : 0;
+                r += (q.y > v || (q.y == v && j + 1 < e)) ? 1 : 0;
+                r += (q.z > v || (q.z == v && j + 2 < e)) ? 1 : 0;
+                r += (q.w > v || (q.w == v && j + 3 < e)) ? 1 : 0;
+            }
+            rank[u * MOE_MAX_E + e] = r;
+        }
+    }
+}
+
+// phase 3, one warp per token: ids_row[r] / w_row[r] for the n_used winners
+// (n_used <= 32).  Lane L's partial adds its experts L + 32 i that won, in
+// round order, as the rounds' `wsum += bv` on the winner's lane does.
+__device__ __forceinline__ void topk_finish(const float *__restrict__ p, const int *__restrict__ rank, int E,
+                                            int n_used, float clamp_val, int32_t *__restrict__ ids_row,
+                                            float *__restrict__ w_row) {
+    const int lane = threadIdx.x & 31;
+    const int per = E / 32;
+    int rk[MOE_MAX_E / 32];
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) rk[i] = (i < per) ? rank[lane + 32 * i] : E;
+    float wsum = 0.0f;
+    for (int r = 0; r < n_used; ++r) {
+#pragma unroll
+        for (int i = 0; i < MOE_MAX_E / 32; ++i)
+            if (rk[i] == r) wsum += p[lane + 32 * i];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, off);
+    wsum = fmaxf(wsum, clamp_val);
+    const float invs = 1.0f / wsum;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_E / 32; ++i) {
+        if (rk[i] < n_used) {
+            ids_row[rk[i]] = lane + 32 * i;
+            w_row[rk[i]] = p[lane + 32 * i] * invs;
+        }
+    }
+}
+
+// The rounds themselves, one warp per token: the form for chunks of 2..4
+// tokens, whose four warps run their rounds side by side (there the CTA-wide
+// rank counting measured slower: MoE layer at T=64 108.7 -> 117.7 us).
 __device__ __forceinline__ void topk_token(const float *__restrict__ l, int E, int n_used, float clamp_val,
                                            int32_t *__restrict__ ids_row, float *__restrict__ w_row) {
     const int lane = threadIdx.x & 31;
@@ -299,11 +394,25 @@ __global__ void __launch_bounds__(256) k_route(const RouteArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // this chunk's tokens: warp u routes token 4 tc + u
+    // this chunk's tokens: warp u routes token 4 tc + u (probabilities and
+    // ranks in the shared scratch the permute uses afterwards)
     const int t = tc * 4 + warp;
-    if (warp < 4 && t < a.T)
+    const int nu = min(4, a.T - tc * 4);
+    float *ps = reinterpret_cast<float *>(sm_route);                 // [4][MOE_MAX_E]
+    int *rk = sm_route + 4 * MOE_MAX_E;                              // [4][MOE_MAX_E]
+    if (nu == 1) {
+        // one token (T = 1): its ranks counted by the whole CTA
+        if (warp == 0) topk_softmax(a.logits + static_cast<int64_t>(t) * a.E, a.E, ps);
+        __syncthreads();
+        topk_ranks(ps, rk, 1, a.E);
+        __syncthreads();
+        if (warp == 0)
+            topk_finish(ps, rk, a.E, a.n_used, a.clamp_val, a.ids + static_cast<int64_t>(t) * a.n_used,
+                        a.wts + static_cast<int64_t>(t) * a.n_used);
+    } else if (warp < nu) {
         topk_token(a.logits + static_cast<int64_t>(t) * a.E, a.E, a.n_used, a.clamp_val,
                    a.ids + static_cast<int64_t>(t) * a.n_used, a.wts + static_cast<int64_t>(t) * a.n_used);
+    }
     __threadfence();
     __syncthreads();
     if (n_tc > 1) {
